@@ -1,0 +1,87 @@
+// engine.h: the device-resident model and session behind hc_model_* / hc_session_* / hc_step.
+#ifndef HWNPU_ENGINE_H
+#define HWNPU_ENGINE_H
+
+#include <map>
+#include <memory>
+#include <vector>
+
+#include "kernels.h"
+#include "repack.h"
+
+namespace hc {
+
+int device_ordinal(const hc_device *d);
+int device_sms(const hc_device *d);
+
+constexpr int kMaxChunk = 8;  // tokens one pass of the GEMVs reads the weights for
+
+// One repacked matrix in HBM.
+struct DevLinear {
+  DevMat m;
+  void *tiles = nullptr, *scales = nullptr, *bias = nullptr;
+  uint64_t bytes = 0;  // bytes a pass reads: tiles, row scales, biases
+  ~DevLinear();
+};
+
+char *upload(const Packed &p, DevLinear *out, cudaStream_t st);
+char *load_linear(const std::vector<RowRef> &rows, DevLinear *out, cudaStream_t st);
+
+struct LayerW {
+  std::unique_ptr<DevLinear> qkv, o, gu, down;
+  float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  float *sinks = nullptr;  // fp16-rounded sink logits, or nullptr
+  int window = 0;
+};
+
+// Norm settings of one RMS norm: the scale of qwen3's normScaled and its fp16 epsilon.
+struct NormCfg {
+  float scale = 1.f, eps16 = 0.f;
+};
+
+}  // namespace hc
+
+struct hc_model {
+  hc_device *dev = nullptr;
+  int ordinal = 0, sms = 148;
+  hc_model_desc d{};
+  std::vector<hc::LayerW> layers;
+  float *final_norm = nullptr;
+  std::unique_ptr<hc::DevLinear> head;
+  uint16_t *embed = nullptr;  // fp16 [vocab][hidden], or nullptr when tied
+  std::vector<double> inv_freq;
+  float rope_factor = 1.f;
+  hc::NormCfg norm_in0, norm_mid, norm_head;
+  float score_scale = 1.f;
+  uint64_t weight_bytes = 0;
+  std::vector<void *> allocs;  // small device arrays (norms, sinks, embedding)
+  ~hc_model();
+};
+
+struct hc_session {
+  hc_model *m = nullptr;
+  hc_session_opts o{};
+  cudaStream_t st = nullptr;
+  int cap = 0, splits = 1;
+  uint16_t *kc = nullptr, *vc = nullptr;  // [layers][slots][kv_heads][cap][hd] fp16
+  size_t layer_kv = 0;                    // elements of one layer's cache
+  uint32_t *rope = nullptr;               // [cap][hd/2] (cos, sin) fp16 pairs
+  std::vector<int> pos;                   // per slot
+  std::vector<bool> poisoned;             // per slot: a failed step may have half written it
+  // work buffers for one chunk of up to kMaxChunk tokens
+  float *x = nullptr, *qkv = nullptr, *q = nullptr, *h = nullptr;
+  uint8_t *act = nullptr;
+  float *part_ml = nullptr, *part_o = nullptr;
+  hc::StepTok *toks_dev = nullptr, *toks_host = nullptr;
+  uint16_t *logits_dev = nullptr;
+  unsigned long long *amax = nullptr;
+  int32_t *am_dev = nullptr, *am_host = nullptr, *res_dev = nullptr, *res_host = nullptr;
+  // captured step graphs by (tokens, accept kernel)
+  std::map<int, cudaGraphExec_t> graphs;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  hc_stats stats{};
+  uint64_t launches_per_chunk[hc::kMaxChunk + 1] = {};
+  ~hc_session();
+};
+
+#endif

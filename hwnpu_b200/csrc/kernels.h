@@ -1,0 +1,101 @@
+// kernels.h: launch wrappers of the sm_100a kernels (gemv.cu, attn.cu, misc.cu).
+#ifndef HWNPU_KERNELS_H
+#define HWNPU_KERNELS_H
+
+#include "common.h"
+
+namespace hc {
+
+// A repacked matrix on the device (repack.h's Packed after the copy).
+struct DevMat {
+  Kind kind = kKindInt8;
+  int fmt = HC_FMT_NONE;
+  int rows = 0, cols = 0, rtiles = 0, ktiles = 0, tile_bytes = 0;
+  const uint8_t *tiles = nullptr;
+  const float *row_scale = nullptr;  // kKindInt8
+  const float *bias = nullptr;       // or nullptr
+};
+
+// What the GEMV does with each output value v of token t and output row r.
+enum GemvMode : int {
+  kStore = 0,     // y[t][r] = v
+  kAdd = 1,       // y[t][r] += v (the residual stream)
+  kGlu = 2,       // tile rows 0-3 gate, 4-7 up: y[t][o] = silu(gate) * up, o = 4 * rtile + j
+  kLogits = 3,    // fp16 logits[t][r] and the greedy choice folded into amax[t]
+};
+
+struct GemvOut {
+  GemvMode mode = kStore;
+  float *y = nullptr;
+  int ldy = 0;
+  uint16_t *logits = nullptr;           // kLogits: [t][ldy] fp16 bits, or nullptr
+  unsigned long long *amax = nullptr;   // kLogits: [t], see argmax_key in misc.cu
+};
+
+// y = x W^T for ntok (1..8) tokens whose activations act_quant wrote into act.
+void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cudaStream_t st);
+
+// Quantises ntok rows of x (float32, stride ldx, n columns) into the GEMV's activation tiles
+// (ktiles of kActTile bytes a token), after an optional RMS norm: when norm_w is set,
+// x is normed as qwen3's normScaled with scale (1 or 64) and epsilon eps16 (the fp16 constant
+// f16(eps / scale^2)) and multiplied by norm_w (float32 values of fp16 weights).
+void act_quant(const float *x, int ldx, int n, int ntok, const float *norm_w, float scale,
+               float eps16, uint8_t *act, int ktiles, cudaStream_t st);
+
+// Attention partials -> merged o (float32 [ntok][heads*hd]) -> activation tiles of the output
+// projection (Flash-Decoding's merge with gpt-oss's sinks, paged.go:252-310).
+void attn_merge_quant(const float *part_ml, const float *part_o, const float *sinks, int ntok,
+                      int heads, int hd, int splits, uint8_t *act, int ktiles, float *o_out,
+                      cudaStream_t st);
+
+// Per-token position data of a step, in device memory so that a captured graph replays it.
+struct StepTok {
+  int32_t token;  // id
+  int32_t slot;   // sequence slot
+  int32_t pos;    // position of this token
+  int32_t pad_;
+};
+
+struct AttnGeom {
+  int heads, kv_heads, hd, cap, window;  // cap: positions a slot's cache holds
+  float score_scale;                     // the fp16 score scale 1/sqrt(hd), as float
+};
+
+// The rows of the fused q|k|v projection (float32 [ntok][(heads + 2 kv_heads) hd]) -> per-head
+// RMS norm of q and k (when qn/kn are set), RoPE with the fp16 tables rope[pos][hd/2] (cos, sin
+// pairs as fp16 bits), q into q_out (float32 [ntok][heads][hd]) and k, v as fp16 into the
+// cache at (slot, kv_head, pos).
+void qkv_post(const float *qkv, const StepTok *toks, int ntok, const AttnGeom &g,
+              const float *qn, const float *kn, float norm_scale, float eps16,
+              const uint32_t *rope, float *q_out, uint16_t *kcache, uint16_t *vcache,
+              cudaStream_t st);
+
+// Split-K decode attention over the fp16 cache: token t attends keys [lo, pos] of its slot
+// (lo = pos - window + 1 with a window); `splits` partials of (m, l) and unnormalised o.
+void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g,
+                const uint16_t *kcache, const uint16_t *vcache, int splits, float *part_ml,
+                float *part_o, cudaStream_t st);
+
+// Embedding rows of the step's tokens into x (float32 [ntok][hidden]): from an fp16 table, or
+// (table nullptr) from the tied head's tiles, dequantised and rounded to fp16. Also resets amax.
+void embed(const StepTok *toks, int ntok, const uint16_t *table, const DevMat *head, int hidden,
+           float *x, unsigned long long *amax, cudaStream_t st);
+
+// Reads the greedy choice out of amax keys.
+void amax_to_index(const unsigned long long *amax, int ntok, int32_t *out, cudaStream_t st);
+
+// Float32 values of rows [row0, row0+nrows) of a repacked matrix (the format's arithmetic).
+void dequant(const DevMat &W, int row0, int nrows, float *out, cudaStream_t st);
+
+// Argmax over fp16 rows (first largest wins); MoE softmax top-k routing.
+void argmax_rows(const uint16_t *logits, int rows, int vocab, int32_t *out, cudaStream_t st);
+void route(const float *logits, int rows, int n, int k, int32_t *idx, float *w, cudaStream_t st);
+
+// Greedy speculative accept on the device: given the argmax of each of n rows and the n tokens
+// read, writes kept (1..n) and next into res[0], res[1].
+void spec_accept(const int32_t *amax_idx, const StepTok *toks, int n, int32_t *res,
+                 cudaStream_t st);
+
+}  // namespace hc
+
+#endif

@@ -1,0 +1,402 @@
+// step.cpp: sessions and the decode step (decode.Session.Step/Speculate, internal/llm/decode/
+// decode.go:1221-1260; chat.tokenSession, internal/chat/session.go:26-32), one CUDA graph per
+// chunk size replayed with the step's tokens and positions read from device memory.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <thread>
+
+#include "engine.h"
+
+using hc::kMaxChunk;
+
+hc_session::~hc_session() {
+  if (!m) return;
+  cudaSetDevice(m->ordinal);
+  if (st) cudaStreamSynchronize(st);
+  for (auto &g : graphs) cudaGraphExecDestroy(g.second);
+  for (void *p : {(void *)kc, (void *)vc, (void *)rope, (void *)x, (void *)qkv, (void *)q, (void *)h,
+                  (void *)act, (void *)part_ml, (void *)part_o, (void *)toks_dev, (void *)logits_dev,
+                  (void *)amax, (void *)am_dev, (void *)res_dev})
+    if (p) cudaFree(p);
+  if (toks_host) cudaFreeHost(toks_host);
+  if (am_host) cudaFreeHost(am_host);
+  if (res_host) cudaFreeHost(res_host);
+  if (ev0) cudaEventDestroy(ev0);
+  if (ev1) cudaEventDestroy(ev1);
+  if (st) cudaStreamDestroy(st);
+}
+
+namespace {
+
+constexpr int kMaxSplits = 64;
+
+int splits_for(const hc_session *s, int n) {
+  const int kv = int(s->m->d.kv_heads);
+  int sp = (2 * s->m->sms) / (kv * n);
+  return std::max(1, std::min(kMaxSplits, sp));
+}
+
+template <typename T>
+char *alloc(T **p, size_t count, const char *what) {
+  void *v = nullptr;
+  if (char *e = hc::dev_alloc(&v, count * sizeof(T), what)) return e;
+  *p = static_cast<T *>(v);
+  return nullptr;
+}
+
+hc::AttnGeom geom(const hc_session *s, int window) {
+  const auto &d = s->m->d;
+  return hc::AttnGeom{int(d.heads), int(d.kv_heads), int(d.head_dim), s->cap, window, s->m->score_scale};
+}
+
+// Enqueues one chunk of n tokens (already in toks_dev) on the session's stream; returns the
+// number of kernels launched.
+int enqueue_chunk(hc_session *s, int n, bool accept) {
+  hc_model *m = s->m;
+  const auto &d = m->d;
+  const int D = int(d.hidden), F = int(d.inter), H = int(d.heads), KV = int(d.kv_heads);
+  const int hd = int(d.head_dim), V = int(d.vocab);
+  const int W = (H + 2 * KV) * hd;
+  const int splits = splits_for(s, n);
+  cudaStream_t st = s->st;
+  int k = 0;
+  hc::embed(s->toks_dev, n, m->embed, m->embed ? nullptr : &m->head->m, D, s->x, s->amax, st);
+  ++k;
+  for (size_t li = 0; li < m->layers.size(); ++li) {
+    const hc::LayerW &w = m->layers[li];
+    const hc::NormCfg nc = li == 0 ? m->norm_in0 : m->norm_mid;
+    uint16_t *kcl = s->kc + li * s->layer_kv, *vcl = s->vc + li * s->layer_kv;
+    const hc::AttnGeom g = geom(s, w.window);
+    hc::act_quant(s->x, D, D, n, w.in_norm, nc.scale, nc.eps16, s->act, w.qkv->m.ktiles, st);
+    hc::GemvOut o1;
+    o1.mode = hc::kStore; o1.y = s->qkv; o1.ldy = W;
+    hc::gemv(w.qkv->m, s->act, n, o1, st);
+    hc::qkv_post(s->qkv, s->toks_dev, n, g, w.q_norm, w.k_norm, m->norm_mid.scale, m->norm_mid.eps16,
+                 s->rope, s->q, kcl, vcl, st);
+    hc::attn_split(s->q, s->toks_dev, n, g, kcl, vcl, splits, s->part_ml, s->part_o, st);
+    hc::attn_merge_quant(s->part_ml, s->part_o, w.sinks, n, H, hd, splits, s->act, w.o->m.ktiles, nullptr, st);
+    hc::GemvOut o2;
+    o2.mode = hc::kAdd; o2.y = s->x; o2.ldy = D;
+    hc::gemv(w.o->m, s->act, n, o2, st);
+    hc::act_quant(s->x, D, D, n, w.post_norm, m->norm_mid.scale, m->norm_mid.eps16, s->act, w.gu->m.ktiles, st);
+    hc::GemvOut o3;
+    o3.mode = hc::kGlu; o3.y = s->h; o3.ldy = F;
+    hc::gemv(w.gu->m, s->act, n, o3, st);
+    hc::act_quant(s->h, F, F, n, nullptr, 1.f, 0.f, s->act, w.down->m.ktiles, st);
+    hc::gemv(w.down->m, s->act, n, o2, st);
+    k += 10;
+  }
+  hc::act_quant(s->x, D, D, n, m->final_norm, m->norm_head.scale, m->norm_head.eps16, s->act, m->head->m.ktiles, st);
+  hc::GemvOut oh;
+  oh.mode = hc::kLogits; oh.ldy = V; oh.logits = s->logits_dev; oh.amax = s->amax;
+  hc::gemv(m->head->m, s->act, n, oh, st);
+  hc::amax_to_index(s->amax, n, s->am_dev, st);
+  k += 3;
+  if (accept) { hc::spec_accept(s->am_dev, s->toks_dev, n, s->res_dev, st); ++k; }
+  return k;
+}
+
+// The whole chunk: tokens in, greedy choices (and the accept result) out, as one graph.
+char *run_chunk(hc_session *s, int n, bool accept) {
+  cudaStream_t st = s->st;
+  const bool use_graph = !(s->o.flags & HC_SESSION_NO_GRAPH);
+  const int key = n * 2 + (accept ? 1 : 0);
+  auto enqueue_all = [&]() -> int {
+    cudaMemcpyAsync(s->toks_dev, s->toks_host, sizeof(hc::StepTok) * n, cudaMemcpyHostToDevice, st);
+    int k = enqueue_chunk(s, n, accept);
+    cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
+    if (accept) cudaMemcpyAsync(s->res_host, s->res_dev, sizeof(int32_t) * 2, cudaMemcpyDeviceToHost, st);
+    return k;
+  };
+  if (use_graph && !s->graphs.count(key)) {
+    cudaGraph_t graph = nullptr;
+    HC_TRY_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    s->launches_per_chunk[n] = uint64_t(enqueue_all());
+    cudaError_t e = cudaStreamEndCapture(st, &graph);
+    if (e != cudaSuccess) return hc::make_error(std::string("graph capture: ") + cudaGetErrorString(e));
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return hc::make_error(std::string("graph instantiate: ") + cudaGetErrorString(e));
+    s->graphs[key] = exec;
+  }
+  HC_TRY_CUDA(cudaEventRecord(s->ev0, st));
+  if (use_graph) {
+    HC_TRY_CUDA(cudaGraphLaunch(s->graphs[key], st));
+  } else {
+    s->launches_per_chunk[n] = uint64_t(enqueue_all());
+  }
+  HC_TRY_CUDA(cudaGetLastError());
+  HC_TRY_CUDA(cudaEventRecord(s->ev1, st));
+  s->stats.launches += s->launches_per_chunk[n];
+  return nullptr;
+}
+
+// Waits for the last chunk with a deadline (xrtshim.h's xs_run_wait with timeout_ms).
+char *wait_done(hc_session *s, uint32_t timeout_ms, int32_t *state) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaEventQuery(s->ev1);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) {
+      if (state) *state = HC_STATE_ERROR;
+      return hc::make_error(std::string("step: ") + cudaGetErrorString(e));
+    }
+    if (timeout_ms) {
+      auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+      if (ms >= long(timeout_ms)) {
+        if (state) *state = HC_STATE_TIMEOUT;
+        return nullptr;
+      }
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+  float ms = 0;
+  cudaEventElapsedTime(&ms, s->ev0, s->ev1);
+  s->stats.last_step_us = double(ms) * 1000.0;
+  if (state) *state = HC_STATE_COMPLETED;
+  return nullptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session **out) {
+  if (!m || !opts || !out) return hc::make_error("hc_session_new: NULL argument");
+  *out = nullptr;
+  const hc_session_opts &o = *opts;
+  if (!o.max_context || !o.max_seqs || !o.max_step) return hc::make_error("hc_session_new: zero size");
+  if (o.kv_format != HC_KV_F16) return hc::make_error("hc_session_new: KV format " + std::to_string(o.kv_format) + " is not supported by this build");
+  HC_TRY_CUDA(cudaSetDevice(m->ordinal));
+  auto s = std::make_unique<hc_session>();
+  s->m = m;
+  s->o = o;
+  s->cap = int(o.max_context);
+  const auto &d = m->d;
+  const int D = int(d.hidden), F = int(d.inter), H = int(d.heads), KV = int(d.kv_heads), hd = int(d.head_dim);
+  s->layer_kv = size_t(o.max_seqs) * KV * s->cap * hd;
+  const size_t kv_elems = s->layer_kv * d.layers;
+  if (char *e = alloc(&s->kc, kv_elems, "key cache")) return e;
+  if (char *e = alloc(&s->vc, kv_elems, "value cache")) return e;
+  HC_TRY_CUDA(cudaMemset(s->kc, 0, kv_elems * 2));
+  HC_TRY_CUDA(cudaMemset(s->vc, 0, kv_elems * 2));
+  // blocks.RopeValues (blocks.go:412-427) as fp16 inputs (qwen3 StepInputs, arch.go:117-137)
+  std::vector<uint32_t> rope(size_t(s->cap) * (hd / 2));
+  for (int p = 0; p < s->cap; ++p)
+    for (int j = 0; j < hd / 2; ++j) {
+      const double a = double(p) * m->inv_freq[j];
+      float c = float(std::cos(a)), sn = float(std::sin(a));
+      if (m->rope_factor != 1.f) { c *= m->rope_factor; sn *= m->rope_factor; }
+      rope[size_t(p) * (hd / 2) + j] = uint32_t(hc::f16_bits(c)) | (uint32_t(hc::f16_bits(sn)) << 16);
+    }
+  if (char *e = alloc(&s->rope, rope.size(), "rope tables")) return e;
+  if (char *e = hc::copy_h2d(s->rope, rope.data(), rope.size() * 4, nullptr)) return e;
+  HC_TRY_CUDA(cudaStreamSynchronize(nullptr));
+  int ktiles = 0;
+  for (auto &w : m->layers)
+    ktiles = std::max({ktiles, w.qkv->m.ktiles, w.o->m.ktiles, w.gu->m.ktiles, w.down->m.ktiles});
+  ktiles = std::max(ktiles, m->head->m.ktiles);
+  const int T = kMaxChunk;
+  if (char *e = alloc(&s->x, size_t(T) * D, "hidden states")) return e;
+  if (char *e = alloc(&s->qkv, size_t(T) * (H + 2 * KV) * hd, "qkv")) return e;
+  if (char *e = alloc(&s->q, size_t(T) * H * hd, "queries")) return e;
+  if (char *e = alloc(&s->h, size_t(T) * F, "mlp activations")) return e;
+  if (char *e = alloc(&s->act, size_t(T) * ktiles * hc::kActTile, "activation tiles")) return e;
+  if (char *e = alloc(&s->part_ml, size_t(T) * H * kMaxSplits * 2, "attention partials")) return e;
+  if (char *e = alloc(&s->part_o, size_t(T) * H * kMaxSplits * hd, "attention partials")) return e;
+  if (char *e = alloc(&s->toks_dev, T, "step tokens")) return e;
+  if (char *e = alloc(&s->logits_dev, size_t(T) * d.vocab, "logits")) return e;
+  if (char *e = alloc(&s->amax, size_t(T) * hc::kAmaxSlots, "argmax keys")) return e;
+  if (char *e = alloc(&s->am_dev, T, "argmax")) return e;
+  if (char *e = alloc(&s->res_dev, 2, "accept result")) return e;
+  HC_TRY_CUDA(cudaHostAlloc(&s->toks_host, sizeof(hc::StepTok) * T, cudaHostAllocDefault));
+  HC_TRY_CUDA(cudaHostAlloc(&s->am_host, sizeof(int32_t) * T, cudaHostAllocDefault));
+  HC_TRY_CUDA(cudaHostAlloc(&s->res_host, sizeof(int32_t) * 2, cudaHostAllocDefault));
+  HC_TRY_CUDA(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+  HC_TRY_CUDA(cudaEventCreate(&s->ev0));
+  HC_TRY_CUDA(cudaEventCreate(&s->ev1));
+  s->pos.assign(o.max_seqs, 0);
+  s->poisoned.assign(o.max_seqs, false);
+  *out = s.release();
+  return nullptr;
+}
+
+HC_API void hc_session_free(hc_session *s) { delete s; }
+
+HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tokens,
+                     const int32_t *tokens, int32_t nseq, int32_t flags, uint16_t *logits,
+                     int32_t *argmax, uint32_t timeout_ms, int32_t *state) {
+  if (state) *state = HC_STATE_ERROR;
+  if (!s || !seq_ids || !n_tokens || !tokens || nseq < 1) return hc::make_error("hc_step: bad argument");
+  const int V = int(s->m->d.vocab);
+  std::vector<hc::StepTok> all;
+  std::vector<int> want;  // indices into `all` whose rows go out
+  for (int i = 0; i < nseq; ++i) {
+    const int sq = seq_ids[i], n = n_tokens[i];
+    if (sq < 0 || sq >= int(s->o.max_seqs)) return hc::make_error("hc_step: sequence " + std::to_string(sq) + " out of range");
+    if (n < 1 || n > int(s->o.max_step)) return hc::make_error("hc_step: " + std::to_string(n) + " tokens for one sequence (max_step " + std::to_string(s->o.max_step) + ")");
+    if (s->poisoned[sq]) return hc::make_error("hc_step: sequence " + std::to_string(sq) + " failed earlier; reset it");
+    for (int j = 0; j < i; ++j)
+      if (seq_ids[j] == sq) return hc::make_error("hc_step: sequence listed twice");
+    if (s->pos[sq] + n > s->cap) return hc::make_error("hc_step: sequence " + std::to_string(sq) + " would exceed max_context");
+  }
+  int off = 0;
+  for (int i = 0; i < nseq; ++i) {
+    for (int j = 0; j < n_tokens[i]; ++j) {
+      const int tok = tokens[off + j];
+      if (tok < 0 || tok >= V) return hc::make_error("hc_step: token " + std::to_string(tok) + " out of the vocabulary");
+      all.push_back(hc::StepTok{tok, seq_ids[i], s->pos[seq_ids[i]] + j, 0});
+      if ((flags & HC_STEP_ALL_ROWS) || j == n_tokens[i] - 1) want.push_back(int(all.size()) - 1);
+    }
+    off += n_tokens[i];
+  }
+  if (hc::fault_fires(hc::kFaultStep)) return hc::make_error("injected fault: step");
+  HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
+  size_t wi = 0;
+  int row = 0;
+  for (size_t c0 = 0; c0 < all.size(); c0 += kMaxChunk) {
+    const int n = int(std::min<size_t>(kMaxChunk, all.size() - c0));
+    std::memcpy(s->toks_host, &all[c0], sizeof(hc::StepTok) * n);
+    if (char *e = run_chunk(s, n, false)) {
+      for (int i = 0; i < nseq; ++i) s->poisoned[seq_ids[i]] = true;
+      return e;
+    }
+    int32_t st_ = HC_STATE_ERROR;
+    char *e = wait_done(s, timeout_ms, &st_);
+    if (e || st_ != HC_STATE_COMPLETED) {
+      for (int i = 0; i < nseq; ++i) s->poisoned[seq_ids[i]] = true;
+      if (state) *state = st_;
+      return e;
+    }
+    for (; wi < want.size() && size_t(want[wi]) < c0 + n; ++wi, ++row) {
+      const int local = int(want[wi] - c0);
+      if (argmax) argmax[row] = s->am_host[local];
+      if (logits) HC_TRY_CUDA(cudaMemcpy(logits + size_t(row) * V, s->logits_dev + size_t(local) * V, size_t(V) * 2, cudaMemcpyDeviceToHost));
+    }
+  }
+  uint64_t kv = 0;
+  const auto &md = s->m->d;
+  for (auto &t : all) kv += uint64_t(t.pos + 1) * md.kv_heads * md.head_dim * 4 * md.layers;
+  s->stats.kv_bytes = kv;
+  for (int i = 0; i < nseq; ++i) s->pos[seq_ids[i]] += n_tokens[i];
+  s->stats.steps++;
+  s->stats.tokens += all.size();
+  s->stats.weight_bytes = s->m->weight_bytes;
+  if (state) *state = HC_STATE_COMPLETED;
+  return nullptr;
+}
+
+HC_API char *hc_speculate(hc_session *s, int32_t seq, const int32_t *toks, int32_t n,
+                          int32_t *kept, int32_t *next, uint16_t *logits, uint32_t timeout_ms,
+                          int32_t *state) {
+  if (state) *state = HC_STATE_ERROR;
+  if (!s || !toks || !kept || !next) return hc::make_error("hc_speculate: NULL argument");
+  if (seq < 0 || seq >= int(s->o.max_seqs)) return hc::make_error("hc_speculate: sequence out of range");
+  if (n < 1 || n > kMaxChunk || n > int(s->o.max_step)) return hc::make_error("hc_speculate: " + std::to_string(n) + " tokens");
+  if (s->poisoned[seq]) return hc::make_error("hc_speculate: sequence failed earlier; reset it");
+  if (s->pos[seq] + n > s->cap) return hc::make_error("hc_speculate: would exceed max_context");
+  const int V = int(s->m->d.vocab);
+  for (int j = 0; j < n; ++j) {
+    if (toks[j] < 0 || toks[j] >= V) return hc::make_error("hc_speculate: token out of the vocabulary");
+    s->toks_host[j] = hc::StepTok{toks[j], seq, s->pos[seq] + j, 0};
+  }
+  if (hc::fault_fires(hc::kFaultStep)) return hc::make_error("injected fault: step");
+  HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
+  if (char *e = run_chunk(s, n, true)) { s->poisoned[seq] = true; return e; }
+  int32_t st_ = HC_STATE_ERROR;
+  char *e = wait_done(s, timeout_ms, &st_);
+  if (e || st_ != HC_STATE_COMPLETED) {
+    s->poisoned[seq] = true;
+    if (state) *state = st_;
+    return e;
+  }
+  *kept = s->res_host[0];
+  *next = s->res_host[1];
+  if (logits) HC_TRY_CUDA(cudaMemcpy(logits, s->logits_dev + size_t(*kept - 1) * V, size_t(V) * 2, cudaMemcpyDeviceToHost));
+  // decode.Session.keep (decode.go:1685-1705): only the kept rows stay; the others are past pos
+  s->pos[seq] += *kept;
+  s->stats.steps++;
+  s->stats.tokens += n;
+  s->stats.weight_bytes = s->m->weight_bytes;
+  if (state) *state = HC_STATE_COMPLETED;
+  return nullptr;
+}
+
+HC_API char *hc_seq_reset(hc_session *s, int32_t seq) {
+  if (!s || seq < 0 || seq >= int(s->o.max_seqs)) return hc::make_error("hc_seq_reset: bad sequence");
+  s->pos[seq] = 0;
+  s->poisoned[seq] = false;
+  return nullptr;
+}
+
+HC_API char *hc_seq_truncate(hc_session *s, int32_t seq, int32_t len) {
+  if (!s || seq < 0 || seq >= int(s->o.max_seqs)) return hc::make_error("hc_seq_truncate: bad sequence");
+  if (len < 0 || len > s->pos[seq]) return hc::make_error("hc_seq_truncate: length out of range");
+  s->pos[seq] = len;
+  return nullptr;
+}
+
+HC_API char *hc_seq_pos(hc_session *s, int32_t seq, int32_t *pos) {
+  if (!s || !pos || seq < 0 || seq >= int(s->o.max_seqs)) return hc::make_error("hc_seq_pos: bad argument");
+  *pos = s->pos[seq];
+  return nullptr;
+}
+
+namespace {
+char *rows_copy(hc_session *s, int32_t seq, int32_t start, int32_t n, void *host, bool out) {
+  const auto &d = s->m->d;
+  const size_t hd = d.head_dim, row = hd * 2;
+  char *p = static_cast<char *>(host);
+  for (uint32_t li = 0; li < d.layers; ++li)
+    for (int kvs = 0; kvs < 2; ++kvs)
+      for (uint32_t h = 0; h < d.kv_heads; ++h) {
+        uint16_t *base = (kvs ? s->vc : s->kc) + li * s->layer_kv + ((size_t(seq) * d.kv_heads + h) * s->cap + start) * hd;
+        const size_t nb = size_t(n) * row;
+        cudaError_t e = out ? cudaMemcpy(p, base, nb, cudaMemcpyDeviceToHost) : cudaMemcpy(base, p, nb, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return hc::make_error(std::string("rows copy: ") + cudaGetErrorString(e));
+        p += nb;
+      }
+  return nullptr;
+}
+}  // namespace
+
+HC_API char *hc_seq_export_rows(hc_session *s, int32_t seq, int32_t start, int32_t n, void *dst,
+                                uint64_t cap, uint64_t *need) {
+  if (!s || seq < 0 || seq >= int(s->o.max_seqs)) return hc::make_error("hc_seq_export_rows: bad sequence");
+  if (start < 0 || n < 0 || start + n > s->pos[seq]) return hc::make_error("hc_seq_export_rows: rows out of range");
+  const auto &d = s->m->d;
+  const uint64_t bytes = uint64_t(d.layers) * 2 * d.kv_heads * n * d.head_dim * 2;
+  if (need) *need = bytes;
+  if (!dst) return nullptr;
+  if (cap < bytes) return hc::make_error("hc_seq_export_rows: buffer too small");
+  HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
+  HC_TRY_CUDA(cudaStreamSynchronize(s->st));
+  return rows_copy(s, seq, start, n, dst, true);
+}
+
+HC_API char *hc_seq_import_rows(hc_session *s, int32_t seq, int32_t start, int32_t n,
+                                const void *src, uint64_t size) {
+  if (!s || !src || seq < 0 || seq >= int(s->o.max_seqs)) return hc::make_error("hc_seq_import_rows: bad argument");
+  if (start < 0 || n < 0 || start > s->pos[seq] || start + n > s->cap) return hc::make_error("hc_seq_import_rows: rows out of range");
+  const auto &d = s->m->d;
+  const uint64_t bytes = uint64_t(d.layers) * 2 * d.kv_heads * n * d.head_dim * 2;
+  if (size != bytes) return hc::make_error("hc_seq_import_rows: size does not match the rows");
+  HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
+  HC_TRY_CUDA(cudaStreamSynchronize(s->st));
+  if (char *e = rows_copy(s, seq, start, n, const_cast<void *>(src), false)) return e;
+  s->pos[seq] = start + n;
+  s->poisoned[seq] = false;
+  return nullptr;
+}
+
+HC_API char *hc_stats_get(hc_session *s, hc_stats *out) {
+  if (!s || !out) return hc::make_error("hc_stats_get: NULL argument");
+  *out = s->stats;
+  return nullptr;
+}
+
+}  // extern "C"

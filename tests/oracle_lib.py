@@ -1,0 +1,103 @@
+"""ctypes binding of oracle/liboracle.so, the CPU restatement of the reference path.
+
+Test infrastructure: only tests/, __graft_entry__.smoke() and bench.py's CPU baseline use it.
+"""
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from hwnpu_b200 import _abi as A
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PATH = os.path.join(ROOT, "oracle", "liboracle.so")
+_o = None
+
+_f32p, _u8p, _u16p, _i32p, _i8p = (C.POINTER(C.c_float), C.POINTER(C.c_uint8), C.POINTER(C.c_uint16),
+                                   C.POINTER(C.c_int32), C.POINTER(C.c_int8))
+SIG = {
+    "or_f16_bits": (C.c_uint16, [C.c_float]),
+    "or_f16_value": (C.c_float, [C.c_uint16]),
+    "or_exp": (C.c_float, [C.c_float]),
+    "or_synth_uniform": (None, [C.c_char_p, _f32p, C.c_uint64]),
+    "or_quantize_linear": (None, [_f32p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int32, C.c_int32, _u8p, _u16p]),
+    "or_dequant_linear": (None, [_u8p, _u16p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int32, _f32p]),
+    "or_dequant_int4_asym": (None, [_u8p, _u16p, _u16p, C.c_uint32, C.c_uint32, _f32p]),
+    "or_quantize_int4_asym": (None, [_f32p, C.c_uint32, C.c_uint32, _u8p, _u16p, _u16p]),
+    "or_mxfp4_nearest": (C.c_uint8, [C.c_double]),
+    "or_mxfp4_encode": (None, [_f32p, C.c_uint32, _u8p, _u8p]),
+    "or_mxfp4_dequant": (None, [_u8p, _u8p, C.c_uint32, _f32p]),
+    "or_mxfp4_quantize": (None, [_f32p, C.c_uint32, _i8p, _f32p]),
+    "or_mxfp4_dot": (C.c_float, [_u8p, _u8p, C.c_uint32, _i8p, _f32p]),
+    "or_route": (None, [_f32p, C.c_int32, C.c_int32, C.c_int32, _i32p, _f32p]),
+    "or_merge_new": (C.c_void_p, [C.c_int32, C.c_int32]),
+    "or_merge_free": (None, [C.c_void_p]),
+    "or_merge_add": (None, [C.c_void_p, _f32p, _f32p, _f32p]),
+    "or_merge_add_sink": (None, [C.c_void_p, _f32p, C.c_int32]),
+    "or_merge_result": (None, [C.c_void_p, _f32p]),
+    "or_gemm_nt": (None, [C.c_int32, C.c_int32, C.c_int32, _f32p, _f32p, _f32p, C.c_int32]),
+    "or_argmax": (C.c_int32, [_f32p, C.c_int32]),
+    "or_argmax_f16": (C.c_int32, [_u16p, C.c_int32]),
+    "or_model_new": (C.c_void_p, [C.POINTER(A.ModelDesc), C.c_int32]),
+    "or_model_free": (None, [C.c_void_p]),
+    "or_session_new": (C.c_void_p, [C.c_void_p, C.c_int32]),
+    "or_session_free": (None, [C.c_void_p]),
+    "or_session_pos": (C.c_int32, [C.c_void_p]),
+    "or_step": (C.c_int32, [C.c_void_p, _i32p, C.c_int32, C.c_int32, _u16p]),
+    "or_speculate": (C.c_int32, [C.c_void_p, _i32p, C.c_int32, _i32p, _u16p]),
+    "or_truncate": (None, [C.c_void_p, C.c_int32]),
+}
+
+
+def lib():
+    global _o
+    if _o is None:
+        L = C.CDLL(PATH)
+        for k, (r, a) in SIG.items():
+            f = getattr(L, k)
+            f.restype, f.argtypes = r, a
+        _o = L
+    return _o
+
+
+def p(a, t):
+    return a.ctypes.data_as(t)
+
+
+class OracleSession:
+    """decode.Session on the CPU interpreter for a synth.Model."""
+
+    def __init__(self, model, max_context, threads=0):
+        self.model = model
+        self.vocab = model.cfg.vocab
+        self.m = lib().or_model_new(C.byref(model.desc()), threads or os.cpu_count())
+        assert self.m, "oracle: model not supported"
+        self.s = lib().or_session_new(self.m, max_context)
+
+    def step(self, toks, all_rows=False):
+        toks = np.ascontiguousarray(toks, np.int32)
+        rows = len(toks) if all_rows else 1
+        out = np.empty((rows, self.vocab), np.uint16)
+        rc = lib().or_step(self.s, p(toks, _i32p), len(toks), int(all_rows), p(out, _u16p))
+        assert rc == 0, "oracle step failed"
+        return out
+
+    def speculate(self, toks):
+        toks = np.ascontiguousarray(toks, np.int32)
+        nxt = np.zeros(1, np.int32)
+        out = np.empty(self.vocab, np.uint16)
+        kept = lib().or_speculate(self.s, p(toks, _i32p), len(toks), p(nxt, _i32p), p(out, _u16p))
+        return kept, int(nxt[0]), out
+
+    def pos(self):
+        return lib().or_session_pos(self.s)
+
+    def truncate(self, n):
+        lib().or_truncate(self.s, n)
+
+    def close(self):
+        if self.s:
+            lib().or_session_free(self.s)
+            lib().or_model_free(self.m)
+            self.s = self.m = None
