@@ -1,0 +1,298 @@
+#!/usr/bin/env python
+"""Decode benchmark of the B200 engine on BASELINE configs[1] (C2): a 28-layer 1.7B Qwen3
+decoder with int4 asymmetric group-32 weights, batch 1, a 1024-id random prompt, greedy steps.
+
+A step is one decoded token. The timed region runs K tokens as passes of 256 greedy steps from
+the same 1024-token prompt (the KV cache is truncated back to the prompt after each pass, so the
+context stays in 1024..1280, the configuration's). value: tokens/s of the device-resident loop
+(hc_generate: tokens fed back on the device), timed with CUDA events on the session's stream.
+e2e: the same through the per-token public call hc_step (token H2D, greedy choice D2H each step).
+
+Under torchrun (N > 1) every rank runs its own replica (sequences are independent; weights are
+replicated; no collective on the path): value = all ranks' tokens / the slowest rank's time.
+
+--impl reference times the reference path's CPU restatement (oracle/, the Go path cannot run
+here) on the host's cores for the same metric, rank 0 only.
+"""
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT = 1024
+PASS = 256
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (clock and throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu, self.p, self.path = gpu, None, None
+
+    def start(self):
+        try:
+            os.makedirs(os.path.join(ROOT, "gpurun_out"), exist_ok=True)
+            self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{self.gpu}_{os.getpid()}.csv")
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-i", str(self.gpu), "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_model(workload):
+    import hwnpu_b200 as hb
+
+    cfg = {"c2": hb.C2, "c1": hb.C1}[workload]
+    return hb.Model(cfg, seed=0)
+
+
+def cpu_generate(model, prompt_len, steps, threads):
+    """The oracle (the reference path restated on the CPU): tokens/s of greedy decode steps after
+    a prefilled prompt; returns (tokens/s, seconds)."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import numpy as np
+    import oracle_lib as O
+    from hwnpu_b200 import synth
+
+    s = O.OracleSession(model, prompt_len + steps + 1, threads=threads)
+    toks = synth.tokens(1, model.cfg.vocab, prompt_len)
+    logits = s.step(toks)[0]
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        t = O.lib().or_argmax_f16(O.p(logits, O._u16p), model.cfg.vocab)
+        logits = s.step([t])[0]
+    dt = time.perf_counter() - t0
+    s.close()
+    return steps / dt, dt
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    model = build_model(args.workload)
+    threads = os.cpu_count()
+    steps = max(1, min(args.steps, 16))
+    tps, dt = cpu_generate(model, 64, steps, threads)
+    sample = (f"{steps} greedy decode tokens of the {args.workload.upper()} model after a 64-id prompt "
+              f"(per-token cost is the fp32 weight stream: the KV of 1024-1280 positions is ~2% of it)")
+    line = {"impl": "reference", "metric": "decode tokens/s", "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": 0, "higher_is_better": True, "data": "synthetic",
+            "config": workload_config(args),
+            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args):
+    return {"workload": f"{args.workload.upper()} bs1 greedy decode: 1024-id random prompt, passes of 256 steps "
+                        f"(context 1024-1280)",
+            "model": "C2 28L d2048 16q/8kv hd128 FFN6144 V151936 tied, int4 asym g32" if args.workload == "c2"
+            else "C1 4L d1024 16q/4kv hd64 FFN2816 V32000, int8 rows",
+            "global_batch": args.gpus, "seq_len": PROMPT + PASS, "prompt": PROMPT, "steps_per_pass": PASS,
+            "parallelism": f"replicas x{args.gpus}", "l2": "inputs larger than L2 (the weights, ~1.1 GB, stream every token)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2560)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c2", "c1"], default="c2")
+    ap.add_argument("--e2e-steps", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import numpy as np
+    import torch
+
+    import hwnpu_b200 as hb
+    from hwnpu_b200 import synth
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    W = max(3, args.warmup)
+    K = args.steps
+    model = build_model(args.workload)
+    dev = hb.Device(local)
+    lm = dev.load_model(model)
+    sess = lm.session(max_context=PROMPT + PASS + W + 8, max_step=8)
+    prompt = synth.tokens(1, model.cfg.vocab, PROMPT)
+    first = sess.greedy(prompt)
+    base = sess.pos()
+    sess.generate(first, W)
+    sess.truncate(base)
+    stream = torch.cuda.ExternalStream(sess.stream())
+    launches0 = sess.stats()["launches"]
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    clocks = Clocks(local)
+    barrier()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    done = 0
+    while done < K:
+        n = min(PASS, K - done)
+        sess.generate(first, n)
+        sess.truncate(base)
+        done += n
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    launches = sess.stats()["launches"] - launches0
+    clk = clocks.stop()
+    barrier()
+
+    # e2e: the public per-token call, token in from pinned host memory, choice out, every step
+    E = min(args.e2e_steps, PASS)
+    tok = first
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(E):
+        tok = sess.greedy([tok])
+    f1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = f0.elapsed_time(f1)
+    sess.truncate(base)
+    barrier()
+
+    # the dominant kernel: the GEMV over the head (151936 x 2048 int4 g32, the largest launch),
+    # timed alone with CUDA events on torch's stream (act quantisation + GEMV of one token)
+    import ctypes as C
+
+    from hwnpu_b200 import _abi as A
+
+    h = C.c_void_p()
+    A.check(A.lib().hc_linear_load(dev.h, C.byref(model.head.desc()), C.byref(h)))
+    x = torch.randn(1, model.cfg.hidden, device="cuda")
+    y = torch.empty(1, model.cfg.vocab, device="cuda")
+    cs = torch.cuda.current_stream()
+    for _ in range(5):
+        A.check(A.lib().hc_linear_run(h, C.c_void_p(x.data_ptr()), 1, C.c_void_p(y.data_ptr()), C.c_void_p(cs.cuda_stream)))
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 50
+    g0.record(cs)
+    for _ in range(reps):
+        A.check(A.lib().hc_linear_run(h, C.c_void_p(x.data_ptr()), 1, C.c_void_p(y.data_ptr()), C.c_void_p(cs.cuda_stream)))
+    g1.record(cs)
+    torch.cuda.synchronize()
+    gemv_ms = g0.elapsed_time(g1) / reps
+    A.lib().hc_linear_free(h)
+    head_bytes = model.head.data.nbytes + model.head.scales.nbytes + (model.head.zeros.nbytes if model.head.zeros is not None else 0)
+
+    t_max = ms
+    if dist:
+        tt = torch.tensor([ms, ms_e2e], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_max, ms_e2e = float(tt[0]), float(tt[1])
+    cfg = model.cfg
+    kv_per_pos = cfg.layers * cfg.kv_heads * cfg.head_dim * 2 * 2
+    mean_ctx = PROMPT + (PASS + 1) / 2.0
+    bytes_tok = lm.weight_bytes + kv_per_pos * mean_ctx
+    peak, peak_kind = peaks()
+    value = world * K / (t_max / 1e3)
+    per_gpu = K / (ms / 1e3)
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "gemv_head_traffic.json")
+    if os.path.exists(tf):
+        try:
+            traffic = json.load(open(tf)).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+    ach = head_bytes / (gemv_ms / 1e3) / 1e9
+    line = {
+        "metric": "decode tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": t_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4 x int8(hi+lo) MMA -> int32, f32 scaling", "data": "synthetic (seeded N(0,0.02) weights, uniform ids)",
+        "config": workload_config(args),
+        "e2e": {"value": world * E / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 16,
+                "d2h_bytes_per_step": 4, "api": "hc_step per token (pinned token in, greedy choice out)"},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<int4> on the 151936x2048 head (+ its act quantiser)",
+                     "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_kind": peak_kind,
+                     "traffic": traffic, "bytes_per_launch": head_bytes, "ms_per_launch": gemv_ms},
+        "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": bytes_tok * per_gpu / 1e9,
+                          "frac": bytes_tok * per_gpu / 1e9 / peak, "ideal_tokens_per_s": peak * 1e9 / bytes_tok},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            tps, dt = cpu_generate(model, 64, 8, os.cpu_count())
+            line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                                    "sample": f"8 greedy decode tokens after a 64-id prompt on the oracle ({dt:.1f} s)"}
+        except Exception as e:  # the baseline is reported, not required for the GPU number
+            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    sess.close()
+    lm.close()
+    dev.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

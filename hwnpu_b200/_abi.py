@@ -91,6 +91,8 @@ SIGNATURES = {
                        C.c_uint32, _i32p]),
     "hc_speculate": (_err, [C.c_void_p, C.c_int32, _i32p, C.c_int32, _i32p, _i32p, _u16p,
                             C.c_uint32, _i32p]),
+    "hc_generate": (_err, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, _i32p, C.c_uint32, _i32p]),
+    "hc_session_stream": (_err, [C.c_void_p, C.POINTER(C.c_void_p)]),
     "hc_seq_reset": (_err, [C.c_void_p, C.c_int32]),
     "hc_seq_truncate": (_err, [C.c_void_p, C.c_int32, C.c_int32]),
     "hc_seq_pos": (_err, [C.c_void_p, C.c_int32, _i32p]),

@@ -76,6 +76,8 @@ struct hc_session {
   uint16_t *logits_dev = nullptr;
   unsigned long long *amax = nullptr;
   int32_t *am_dev = nullptr, *am_host = nullptr, *res_dev = nullptr, *res_host = nullptr;
+  int32_t *gen_out = nullptr, *gen_count = nullptr;  // hc_generate's tokens [cap] and counter
+  cudaGraphExec_t gen_graph = nullptr;
   // captured step graphs by (tokens, accept kernel)
   std::map<int, cudaGraphExec_t> graphs;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;

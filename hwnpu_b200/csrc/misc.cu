@@ -119,7 +119,20 @@ __global__ void spec_accept_kernel(const int32_t *__restrict__ am, const StepTok
   res[1] = next;
 }
 
+__global__ void advance_kernel(StepTok *__restrict__ toks, const int32_t *__restrict__ am,
+                               int32_t *__restrict__ out, int32_t *__restrict__ count) {
+  const int i = *count;
+  out[i] = am[0];
+  toks[0].token = am[0];
+  toks[0].pos += 1;
+  *count = i + 1;
+}
+
 }  // namespace
+
+void advance(StepTok *toks, const int32_t *am, int32_t *out, int32_t *count, cudaStream_t st) {
+  advance_kernel<<<1, 1, 0, st>>>(toks, am, out, count);
+}
 
 void embed(const StepTok *toks, int ntok, const uint16_t *table, const DevMat *head, int hidden,
            float *x, unsigned long long *amax, cudaStream_t st) {

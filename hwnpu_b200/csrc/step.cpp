@@ -17,6 +17,9 @@ hc_session::~hc_session() {
   cudaSetDevice(m->ordinal);
   if (st) cudaStreamSynchronize(st);
   for (auto &g : graphs) cudaGraphExecDestroy(g.second);
+  if (gen_graph) cudaGraphExecDestroy(gen_graph);
+  if (gen_out) cudaFree(gen_out);
+  if (gen_count) cudaFree(gen_count);
   for (void *p : {(void *)kc, (void *)vc, (void *)rope, (void *)x, (void *)qkv, (void *)q, (void *)h,
                   (void *)act, (void *)part_ml, (void *)part_o, (void *)toks_dev, (void *)logits_dev,
                   (void *)amax, (void *)am_dev, (void *)res_dev})
@@ -213,6 +216,8 @@ HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session
   if (char *e = alloc(&s->amax, size_t(T) * hc::kAmaxSlots, "argmax keys")) return e;
   if (char *e = alloc(&s->am_dev, T, "argmax")) return e;
   if (char *e = alloc(&s->res_dev, 2, "accept result")) return e;
+  if (char *e = alloc(&s->gen_out, size_t(s->cap), "generated tokens")) return e;
+  if (char *e = alloc(&s->gen_count, 1, "generated count")) return e;
   HC_TRY_CUDA(cudaHostAlloc(&s->toks_host, sizeof(hc::StepTok) * T, cudaHostAllocDefault));
   HC_TRY_CUDA(cudaHostAlloc(&s->am_host, sizeof(int32_t) * T, cudaHostAllocDefault));
   HC_TRY_CUDA(cudaHostAlloc(&s->res_host, sizeof(int32_t) * 2, cudaHostAllocDefault));
@@ -323,6 +328,58 @@ HC_API char *hc_speculate(hc_session *s, int32_t seq, const int32_t *toks, int32
   s->stats.tokens += n;
   s->stats.weight_bytes = s->m->weight_bytes;
   if (state) *state = HC_STATE_COMPLETED;
+  return nullptr;
+}
+
+HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, int32_t *out_tokens,
+                         uint32_t timeout_ms, int32_t *state) {
+  if (state) *state = HC_STATE_ERROR;
+  if (!s || !out_tokens) return hc::make_error("hc_generate: NULL argument");
+  if (seq < 0 || seq >= int(s->o.max_seqs)) return hc::make_error("hc_generate: sequence out of range");
+  if (n < 1) return hc::make_error("hc_generate: n must be at least 1");
+  if (s->poisoned[seq]) return hc::make_error("hc_generate: sequence failed earlier; reset it");
+  if (s->pos[seq] + n > s->cap) return hc::make_error("hc_generate: would exceed max_context");
+  if (first < 0 || first >= int(s->m->d.vocab)) return hc::make_error("hc_generate: token out of the vocabulary");
+  if (hc::fault_fires(hc::kFaultStep)) return hc::make_error("injected fault: step");
+  HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
+  cudaStream_t st = s->st;
+  s->toks_host[0] = hc::StepTok{first, seq, s->pos[seq], 0};
+  if (!s->gen_graph) {
+    cudaGraph_t graph = nullptr;
+    HC_TRY_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    s->launches_per_chunk[0] = uint64_t(enqueue_chunk(s, 1, false)) + 1;
+    hc::advance(s->toks_dev, s->am_dev, s->gen_out, s->gen_count, st);
+    cudaError_t e = cudaStreamEndCapture(st, &graph);
+    if (e != cudaSuccess) return hc::make_error(std::string("graph capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&s->gen_graph, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return hc::make_error(std::string("graph instantiate: ") + cudaGetErrorString(e));
+  }
+  HC_TRY_CUDA(cudaMemcpyAsync(s->toks_dev, s->toks_host, sizeof(hc::StepTok), cudaMemcpyHostToDevice, st));
+  HC_TRY_CUDA(cudaMemsetAsync(s->gen_count, 0, sizeof(int32_t), st));
+  HC_TRY_CUDA(cudaEventRecord(s->ev0, st));
+  for (int i = 0; i < n; ++i) HC_TRY_CUDA(cudaGraphLaunch(s->gen_graph, st));
+  HC_TRY_CUDA(cudaEventRecord(s->ev1, st));
+  s->stats.launches += uint64_t(n) * s->launches_per_chunk[0];
+  int32_t st_ = HC_STATE_ERROR;
+  char *e = wait_done(s, timeout_ms, &st_);
+  if (e || st_ != HC_STATE_COMPLETED) {
+    s->poisoned[seq] = true;
+    if (state) *state = st_;
+    return e;
+  }
+  HC_TRY_CUDA(cudaMemcpy(out_tokens, s->gen_out, sizeof(int32_t) * n, cudaMemcpyDeviceToHost));
+  s->pos[seq] += n;
+  s->stats.steps += n;
+  s->stats.tokens += n;
+  s->stats.weight_bytes = s->m->weight_bytes;
+  if (state) *state = HC_STATE_COMPLETED;
+  return nullptr;
+}
+
+HC_API char *hc_session_stream(hc_session *s, void **stream) {
+  if (!s || !stream) return hc::make_error("hc_session_stream: NULL argument");
+  *stream = s->st;
   return nullptr;
 }
 

@@ -163,6 +163,21 @@ class Session:
                                      _u16(logits) if logits is not None else None, 0, C.byref(state)))
         return kept.value, nxt.value, (f16_values(logits) if logits is not None else None)
 
+    def generate(self, first, n, seq=0, timeout_ms=0):
+        """Greedy generation of n tokens on the device from `first` (hc_generate)."""
+        out = np.empty(n, np.int32)
+        state = C.c_int32()
+        A.check(A.lib().hc_generate(self.h, seq, int(first), n, _i32(out), timeout_ms, C.byref(state)))
+        if state.value == A.HC_STATE_TIMEOUT:
+            raise TimeoutError("hc_generate timed out")
+        return out
+
+    def stream(self):
+        """The session's cudaStream_t as an integer handle."""
+        p = C.c_void_p()
+        A.check(A.lib().hc_session_stream(self.h, C.byref(p)))
+        return p.value or 0
+
     # -- session ---------------------------------------------------------------------------
     def pos(self, seq=0):
         p = C.c_int32()

@@ -253,6 +253,18 @@ HC_API char *hc_speculate(hc_session *s, int32_t seq, const int32_t *toks, int32
                           int32_t *kept, int32_t *next, uint16_t *logits, uint32_t timeout_ms,
                           int32_t *state);
 
+/* Greedy generation on the device, the per-token loop of chat.Engine.Generate
+ * (internal/chat/engine.go:1509) without a host round trip per token (the device-resident
+ * precedent is ironSession, internal/chat/iron.go:22-260): sequence seq reads `first`, then each
+ * greedy choice (chat/sample.go:80-88) in turn, n tokens in all; out_tokens ([n]) gets the n
+ * choices. The sequence's position moves by n. */
+HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, int32_t *out_tokens,
+                         uint32_t timeout_ms, int32_t *state);
+
+/* The CUDA stream (cudaStream_t) the session's steps run on, for callers that time them with
+ * CUDA events or order their own work after them. */
+HC_API char *hc_session_stream(hc_session *s, void **stream);
+
 /* Session.Reset (session.go:14). */
 HC_API char *hc_seq_reset(hc_session *s, int32_t seq);
 /* Session.Truncate (decode.go:1774): keeps the first len positions. */

@@ -1,0 +1,221 @@
+"""Decode sessions on a B200 through the C ABI against the CPU oracle on identical seeded
+weights and tokens: logits within max-abs 2e-2 and cosine >= 0.9999, greedy tokens identical
+wherever the oracle's top-2 margin exceeds the tolerance (the acceptance bar of BASELINE's
+north star), speculative verification equal to plain greedy decoding, and session state."""
+
+import numpy as np
+import pytest
+
+import hwnpu_b200 as hb
+import oracle_lib as O
+from hwnpu_b200 import _abi as A
+from hwnpu_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+
+TINY = synth.Config("tiny-qwen3", 2, 256, 512, 4, 2, 64, 1000, A.HC_FMT_INT4_ASYM_G32, tied=True, qk_norm=True,
+                    rope_theta=1e6, std=0.05)
+# C1's shapes (4 layers, 1024, 16/4 heads of 64, FFN 2816, V 32000, int8 rows)
+C1 = synth.C1
+# C2's layer shapes and vocabulary on 2 layers (28 in the benchmark)
+C2_2L = synth.Config("c2-2layers", 2, 2048, 6144, 16, 8, 128, 151936, A.HC_FMT_INT4_ASYM_G32, tied=True,
+                     qk_norm=True, rope_theta=1e6)
+SYM4 = synth.Config("tiny-int4sym", 2, 512, 1024, 8, 2, 128, 3000, A.HC_FMT_INT4_SYM_G32, std=0.04)
+
+
+def cosine(a, b):
+    a, b = a.astype(np.float64), b.astype(np.float64)
+    return float(a @ b / np.sqrt((a @ a) * (b @ b)))
+
+
+def compare(got, want):
+    assert np.abs(got - want).max() <= TOL, np.abs(got - want).max()
+    assert cosine(got, want) >= 0.9999
+
+
+def top2_margin(v):
+    s = np.sort(v)
+    return float(s[-1] - s[-2])
+
+
+@pytest.fixture(scope="module")
+def models():
+    return {}
+
+
+def get(models, cfg, seed=0, norm_std=0.1):
+    key = (cfg.name, seed)
+    if key not in models:
+        models[key] = synth.Model(cfg, seed=seed, norm_std=norm_std)
+    return models[key]
+
+
+@pytest.mark.parametrize("cfg,prompt,steps", [(TINY, 9, 8), (SYM4, 5, 6), (C1, 64, 6), (C2_2L, 40, 4)],
+                         ids=lambda v: getattr(v, "name", str(v)))
+def test_decode_matches_oracle(device, models, cfg, prompt, steps):
+    model = get(models, cfg)
+    lm = device.load_model(model)
+    sess = lm.session(max_context=prompt + steps + 4)
+    ref = O.OracleSession(model, prompt + steps + 4)
+    toks = list(synth.tokens(21, cfg.vocab, prompt))
+    got = sess.step_tokens(toks)
+    want = synth.f16_values(ref.step(toks)[0])
+    compare(got, want)
+    for _ in range(steps):
+        g_tok, w_tok = int(np.argmax(got)), int(np.argmax(want))
+        if top2_margin(want) > 2 * TOL:
+            assert g_tok == w_tok
+        got = sess.step_tokens([w_tok])
+        want = synth.f16_values(ref.step([w_tok])[0])
+        compare(got, want)
+    assert sess.pos() == ref.pos() == prompt + steps
+    st = sess.stats()
+    assert st["steps"] == steps + 1 and st["launches"] > 0
+    sess.close()
+    lm.close()
+    ref.close()
+
+
+def test_all_rows_and_chunking(device, models):
+    # 11 tokens in one call cross the 8-token chunks; every row against the oracle's
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    sess = lm.session(max_context=32, max_step=16)
+    ref = O.OracleSession(model, 32)
+    toks = list(synth.tokens(3, TINY.vocab, 11))
+    got = sess.step_tokens(toks, all_rows=True)
+    want = synth.f16_values(ref.step(toks, all_rows=True))
+    for r in range(len(toks)):
+        compare(got[r], want[r])
+    sess.close()
+    lm.close()
+    ref.close()
+
+
+def test_graph_and_eager_agree_bit_for_bit(device, models):
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    a = lm.session(max_context=32, graphs=True)
+    b = lm.session(max_context=32, graphs=False)
+    toks = list(synth.tokens(4, TINY.vocab, 7))
+    la, lb = a.step_batch([0], [toks])[0], b.step_batch([0], [toks])[0]
+    assert np.array_equal(la, lb)
+    for t in (5, 17, 999):
+        la, lb = a.step_batch([0], [[t]])[0], b.step_batch([0], [[t]])[0]
+        assert np.array_equal(la, lb)
+    a.close()
+    b.close()
+    lm.close()
+
+
+def test_speculate_equals_plain_greedy(device, models):
+    # chat TestSpeculate (internal/chat/engine_test.go:348-478) on the device's accept kernel
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    plain = lm.session(max_context=96)
+    prompt = list(synth.tokens(8, TINY.vocab, 6))
+    out_plain = []
+    t = plain.greedy(prompt)
+    for _ in range(20):
+        out_plain.append(t)
+        t = plain.greedy([t])
+    spec = lm.session(max_context=96)
+    out = [spec.greedy(prompt)]
+    rng = np.random.default_rng(2)
+    while len(out) < 20:
+        k = len(out)
+        drafts = [out_plain[k + i] if k + i < len(out_plain) and rng.random() > 0.25 else int(rng.integers(TINY.vocab))
+                  for i in range(4)]
+        kept, nxt, _ = spec.speculate_tokens([out[-1]] + drafts)
+        assert 1 <= kept <= 5
+        out.extend(drafts[:kept - 1])
+        out.append(nxt)
+        assert spec.pos() == len(prompt) + len(out) - 1
+    assert out[:20] == out_plain
+    plain.close()
+    spec.close()
+    lm.close()
+
+
+def test_ragged_batch_equals_single_sequences(device, models):
+    # sequences of different lengths in one call read the same logits as alone
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    batch = lm.session(max_context=40, max_seqs=3, max_step=8)
+    alone = [lm.session(max_context=40) for _ in range(3)]
+    prompts = [list(synth.tokens(30 + i, TINY.vocab, n)) for i, n in enumerate((3, 7, 1))]
+    lb, ab = batch.step_batch([0, 1, 2], prompts)
+    for i in range(3):
+        la, aa = alone[i].step_batch([0], [prompts[i]])
+        assert ab[i] == aa[0]
+        assert np.abs(synth.f16_values(lb[i]) - synth.f16_values(la[0])).max() <= 1e-3
+    for s in alone:
+        s.close()
+    batch.close()
+    lm.close()
+
+
+def test_generate_equals_stepwise_greedy(device, models):
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    a, b = lm.session(max_context=64), lm.session(max_context=64)
+    prompt = list(synth.tokens(12, TINY.vocab, 5))
+    first = a.greedy(prompt)
+    assert b.greedy(prompt) == first
+    gen = a.generate(first, 20)
+    seq, t = [], first
+    for _ in range(20):
+        t = b.greedy([t])
+        seq.append(t)
+    assert gen.tolist() == seq
+    assert a.pos() == b.pos() == 25
+    a.close()
+    b.close()
+    lm.close()
+
+
+def test_truncate_export_import(device, models):
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    s = lm.session(max_context=32)
+    toks = list(synth.tokens(9, TINY.vocab, 10))
+    s.step_tokens(toks[:6])
+    rows = s.export_rows(0, 6)
+    after = s.step_tokens(toks[6:])
+    s.truncate(6)
+    assert s.pos() == 6
+    again = s.step_tokens(toks[6:])
+    assert np.array_equal(after, again)
+    s2 = lm.session(max_context=32)
+    s2.import_rows(0, 6, rows)
+    assert s2.pos() == 6
+    assert np.array_equal(s2.step_tokens(toks[6:]), after)
+    s.reset()
+    assert s.pos() == 0
+    s.close()
+    s2.close()
+    lm.close()
+
+
+def test_injected_faults_leave_the_session_usable(device, models):
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    s = lm.session(max_context=32)
+    A.check(A.lib().hc_set_fault(b"step:1"))
+    with pytest.raises(hb.HcError, match="injected"):
+        s.step_tokens([1, 2, 3])
+    assert s.pos() == 0
+    s.step_tokens([1, 2, 3])
+    A.check(A.lib().hc_set_fault(b"alloc:1"))
+    with pytest.raises(hb.HcError, match="injected"):
+        lm.session(max_context=32)
+    with pytest.raises(hb.HcError, match="max_step"):
+        s.step_tokens(list(range(8)) * 4)
+    with pytest.raises(hb.HcError, match="max_context"):
+        s.generate(1, 40)
+    with pytest.raises(hb.HcError, match="vocabulary"):
+        s.step_tokens([TINY.vocab])
+    s.close()
+    lm.close()
