@@ -145,6 +145,13 @@ def main():
     ap.add_argument("--workload", choices=["c2", "c1"], default="c2")
     ap.add_argument("--e2e-steps", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--chunk-trace", default=None,
+                    help="with --phases: save CTA 0's per-chunk ring events of the last step (.npy)")
+    ap.add_argument("--phases", action="store_true",
+                    help="print the persistent step's per-phase timing (hc_profile_get) after a few steps and exit")
+    ap.add_argument("--profile", type=int, default=0,
+                    help="run this many decode steps between cudaProfilerStart/Stop after the warm-up and exit "
+                         "(for ncu --profile-from-start off)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -172,13 +179,40 @@ def main():
     model = build_model(args.workload)
     dev = hb.Device(local)
     lm = dev.load_model(model)
-    sess = lm.session(max_context=PROMPT + PASS + W + 8, max_step=8)
+    sess = lm.session(max_context=PROMPT + PASS + W + 8, max_step=8, profile=args.phases)
     prompt = synth.tokens(1, model.cfg.vocab, PROMPT)
     first = sess.greedy(prompt)
     base = sess.pos()
     sess.generate(first, W)
     sess.truncate(base)
     stream = torch.cuda.ExternalStream(sess.stream())
+    if args.phases:
+        import numpy as np
+        acc = None
+        for _ in range(8):
+            sess.generate(first, 1)
+            ph = sess.profile()
+            acc = ph if acc is None else acc + ph
+        acc /= 8
+        cyc = sess.last_cycles
+        if args.chunk_trace:
+            np.save(args.chunk_trace, sess.last_chunks)
+            np.save(args.chunk_trace.replace(".npy", "_unit.npy"), sess.last_unit)
+        L = model.cfg.layers
+        names = ["qkv", "attention", "o", "gate/up", "down"]
+        per = {n: [round(float(x), 3) for x in acc[1 + i:1 + 5 * L:5].mean(axis=0)] for i, n in enumerate(names)}
+        print(json.dumps({"phase_us_per_layer_inputs_weights_epilogue_barrier": per, "embed": acc[0].tolist(),
+                          "head": acc[1 + 5 * L].tolist(), "total_us": float(acc.sum()),
+                          "cycles_producer_waited_busy_consumer_waited_busy": [float(x) for x in cyc]}), flush=True)
+        return
+    if args.profile:
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        sess.generate(first, args.profile)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profiled_steps": args.profile, "launches_per_step": sess.stats()["launches"]}), flush=True)
+        return
     launches0 = sess.stats()["launches"]
 
     def barrier():

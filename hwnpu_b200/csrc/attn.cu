@@ -83,9 +83,11 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(const float *__restrict__
   }
 }
 
-// One CTA per (split, kv head, token), 4 warps over its keys; each warp keeps an online softmax
-// per query head of the group (GQA: heads kvh*rep .. kvh*rep+rep-1 read kv head kvh).
-template <int E, int REP>
+// One CTA per (split, kv head, token). Its 16 groups of 8 lanes each take a key at a time (8 lanes
+// cover the key's head_dim in 16-byte loads, so a warp has 4 keys in flight), keeping an online
+// softmax for every query head of the kv head's group (GQA: heads kvh*REP .. kvh*REP+REP-1);
+// the groups then merge, first within a warp by shuffles, then across the 4 warps in smem.
+template <int HD, int REP>
 __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict__ q,
                                                          const StepTok *__restrict__ toks,
                                                          AttnGeom g,
@@ -93,12 +95,12 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
                                                          const uint16_t *__restrict__ vcache,
                                                          int splits, float *__restrict__ part_ml,
                                                          float *__restrict__ part_o) {
-  constexpr int hd = E * 32;
-  constexpr int rep = REP;
+  constexpr int E = HD / 8;  // elements a lane: 16 (hd 128) or 8 (hd 64)
   __shared__ float sm_m[4][REP], sm_l[4][REP];
-  __shared__ float sm_o[4][REP][hd];
+  __shared__ float sm_o[4][REP][HD];
   const int s = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = threadIdx.x >> 3, l8 = threadIdx.x & 7;
   const StepTok tk = toks[t];
   const int P = tk.pos;
   const int lo = g.window > 0 ? max(0, P - g.window + 1) : 0;
@@ -107,10 +109,14 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
   const int k0 = lo + s * chunk, k1 = min(P + 1, k0 + chunk);
   float qv[REP][E];
 #pragma unroll
-  for (int r = 0; r < rep; ++r)
+  for (int r = 0; r < REP; ++r) {
+    const float4 *qp = reinterpret_cast<const float4 *>(q + (size_t(t) * g.heads + kvh * REP + r) * HD + l8 * E);
 #pragma unroll
-    for (int k = 0; k < E; ++k)
-      qv[r][k] = q[(size_t(t) * g.heads + kvh * rep + r) * hd + lane * E + k];
+    for (int k = 0; k < E / 4; ++k) {
+      const float4 v = qp[k];
+      qv[r][4 * k] = v.x; qv[r][4 * k + 1] = v.y; qv[r][4 * k + 2] = v.z; qv[r][4 * k + 3] = v.w;
+    }
+  }
   float m[REP], l[REP], o[REP][E];
 #pragma unroll
   for (int r = 0; r < REP; ++r) {
@@ -119,71 +125,94 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
 #pragma unroll
     for (int k = 0; k < E; ++k) o[r][k] = 0.f;
   }
-  const size_t base = (size_t(tk.slot) * g.kv_heads + kvh) * size_t(g.cap) * hd;
-  for (int j = k0 + warp; j < k1; j += 4) {
-    const uint16_t *kr = kcache + base + size_t(j) * hd + lane * E;
-    const uint16_t *vr = vcache + base + size_t(j) * hd + lane * E;
+  const size_t base = (size_t(tk.slot) * g.kv_heads + kvh) * size_t(g.cap) * HD;
+  // the trip count is the same for every lane (the shuffles below take the whole warp); a group
+  // whose key is past the chunk's end loads nothing and leaves its softmax as it is
+  for (int j0 = k0; j0 < k1; j0 += 16) {
+    const int j = j0 + grp;
+    const bool valid = j < k1;
     float kf[E], vf[E];
-    if constexpr (E == 4) {
-      const uint2 kk = *reinterpret_cast<const uint2 *>(kr);
-      const uint2 vv = *reinterpret_cast<const uint2 *>(vr);
-      const __half2 k01 = *reinterpret_cast<const __half2 *>(&kk.x), k23 = *reinterpret_cast<const __half2 *>(&kk.y);
-      const __half2 v01 = *reinterpret_cast<const __half2 *>(&vv.x), v23 = *reinterpret_cast<const __half2 *>(&vv.y);
-      kf[0] = __low2float(k01); kf[1] = __high2float(k01); kf[2] = __low2float(k23); kf[3] = __high2float(k23);
-      vf[0] = __low2float(v01); vf[1] = __high2float(v01); vf[2] = __low2float(v23); vf[3] = __high2float(v23);
-    } else {
 #pragma unroll
-      for (int k = 0; k < E; ++k) {
-        kf[k] = __half2float(__ushort_as_half(kr[k]));
-        vf[k] = __half2float(__ushort_as_half(vr[k]));
+    for (int u = 0; u < E / 8; ++u) {
+      uint4 kk = make_uint4(0, 0, 0, 0), vv = kk;
+      if (valid) {
+        kk = reinterpret_cast<const uint4 *>(kcache + base + size_t(j) * HD + l8 * E)[u];
+        vv = reinterpret_cast<const uint4 *>(vcache + base + size_t(j) * HD + l8 * E)[u];
+      }
+      const uint32_t kw[4] = {kk.x, kk.y, kk.z, kk.w}, vw[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2 k2 = *reinterpret_cast<const __half2 *>(&kw[i]);
+        const __half2 v2 = *reinterpret_cast<const __half2 *>(&vw[i]);
+        kf[8 * u + 2 * i] = __low2float(k2); kf[8 * u + 2 * i + 1] = __high2float(k2);
+        vf[8 * u + 2 * i] = __low2float(v2); vf[8 * u + 2 * i + 1] = __high2float(v2);
       }
     }
 #pragma unroll
-    for (int r = 0; r < rep; ++r) {
+    for (int r = 0; r < REP; ++r) {
       float d = 0.f;
 #pragma unroll
       for (int k = 0; k < E; ++k) d = fmaf(qv[r][k], kf[k], d);
-      d = warp_sum(d);
-      const float sc = d * g.score_scale;
-      if (sc > m[r]) {
-        const float corr = expf(m[r] - sc);
-        l[r] *= corr;
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      d += __shfl_xor_sync(0xffffffffu, d, 4);
+      if (valid) {
+        const float sc = d * g.score_scale;
+        const float mn = fmaxf(m[r], sc);
+        const float corr = expf(m[r] - mn), p = expf(sc - mn);
+        l[r] = fmaf(l[r], corr, p);
 #pragma unroll
-        for (int k = 0; k < E; ++k) o[r][k] *= corr;
-        m[r] = sc;
+        for (int k = 0; k < E; ++k) o[r][k] = fmaf(o[r][k], corr, p * vf[k]);
+        m[r] = mn;
       }
-      const float p = expf(sc - m[r]);
-      l[r] += p;
-#pragma unroll
-      for (int k = 0; k < E; ++k) o[r][k] = fmaf(p, vf[k], o[r][k]);
     }
   }
+  // merge the 4 groups of the warp (lanes differing in bits 3 and 4)
 #pragma unroll
-  for (int r = 0; r < rep; ++r) {
-    if (lane == 0) { sm_m[warp][r] = m[r]; sm_l[warp][r] = l[r]; }
+  for (int r = 0; r < REP; ++r) {
+    float M = m[r];
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 8));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
+    const float f = l[r] > 0.f ? expf(m[r] - M) : 0.f;
+    float L = l[r] * f;
+    L += __shfl_xor_sync(0xffffffffu, L, 8);
+    L += __shfl_xor_sync(0xffffffffu, L, 16);
 #pragma unroll
-    for (int k = 0; k < E; ++k) sm_o[warp][r][lane * E + k] = o[r][k];
+    for (int k = 0; k < E; ++k) {
+      float v = o[r][k] * f;
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      o[r][k] = v;
+    }
+    if (lane < 8) {
+#pragma unroll
+      for (int k = 0; k < E; ++k) sm_o[warp][r][l8 * E + k] = o[r][k];
+    }
+    if (lane == 0) { sm_m[warp][r] = M; sm_l[warp][r] = L; }
   }
   __syncthreads();
-  // warp r' merges head r' of the group (4 warps, rep up to 8: loop)
-  for (int r = warp; r < rep; r += 4) {
+  // merge the 4 warps: thread e of the CTA takes element e of every head of the group
+  for (int r = 0; r < REP; ++r) {
     float M = -INFINITY;
+#pragma unroll
     for (int w = 0; w < 4; ++w)
       if (sm_l[w][r] > 0.f) M = fmaxf(M, sm_m[w][r]);
-    float L = 0.f;
-    for (int w = 0; w < 4; ++w)
-      if (sm_l[w][r] > 0.f) L += sm_l[w][r] * expf(sm_m[w][r] - M);
-    const int h = kvh * rep + r;
-    const size_t pi = (size_t(t) * g.heads + h) * splits + s;
-    if (lane == 0) {
+    float fw[4], L = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      fw[w] = sm_l[w][r] > 0.f ? expf(sm_m[w][r] - M) : 0.f;
+      L += sm_l[w][r] * fw[w];
+    }
+    const size_t pi = (size_t(t) * g.heads + kvh * REP + r) * splits + s;
+    if (threadIdx.x == 0) {
       part_ml[pi * 2] = M;
       part_ml[pi * 2 + 1] = L;
     }
-    for (int e = lane; e < hd; e += 32) {
+    for (int e = threadIdx.x; e < HD; e += blockDim.x) {
       float acc = 0.f;
-      for (int w = 0; w < 4; ++w)
-        if (sm_l[w][r] > 0.f) acc += sm_o[w][r][e] * expf(sm_m[w][r] - M);
-      part_o[pi * hd + e] = acc;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) acc = fmaf(sm_o[w][r][e], fw[w], acc);
+      part_o[pi * HD + e] = acc;
     }
   }
 }
@@ -206,14 +235,14 @@ void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g
                 float *part_o, cudaStream_t st) {
   dim3 grid(splits, g.kv_heads, ntok);
   const int rep = g.heads / g.kv_heads;
-#define HC_ATT(E, R)                                                                         \
-  if (g.hd == E * 32 && rep == R) {                                                          \
-    attn_split_kernel<E, R><<<grid, 128, 0, st>>>(q, toks, g, kcache, vcache, splits, part_ml, \
+#define HC_ATT(D, R)                                                                         \
+  if (g.hd == D && rep == R) {                                                               \
+    attn_split_kernel<D, R><<<grid, 128, 0, st>>>(q, toks, g, kcache, vcache, splits, part_ml, \
                                                   part_o);                                   \
     return;                                                                                  \
   }
-  HC_ATT(4, 1) HC_ATT(4, 2) HC_ATT(4, 4) HC_ATT(4, 8)
-  HC_ATT(2, 1) HC_ATT(2, 2) HC_ATT(2, 4) HC_ATT(2, 8)
+  HC_ATT(128, 1) HC_ATT(128, 2) HC_ATT(128, 4) HC_ATT(128, 8)
+  HC_ATT(64, 1) HC_ATT(64, 2) HC_ATT(64, 4) HC_ATT(64, 8)
 #undef HC_ATT
 }
 

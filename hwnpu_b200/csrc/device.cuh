@@ -5,6 +5,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "common.h"
+
 namespace hc {
 
 // mma.sync m16n8k32 with int32 accumulation: A (16x32, row) signed bytes, B (32x8, col)
@@ -70,6 +72,29 @@ __device__ __forceinline__ int warp_sum_i(int v) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// The float32 value of (row, col) of a repacked matrix, as dequant_kernel computes it.
+__device__ __forceinline__ float tile_value(const uint8_t *tiles, const float *row_scale, int kind, int ktiles,
+                            int tile_bytes, int r, int col) {
+  const int rt = r / 8, g = r % 8, kt = col / kTileCols, cc = col % kTileCols;
+  const int grp = cc / 32, e = cc % 32, i4 = e / 4, p = e % 4;
+  const int c = grp & 3, hi = grp >> 2, lane = g * 4 + c, sl = grp * 4 + g / 2;
+  const uint8_t *tile = tiles + (size_t(rt) * ktiles + kt) * tile_bytes;
+  if (kind == kKindInt8) return float(int8_t(tile[lane * 64 + i4 * 8 + hi * 4 + p])) * row_scale[r];
+  if (kind == kKindInt4) {
+    const uint8_t by = tile[lane * 32 + i4 * 4 + p];
+    const int q = hi ? (by >> 4) : (by & 15);
+    const uint16_t *sz = reinterpret_cast<const uint16_t *>(tile + kTileCodes4 + sl * 8);
+    const float s = __half2float(__ushort_as_half(sz[g & 1]));
+    const float z = __half2float(__ushort_as_half(sz[2 + (g & 1)]));
+    return __fmul_rn(__fsub_rn(float(q), z), s);
+  }
+  const uint8_t by = tile[lane * 32 + i4 * 4 + hi * 2 + p / 2];
+  const int code = (p & 1) ? (by >> 4) : (by & 15);
+  const float mag[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+  const float val = (code & 8) ? -mag[code & 7] : mag[code & 7];
+  return __fmul_rn(val, __uint_as_float(uint32_t(tile[kTileCodes4 + sl * 2 + (g & 1)]) << 23));
 }
 
 }  // namespace hc

@@ -7,6 +7,7 @@
 #include <vector>
 
 #include "kernels.h"
+#include "mk.h"
 #include "repack.h"
 
 namespace hc {
@@ -78,11 +79,21 @@ struct hc_session {
   int32_t *am_dev = nullptr, *am_host = nullptr, *res_dev = nullptr, *res_host = nullptr;
   int32_t *gen_out = nullptr, *gen_count = nullptr;  // hc_generate's tokens [cap] and counter
   cudaGraphExec_t gen_graph = nullptr;
+  // the persistent one-launch step (mk.h), when the model has one
+  bool mk = false;
+  int mk_ctas = 0;
+  hc::MkLayer *mk_layers = nullptr;  // device [layers]
+  uint8_t *mk_act[2] = {nullptr, nullptr};
+  double *mk_sq = nullptr;
+  unsigned *mk_cnt = nullptr, *mk_bar = nullptr;
+  int *mk_status = nullptr, *mk_status_host = nullptr;
+  unsigned long long *mk_trace = nullptr;  // HC_SESSION_PROFILE
   // captured step graphs by (tokens, accept kernel)
   std::map<int, cudaGraphExec_t> graphs;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   hc_stats stats{};
   uint64_t launches_per_chunk[hc::kMaxChunk + 1] = {};
+  std::map<int, uint64_t> launches_per_key;
   ~hc_session();
 };
 

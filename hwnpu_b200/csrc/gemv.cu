@@ -230,12 +230,14 @@ __device__ __forceinline__ void quant_group(float v, uint8_t *act_tile, int gi, 
   }
 }
 
+// One CTA per (token, column tile): the RMS norm's sum of squares is taken over the whole row by
+// every CTA (the row is a few KB in L2), then the CTA quantises its tile's 8 groups, one warp each.
 __global__ void __launch_bounds__(256) act_quant_kernel(const float *__restrict__ x, int ldx,
                                                         int n, const float *__restrict__ norm_w,
                                                         float scale, float eps16,
                                                         uint8_t *__restrict__ act, int ktiles) {
   __shared__ double red[32];
-  const int t = blockIdx.x;
+  const int t = blockIdx.y, kt = blockIdx.x;
   const float *xt = x + size_t(t) * ldx;
   const float inv = scale == 1.f ? 1.f : 1.f / scale;
   float r = 1.f;
@@ -251,59 +253,61 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const float *__restrict_
     r = float(1.0 / sqrt(double(ms) + double(eps16)));
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int grp = warp; grp < ktiles * kGroupsPerTile; grp += blockDim.x >> 5) {
-    const int col = grp * kGroup + lane;
-    float v = 0.f;
-    if (col < n) {
-      v = xt[col];
-      if (norm_w) {
-        const float xs = scale == 1.f ? v : v * inv;
-        const float y = xs * r;
-        v = y * norm_w[col];
-      }
+  const int col = (kt * kGroupsPerTile + warp) * kGroup + lane;
+  float v = 0.f;
+  if (col < n) {
+    v = xt[col];
+    if (norm_w) {
+      const float xs = scale == 1.f ? v : v * inv;
+      const float y = xs * r;
+      v = y * norm_w[col];
     }
-    uint8_t *tile = act + (size_t(t) * ktiles + grp / kGroupsPerTile) * kActTile;
-    quant_group(v, tile, grp % kGroupsPerTile, lane);
   }
+  quant_group(v, act + (size_t(t) * ktiles + kt) * kActTile, warp, lane);
 }
 
-// Merges the attention partials of each head (Flash-Decoding), with a sink logit when given
-// (paged.Merge.AddSink, paged.go:281-297), into smem, then quantises the vector.
-__global__ void __launch_bounds__(256) attn_merge_kernel(const float *__restrict__ part_ml,
+// Merges the attention partials of one (token, head) (Flash-Decoding; with a sink logit when
+// given, paged.Merge.AddSink, paged.go:281-297) and quantises the head's groups of 32 (a group
+// never crosses a head: head_dim is 64 or 128).
+__global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict__ part_ml,
                                                          const float *__restrict__ part_o,
                                                          const float *__restrict__ sinks,
                                                          int heads, int hd, int splits,
                                                          uint8_t *__restrict__ act, int ktiles,
                                                          float *__restrict__ o_out) {
-  extern __shared__ float ov[];
-  const int t = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int h = warp; h < heads; h += nw) {
-    const float *ml = part_ml + (size_t(t) * heads + h) * splits * 2;
+  __shared__ float wsh[64];
+  __shared__ float stat[2];
+  const int h = blockIdx.x, t = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float *ml = part_ml + (size_t(t) * heads + h) * splits * 2;
+  if (warp == 0) {
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    if (lane < splits) { m0 = ml[2 * lane]; l0 = ml[2 * lane + 1]; }
+    if (lane + 32 < splits) { m1 = ml[2 * (lane + 32)]; l1 = ml[2 * (lane + 32) + 1]; }
     float M = sinks ? sinks[h] : -INFINITY;
-    for (int s = 0; s < splits; ++s)
-      if (ml[2 * s + 1] > 0.f) M = fmaxf(M, ml[2 * s]);
-    float L = sinks ? expf(sinks[h] - M) : 0.f;
-    for (int s = 0; s < splits; ++s)
-      if (ml[2 * s + 1] > 0.f) L += ml[2 * s + 1] * expf(ml[2 * s] - M);
-    const float invL = L > 0.f ? 1.f / L : 0.f;
-    for (int d = lane; d < hd; d += 32) {
-      float o = 0.f;
-      for (int s = 0; s < splits; ++s)
-        if (ml[2 * s + 1] > 0.f)
-          o += part_o[((size_t(t) * heads + h) * splits + s) * hd + d] * expf(ml[2 * s] - M);
-      ov[h * hd + d] = o * invL;
-    }
+    M = fmaxf(M, l0 > 0.f ? m0 : -INFINITY);
+    M = fmaxf(M, l1 > 0.f ? m1 : -INFINITY);
+    M = warp_max(M);
+    const float w0 = l0 > 0.f ? expf(m0 - M) : 0.f, w1 = l1 > 0.f ? expf(m1 - M) : 0.f;
+    float L = warp_sum(l0 * w0 + l1 * w1);
+    if (sinks) L += expf(sinks[h] - M);
+    if (lane < splits) wsh[lane] = w0;
+    if (lane + 32 < splits) wsh[lane + 32] = w1;
+    if (lane == 0) stat[0] = L > 0.f ? 1.f / L : 0.f;
   }
   __syncthreads();
-  const int n = heads * hd;
-  if (o_out)
-    for (int i = threadIdx.x; i < n; i += blockDim.x) o_out[size_t(t) * n + i] = ov[i];
-  for (int grp = warp; grp < ktiles * kGroupsPerTile; grp += nw) {
-    const int col = grp * kGroup + lane;
-    const float v = col < n ? ov[col] : 0.f;
-    uint8_t *tile = act + (size_t(t) * ktiles + grp / kGroupsPerTile) * kActTile;
-    quant_group(v, tile, grp % kGroupsPerTile, lane);
+  const float invL = stat[0];
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    const float *po = part_o + ((size_t(t) * heads + h) * splits) * hd + d;
+    float o = 0.f;
+#pragma unroll 8
+    for (int s = 0; s < splits; ++s) o = fmaf(po[size_t(s) * hd], wsh[s], o);
+    o *= invL;
+    if (o_out) o_out[(size_t(t) * heads + h) * hd + d] = o;
+    // one warp a group of 32: warp w of this head holds columns h*hd + 32w .. + 31
+    const int gcol = h * hd + d;
+    const int grp = gcol / kGroup;
+    quant_group(o, act + (size_t(t) * ktiles + grp / kGroupsPerTile) * kActTile, grp % kGroupsPerTile, lane);
   }
 }
 
@@ -365,14 +369,20 @@ void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cud
 
 void act_quant(const float *x, int ldx, int n, int ntok, const float *norm_w, float scale,
                float eps16, uint8_t *act, int ktiles, cudaStream_t st) {
-  act_quant_kernel<<<ntok, 256, 0, st>>>(x, ldx, n, norm_w, scale, eps16, act, ktiles);
+  act_quant_kernel<<<dim3(ktiles, ntok), 256, 0, st>>>(x, ldx, n, norm_w, scale, eps16, act, ktiles);
 }
 
 void attn_merge_quant(const float *part_ml, const float *part_o, const float *sinks, int ntok,
                       int heads, int hd, int splits, uint8_t *act, int ktiles, float *o_out,
                       cudaStream_t st) {
-  attn_merge_kernel<<<ntok, 256, size_t(heads) * hd * sizeof(float), st>>>(
-      part_ml, part_o, sinks, heads, hd, splits, act, ktiles, o_out);
+  // columns past heads*hd in the last tile are zero groups
+  const int n = heads * hd;
+  if (n % kTileCols) {
+    for (int t = 0; t < ntok; ++t)
+      cudaMemsetAsync(act + (size_t(t) * ktiles + ktiles - 1) * kActTile, 0, kActTile, st);
+  }
+  attn_merge_kernel<<<dim3(heads, ntok), hd, 0, st>>>(part_ml, part_o, sinks, heads, hd, splits, act,
+                                                     ktiles, o_out);
 }
 
 void dequant(const DevMat &W, int row0, int nrows, float *out, cudaStream_t st) {

@@ -5,38 +5,15 @@
 namespace hc {
 namespace {
 
-// The float32 value of (row, col) of a repacked matrix, as dequant_kernel computes it.
-__device__ float tile_value(const uint8_t *tiles, const float *row_scale, int kind, int ktiles,
-                            int tile_bytes, int r, int col) {
-  const int rt = r / 8, g = r % 8, kt = col / kTileCols, cc = col % kTileCols;
-  const int grp = cc / 32, e = cc % 32, i4 = e / 4, p = e % 4;
-  const int c = grp & 3, hi = grp >> 2, lane = g * 4 + c, sl = grp * 4 + g / 2;
-  const uint8_t *tile = tiles + (size_t(rt) * ktiles + kt) * tile_bytes;
-  if (kind == kKindInt8) return float(int8_t(tile[lane * 64 + i4 * 8 + hi * 4 + p])) * row_scale[r];
-  if (kind == kKindInt4) {
-    const uint8_t by = tile[lane * 32 + i4 * 4 + p];
-    const int q = hi ? (by >> 4) : (by & 15);
-    const uint16_t *sz = reinterpret_cast<const uint16_t *>(tile + kTileCodes4 + sl * 8);
-    const float s = __half2float(__ushort_as_half(sz[g & 1]));
-    const float z = __half2float(__ushort_as_half(sz[2 + (g & 1)]));
-    return __fmul_rn(__fsub_rn(float(q), z), s);
-  }
-  const uint8_t by = tile[lane * 32 + i4 * 4 + hi * 2 + p / 2];
-  const int code = (p & 1) ? (by >> 4) : (by & 15);
-  const float mag[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
-  const float val = (code & 8) ? -mag[code & 7] : mag[code & 7];
-  return __fmul_rn(val, __uint_as_float(uint32_t(tile[kTileCodes4 + sl * 2 + (g & 1)]) << 23));
-}
-
 // llm.TokenRow (internal/llm/llm.go:43-60): the token's row of the embedding table, the program's
 // fp16 input x; a tied table is the head's rows in its format, rounded to fp16.
 __global__ void embed_kernel(const StepTok *__restrict__ toks, const uint16_t *__restrict__ table,
                              const uint8_t *__restrict__ tiles, const float *__restrict__ row_scale,
                              int kind, int ktiles, int tile_bytes, int hidden,
                              float *__restrict__ x, unsigned long long *__restrict__ amax) {
-  const int t = blockIdx.x;
+  const int t = blockIdx.y;
   const int tok = toks[t].token;
-  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < hidden; c += blockDim.x * gridDim.x) {
     float v;
     if (table) {
       v = __half2float(__ushort_as_half(table[size_t(tok) * hidden + c]));
@@ -46,7 +23,7 @@ __global__ void embed_kernel(const StepTok *__restrict__ toks, const uint16_t *_
     }
     x[size_t(t) * hidden + c] = v;
   }
-  if (amax)
+  if (amax && blockIdx.x == 0)
     for (int i = threadIdx.x; i < kAmaxSlots; i += blockDim.x) amax[t * kAmaxSlots + i] = 0ull;
 }
 
@@ -136,7 +113,7 @@ void advance(StepTok *toks, const int32_t *am, int32_t *out, int32_t *count, cud
 
 void embed(const StepTok *toks, int ntok, const uint16_t *table, const DevMat *head, int hidden,
            float *x, unsigned long long *amax, cudaStream_t st) {
-  embed_kernel<<<ntok, 256, 0, st>>>(toks, table, head ? head->tiles : nullptr,
+  embed_kernel<<<dim3((hidden + 255) / 256, ntok), 256, 0, st>>>(toks, table, head ? head->tiles : nullptr,
                                      head ? head->row_scale : nullptr, head ? head->kind : 0,
                                      head ? head->ktiles : 0, head ? head->tile_bytes : 0, hidden,
                                      x, amax);

@@ -19,6 +19,10 @@ hc_session::~hc_session() {
   for (auto &g : graphs) cudaGraphExecDestroy(g.second);
   if (gen_graph) cudaGraphExecDestroy(gen_graph);
   if (gen_out) cudaFree(gen_out);
+  for (void *p : {(void *)mk_layers, (void *)mk_act[0], (void *)mk_act[1], (void *)mk_sq, (void *)mk_cnt,
+                  (void *)mk_bar, (void *)mk_status, (void *)mk_trace})
+    if (p) cudaFree(p);
+  if (mk_status_host) cudaFreeHost(mk_status_host);
   if (gen_count) cudaFree(gen_count);
   for (void *p : {(void *)kc, (void *)vc, (void *)rope, (void *)x, (void *)qkv, (void *)q, (void *)h,
                   (void *)act, (void *)part_ml, (void *)part_o, (void *)toks_dev, (void *)logits_dev,
@@ -102,14 +106,86 @@ int enqueue_chunk(hc_session *s, int n, bool accept) {
   return k;
 }
 
+// The persistent step's parameters for n tokens (one per sequence); gen: hc_generate's feedback.
+hc::MkParams mk_params(hc_session *s, int n, bool gen) {
+  hc_model *m = s->m;
+  const auto &d = m->d;
+  hc::MkParams p{};
+  p.layers = int(d.layers);
+  p.D = int(d.hidden);
+  p.F = int(d.inter);
+  p.H = int(d.heads);
+  p.KV = int(d.kv_heads);
+  p.hd = int(d.head_dim);
+  p.V = int(d.vocab);
+  p.cap = s->cap;
+  p.ntok = n;
+  p.kind = m->head->m.kind;
+  p.kt_d = p.D / hc::kTileCols;
+  p.kt_f = p.F / hc::kTileCols;
+  p.kt_o = p.H * p.hd / hc::kTileCols;
+  p.rt_qkv = m->layers[0].qkv->m.rtiles;
+  p.rt_head = m->head->m.rtiles;
+  p.splits = std::max(1, std::min(kMaxSplits, s->mk_ctas / (n * p.KV)));
+  p.sc_in0 = m->norm_in0.scale;
+  p.eps_in0 = m->norm_in0.eps16;
+  p.sc = m->norm_mid.scale;
+  p.eps = m->norm_mid.eps16;
+  p.score_scale = m->score_scale;
+  p.L = s->mk_layers;
+  p.head = m->head->m.tiles;
+  p.head_scale = m->head->m.row_scale;
+  p.embed = m->embed;
+  p.in_norm0 = m->layers[0].in_norm;
+  p.rope = s->rope;
+  p.toks = s->toks_dev;
+  p.x = s->x;
+  p.qkv = s->qkv;
+  p.act[0] = s->mk_act[0];
+  p.act[1] = s->mk_act[1];
+  p.sq = s->mk_sq;
+  p.part_ml = s->part_ml;
+  p.part_o = s->part_o;
+  p.cnt = s->mk_cnt;
+  p.logits = s->logits_dev;
+  p.amax = s->amax;
+  p.am = s->am_dev;
+  p.gen_out = gen ? s->gen_out : nullptr;
+  p.gen_count = gen ? s->gen_count : nullptr;
+  p.bar = s->mk_bar;
+  p.status = s->mk_status;
+  p.spin_limit = 4000000000ll;  // ~2 s of SM clocks
+  p.trace = s->mk_trace;
+  return p;
+}
+
+// Enqueues the persistent step (barrier and status zeroed first); returns its launches.
+int enqueue_mk(hc_session *s, int n, bool gen) {
+  cudaMemsetAsync(s->mk_bar, 0, sizeof(unsigned), s->st);
+  cudaMemsetAsync(s->mk_status, 0, sizeof(int), s->st);
+  hc::mk_launch(mk_params(s, n, gen), s->mk_ctas, s->st);
+  return 1;
+}
+
+bool mk_chunk(const hc_session *s, int n) {
+  if (!s->mk || !hc::mk_supported(s->m->head->m.kind, n, int(s->m->d.head_dim), int(s->m->d.heads / s->m->d.kv_heads)))
+    return false;
+  for (int i = 0; i < n; ++i)
+    for (int j = 0; j < i; ++j)
+      if (s->toks_host[i].slot == s->toks_host[j].slot) return false;  // one token a sequence
+  return true;
+}
+
 // The whole chunk: tokens in, greedy choices (and the accept result) out, as one graph.
 char *run_chunk(hc_session *s, int n, bool accept) {
   cudaStream_t st = s->st;
   const bool use_graph = !(s->o.flags & HC_SESSION_NO_GRAPH);
-  const int key = n * 2 + (accept ? 1 : 0);
+  const bool mk = !accept && mk_chunk(s, n);
+  const int key = n * 4 + (accept ? 1 : 0) + (mk ? 2 : 0);
   auto enqueue_all = [&]() -> int {
     cudaMemcpyAsync(s->toks_dev, s->toks_host, sizeof(hc::StepTok) * n, cudaMemcpyHostToDevice, st);
-    int k = enqueue_chunk(s, n, accept);
+    int k = mk ? enqueue_mk(s, n, false) : enqueue_chunk(s, n, accept);
+    if (mk) cudaMemcpyAsync(s->mk_status_host, s->mk_status, sizeof(int), cudaMemcpyDeviceToHost, st);
     cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
     if (accept) cudaMemcpyAsync(s->res_host, s->res_dev, sizeof(int32_t) * 2, cudaMemcpyDeviceToHost, st);
     return k;
@@ -117,7 +193,7 @@ char *run_chunk(hc_session *s, int n, bool accept) {
   if (use_graph && !s->graphs.count(key)) {
     cudaGraph_t graph = nullptr;
     HC_TRY_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    s->launches_per_chunk[n] = uint64_t(enqueue_all());
+    s->launches_per_key[key] = uint64_t(enqueue_all());
     cudaError_t e = cudaStreamEndCapture(st, &graph);
     if (e != cudaSuccess) return hc::make_error(std::string("graph capture: ") + cudaGetErrorString(e));
     cudaGraphExec_t exec = nullptr;
@@ -130,11 +206,18 @@ char *run_chunk(hc_session *s, int n, bool accept) {
   if (use_graph) {
     HC_TRY_CUDA(cudaGraphLaunch(s->graphs[key], st));
   } else {
-    s->launches_per_chunk[n] = uint64_t(enqueue_all());
+    s->launches_per_key[key] = uint64_t(enqueue_all());
   }
   HC_TRY_CUDA(cudaGetLastError());
   HC_TRY_CUDA(cudaEventRecord(s->ev1, st));
-  s->stats.launches += s->launches_per_chunk[n];
+  s->stats.launches += use_graph ? s->launches_per_key[key] : s->launches_per_key[key];
+  return nullptr;
+}
+
+// The persistent step's status after a wait: an error string when a barrier gave up.
+char *mk_status_error(hc_session *s) {
+  if (s->mk && *s->mk_status_host)
+    return hc::make_error("step: a device grid barrier timed out (phase " + std::to_string(*s->mk_status_host) + ")");
   return nullptr;
 }
 
@@ -161,6 +244,61 @@ char *wait_done(hc_session *s, uint32_t timeout_ms, int32_t *state) {
   cudaEventElapsedTime(&ms, s->ev0, s->ev1);
   s->stats.last_step_us = double(ms) * 1000.0;
   if (state) *state = HC_STATE_COMPLETED;
+  return nullptr;
+}
+
+// Sets up the persistent one-launch step when the model and the device allow it.
+char *mk_setup(hc_session *s) {
+  hc_model *m = s->m;
+  const auto &d = m->d;
+  if (s->o.flags & HC_SESSION_NO_MEGAKERNEL) return nullptr;
+  const int kind = m->head->m.kind, rep = int(d.heads / d.kv_heads);
+  if (!hc::mk_supported(kind, 1, int(d.head_dim), rep)) return nullptr;
+  if (d.hidden % hc::kTileCols || d.inter % hc::kTileCols || (d.heads * d.head_dim) % hc::kTileCols) return nullptr;
+  for (auto &w : m->layers)
+    if (w.qkv->m.kind != kind || w.o->m.kind != kind || w.gu->m.kind != kind || w.down->m.kind != kind ||
+        w.gu->m.bias || w.down->m.bias)
+      return nullptr;
+  int coop = 0;
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->ordinal);
+  if (!coop) return nullptr;
+  s->mk_ctas = hc::mk_max_ctas(m->ordinal);
+  hc::MkParams probe = mk_params(s, kMaxChunk, false);
+  const size_t smem = hc::mk_smem(probe, s->mk_ctas);
+  if (smem == 0) return nullptr;
+  HC_TRY_CUDA(hc::mk_prepare(225 * 1024));  // every layout mk_layout makes fits in it
+  std::vector<hc::MkLayer> L(d.layers);
+  for (size_t i = 0; i < L.size(); ++i) {
+    const hc::LayerW &w = m->layers[i];
+    L[i] = hc::MkLayer{w.qkv->m.tiles, w.o->m.tiles, w.gu->m.tiles, w.down->m.tiles,
+                       w.qkv->m.row_scale, w.o->m.row_scale, w.gu->m.row_scale, w.down->m.row_scale,
+                       w.qkv->m.bias, w.o->m.bias, w.post_norm,
+                       i + 1 < L.size() ? m->layers[i + 1].in_norm : m->final_norm,
+                       w.q_norm, w.k_norm, w.sinks,
+                       s->kc + i * s->layer_kv, s->vc + i * s->layer_kv, w.window};
+  }
+  if (char *e = alloc(&s->mk_layers, L.size(), "step layer table")) return e;
+  HC_TRY_CUDA(cudaMemcpy(s->mk_layers, L.data(), sizeof(hc::MkLayer) * L.size(), cudaMemcpyHostToDevice));
+  const int ktmax = std::max({probe.kt_d, probe.kt_f, probe.kt_o});
+  for (int b = 0; b < 2; ++b) {
+    if (char *e = alloc(&s->mk_act[b], size_t(kMaxChunk) * ktmax * hc::kActTile, "activation tiles")) return e;
+    HC_TRY_CUDA(cudaMemset(s->mk_act[b], 0, size_t(kMaxChunk) * ktmax * hc::kActTile));
+  }
+  if (char *e = alloc(&s->mk_sq, size_t(kMaxChunk) * (d.hidden / 32), "norm partials")) return e;
+  if (char *e = alloc(&s->mk_cnt, size_t(kMaxChunk) * d.kv_heads, "split counters")) return e;
+  HC_TRY_CUDA(cudaMemset(s->mk_cnt, 0, sizeof(unsigned) * kMaxChunk * d.kv_heads));
+  if (char *e = alloc(&s->mk_bar, 1, "grid barrier")) return e;
+  if (char *e = alloc(&s->mk_status, 1, "step status")) return e;
+  HC_TRY_CUDA(cudaMemset(s->mk_status, 0, sizeof(int)));
+  HC_TRY_CUDA(cudaHostAlloc(&s->mk_status_host, sizeof(int), cudaHostAllocDefault));
+  *s->mk_status_host = 0;
+  if (s->o.flags & HC_SESSION_PROFILE) {
+    const size_t n = (size_t(4) * hc::mk_phases(int(d.layers)) + 4) * s->mk_ctas + size_t(4) * hc::kMkChunkTrace +
+                     size_t(8) * d.layers;
+    if (char *e = alloc(&s->mk_trace, n, "phase trace")) return e;
+    HC_TRY_CUDA(cudaMemset(s->mk_trace, 0, n * sizeof(unsigned long long)));
+  }
+  s->mk = true;
   return nullptr;
 }
 
@@ -226,6 +364,8 @@ HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session
   HC_TRY_CUDA(cudaEventCreate(&s->ev1));
   s->pos.assign(o.max_seqs, 0);
   s->poisoned.assign(o.max_seqs, false);
+  HC_TRY_CUDA(cudaMemset(s->amax, 0, sizeof(unsigned long long) * T * hc::kAmaxSlots));
+  if (char *e = mk_setup(s.get())) return e;
   *out = s.release();
   return nullptr;
 }
@@ -243,7 +383,7 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
   for (int i = 0; i < nseq; ++i) {
     const int sq = seq_ids[i], n = n_tokens[i];
     if (sq < 0 || sq >= int(s->o.max_seqs)) return hc::make_error("hc_step: sequence " + std::to_string(sq) + " out of range");
-    if (n < 1 || n > int(s->o.max_step)) return hc::make_error("hc_step: " + std::to_string(n) + " tokens for one sequence (max_step " + std::to_string(s->o.max_step) + ")");
+    if (n < 1) return hc::make_error("hc_step: a sequence with no tokens");
     if (s->poisoned[sq]) return hc::make_error("hc_step: sequence " + std::to_string(sq) + " failed earlier; reset it");
     for (int j = 0; j < i; ++j)
       if (seq_ids[j] == sq) return hc::make_error("hc_step: sequence listed twice");
@@ -266,15 +406,17 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
   for (size_t c0 = 0; c0 < all.size(); c0 += kMaxChunk) {
     const int n = int(std::min<size_t>(kMaxChunk, all.size() - c0));
     std::memcpy(s->toks_host, &all[c0], sizeof(hc::StepTok) * n);
+    if (s->mk_status_host) *s->mk_status_host = 0;
     if (char *e = run_chunk(s, n, false)) {
       for (int i = 0; i < nseq; ++i) s->poisoned[seq_ids[i]] = true;
       return e;
     }
     int32_t st_ = HC_STATE_ERROR;
     char *e = wait_done(s, timeout_ms, &st_);
+    if (!e && st_ == HC_STATE_COMPLETED) e = mk_status_error(s);
     if (e || st_ != HC_STATE_COMPLETED) {
       for (int i = 0; i < nseq; ++i) s->poisoned[seq_ids[i]] = true;
-      if (state) *state = st_;
+      if (state) *state = e ? HC_STATE_ERROR : st_;
       return e;
     }
     for (; wi < want.size() && size_t(want[wi]) < c0 + n; ++wi, ++row) {
@@ -344,11 +486,20 @@ HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, i
   HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
   cudaStream_t st = s->st;
   s->toks_host[0] = hc::StepTok{first, seq, s->pos[seq], 0};
+  const bool mk = s->mk && hc::mk_supported(s->m->head->m.kind, 1, int(s->m->d.head_dim),
+                                             int(s->m->d.heads / s->m->d.kv_heads));
   if (!s->gen_graph) {
     cudaGraph_t graph = nullptr;
     HC_TRY_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    s->launches_per_chunk[0] = uint64_t(enqueue_chunk(s, 1, false)) + 1;
-    hc::advance(s->toks_dev, s->am_dev, s->gen_out, s->gen_count, st);
+    if (mk) {
+      // the status word is zeroed once before the loop: a failed launch makes the later ones return
+      cudaMemsetAsync(s->mk_bar, 0, sizeof(unsigned), st);
+      hc::mk_launch(mk_params(s, 1, true), s->mk_ctas, st);
+      s->launches_per_chunk[0] = 1;
+    } else {
+      s->launches_per_chunk[0] = uint64_t(enqueue_chunk(s, 1, false)) + 1;
+      hc::advance(s->toks_dev, s->am_dev, s->gen_out, s->gen_count, st);
+    }
     cudaError_t e = cudaStreamEndCapture(st, &graph);
     if (e != cudaSuccess) return hc::make_error(std::string("graph capture: ") + cudaGetErrorString(e));
     e = cudaGraphInstantiate(&s->gen_graph, graph, 0);
@@ -357,15 +508,21 @@ HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, i
   }
   HC_TRY_CUDA(cudaMemcpyAsync(s->toks_dev, s->toks_host, sizeof(hc::StepTok), cudaMemcpyHostToDevice, st));
   HC_TRY_CUDA(cudaMemsetAsync(s->gen_count, 0, sizeof(int32_t), st));
+  if (mk) HC_TRY_CUDA(cudaMemsetAsync(s->mk_status, 0, sizeof(int), st));
   HC_TRY_CUDA(cudaEventRecord(s->ev0, st));
   for (int i = 0; i < n; ++i) HC_TRY_CUDA(cudaGraphLaunch(s->gen_graph, st));
   HC_TRY_CUDA(cudaEventRecord(s->ev1, st));
+  if (mk) HC_TRY_CUDA(cudaMemcpyAsync(s->mk_status_host, s->mk_status, sizeof(int), cudaMemcpyDeviceToHost, st));
   s->stats.launches += uint64_t(n) * s->launches_per_chunk[0];
   int32_t st_ = HC_STATE_ERROR;
   char *e = wait_done(s, timeout_ms, &st_);
+  if (!e && st_ == HC_STATE_COMPLETED && mk) {
+    HC_TRY_CUDA(cudaStreamSynchronize(st));
+    e = mk_status_error(s);
+  }
   if (e || st_ != HC_STATE_COMPLETED) {
     s->poisoned[seq] = true;
-    if (state) *state = st_;
+    if (state) *state = e ? HC_STATE_ERROR : st_;
     return e;
   }
   HC_TRY_CUDA(cudaMemcpy(out_tokens, s->gen_out, sizeof(int32_t) * n, cudaMemcpyDeviceToHost));
@@ -447,6 +604,68 @@ HC_API char *hc_seq_import_rows(hc_session *s, int32_t seq, int32_t start, int32
   if (char *e = rows_copy(s, seq, start, n, const_cast<void *>(src), false)) return e;
   s->pos[seq] = start + n;
   s->poisoned[seq] = false;
+  return nullptr;
+}
+
+HC_API char *hc_profile_get(hc_session *s, double *us, uint32_t cap, uint32_t *n) {
+  if (!s || !n) return hc::make_error("hc_profile_get: NULL argument");
+  if (!s->mk_trace) return hc::make_error("hc_profile_get: the session was not opened with HC_SESSION_PROFILE and the persistent step");
+  const int P = hc::mk_phases(int(s->m->d.layers)), C = s->mk_ctas;
+  *n = uint32_t(P);
+  if (!us) return nullptr;
+  std::vector<unsigned long long> t((size_t(4) * P + 4) * C);
+  HC_TRY_CUDA(cudaStreamSynchronize(s->st));
+  HC_TRY_CUDA(cudaMemcpy(t.data(), s->mk_trace, t.size() * 8, cudaMemcpyDeviceToHost));
+  auto plane = [&](int k, int i, int c) { return t[(size_t(k) * P + i) * C + c]; };
+  unsigned long long prev = ~0ull;
+  for (int c = 0; c < C; ++c) prev = std::min(prev, plane(0, 0, c));
+  for (int i = 0; i < P && uint32_t(4 * i + 3) < cap; ++i) {
+    // the phase's marks (the slowest CTA of each): inputs ready, chunks consumed, arrival, release
+    unsigned long long m0 = 0, m1 = 0, arr = 0, rel = 0;
+    for (int c = 0; c < C; ++c) {
+      m0 = std::max(m0, plane(2, i, c));
+      m1 = std::max(m1, plane(3, i, c));
+      arr = std::max(arr, plane(0, i, c));
+      rel = std::max(rel, plane(1, i, c));
+    }
+    if (i == 0 || m0 < prev) m0 = prev;
+    if (m1 < m0) m1 = m0;
+    if (arr < m1) m1 = arr;
+    us[4 * i] = double(m0 - prev) / 1e3;      // activations into smem
+    us[4 * i + 1] = double(m1 - m0) / 1e3;    // chunks consumed
+    us[4 * i + 2] = double(arr - m1) / 1e3;   // epilogue to the last arrival
+    us[4 * i + 3] = double(rel - arr) / 1e3;  // the barrier
+    prev = rel;
+  }
+  // after the phases: the mean over CTAs of producer waited/busy and consumer (warp 0) waited/busy
+  // cycles of the step
+  if (cap >= uint32_t(4 * P + 4)) {
+    for (int k = 0; k < 4; ++k) {
+      double a = 0;
+      for (int c = 0; c < C; ++c) a += double(t[size_t(4) * P * C + size_t(c) * 4 + k]);
+      us[4 * P + k] = a / C;
+    }
+  }
+  // then CTA 0's ring chunks: [kMkChunkTrace][4] us since the step's first phase mark (0 = none)
+  if (cap >= uint32_t(4 * P + 4 + 4 * hc::kMkChunkTrace)) {
+    std::vector<unsigned long long> ct(size_t(4) * hc::kMkChunkTrace);
+    HC_TRY_CUDA(cudaMemcpy(ct.data(), s->mk_trace + t.size(), ct.size() * 8, cudaMemcpyDeviceToHost));
+    unsigned long long t0 = ~0ull;
+    for (int c = 0; c < C; ++c) t0 = std::min(t0, plane(0, 0, c));
+    for (size_t k = 0; k < ct.size(); ++k)
+      us[4 * P + 4 + k] = ct[k] ? (double(ct[k]) - double(t0)) / 1e3 : 0.0;
+  }
+  // then CTA 1's attention unit: [layers][8] clock cycles since the layer's event 0
+  const int Ly = int(s->m->d.layers);
+  if (cap >= uint32_t(4 * P + 4 + 4 * hc::kMkChunkTrace + 8 * Ly)) {
+    std::vector<unsigned long long> ut(size_t(8) * Ly);
+    HC_TRY_CUDA(cudaMemcpy(ut.data(), s->mk_trace + t.size() + size_t(4) * hc::kMkChunkTrace, ut.size() * 8,
+                           cudaMemcpyDeviceToHost));
+    for (int l = 0; l < Ly; ++l)
+      for (int k = 0; k < 8; ++k)
+        us[4 * P + 4 + 4 * hc::kMkChunkTrace + 8 * l + k] =
+            ut[8 * l + k] ? double(ut[8 * l + k]) - double(ut[8 * l]) : -1.0;
+  }
   return nullptr;
 }
 

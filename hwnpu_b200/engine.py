@@ -95,8 +95,11 @@ class LoadedModel:
     def weight_bytes(self):
         return A.lib().hc_model_weight_bytes(self.h)
 
-    def session(self, max_context, max_seqs=1, max_step=8, kv_format=A.HC_KV_F16, page_size=16, graphs=True):
-        return Session(self, max_context, max_seqs, max_step, kv_format, page_size, graphs)
+    def session(self, max_context, max_seqs=1, max_step=8, kv_format=A.HC_KV_F16, page_size=16, graphs=True,
+                megakernel=True, profile=False):
+        flags = (0 if graphs else A.HC_SESSION_NO_GRAPH) | (0 if megakernel else A.HC_SESSION_NO_MEGAKERNEL) | \
+                (A.HC_SESSION_PROFILE if profile else 0)
+        return Session(self, max_context, max_seqs, max_step, kv_format, page_size, flags)
 
     def close(self):
         if self.h:
@@ -115,10 +118,10 @@ def _u16(a):
 class Session:
     """decode.Session / chat.tokenSession over a device-resident KV cache of max_seqs slots."""
 
-    def __init__(self, lm, max_context, max_seqs, max_step, kv_format, page_size, graphs):
+    def __init__(self, lm, max_context, max_seqs, max_step, kv_format, page_size, flags):
         self.lm = lm
         self.vocab = lm.model.cfg.vocab
-        o = A.SessionOpts(max_context, max_seqs, max_step, kv_format, page_size, 0 if graphs else A.HC_SESSION_NO_GRAPH)
+        o = A.SessionOpts(max_context, max_seqs, max_step, kv_format, page_size, flags)
         h = C.c_void_p()
         A.check(A.lib().hc_session_new(lm.h, C.byref(o), C.byref(h)))
         self.h, self.max_context, self.max_seqs, self.max_step = h, max_context, max_seqs, max_step
@@ -200,6 +203,22 @@ class Session:
     def import_rows(self, start, n, rows, seq=0):
         rows = np.ascontiguousarray(rows, np.uint8)
         A.check(A.lib().hc_seq_import_rows(self.h, seq, start, n, rows.ctypes.data_as(C.c_void_p), rows.nbytes))
+
+    def profile(self):
+        """Per-phase (inputs, weights, epilogue, barrier) microseconds of the last persistent step
+        (hc_profile_get)."""
+        n = C.c_uint32()
+        A.check(A.lib().hc_profile_get(self.h, None, 0, C.byref(n)))
+        P = n.value
+        L = self.lm.model.cfg.layers
+        out = np.zeros(4 * P + 4 + 4 * A.MK_CHUNK_TRACE + 8 * L, np.float64)
+        A.check(A.lib().hc_profile_get(self.h, out.ctypes.data_as(C.POINTER(C.c_double)), out.size, C.byref(n)))
+        self.last_cycles = out[4 * P:4 * P + 4].copy()  # producer waited/busy, consumer waited/busy
+        # CTA 0's ring chunks: us of producer issue, warp 0 saw full, warp 0 done, warp 7 done
+        self.last_chunks = out[4 * P + 4:4 * P + 4 + 4 * A.MK_CHUNK_TRACE].reshape(A.MK_CHUNK_TRACE, 4)
+        # CTA 1's attention unit per layer: cycles of its 8 events since the first
+        self.last_unit = out[4 * P + 4 + 4 * A.MK_CHUNK_TRACE:].reshape(-1, 8) if L else None
+        return out[:4 * P].reshape(P, 4)
 
     def stats(self):
         s = A.Stats()

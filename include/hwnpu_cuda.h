@@ -212,13 +212,17 @@ enum {
   HC_KV_INT8_PAGED = 1, /* int8 in pages of page_size positions, one fp16 scale a (head, page) */
 };
 enum {
-  HC_SESSION_NO_GRAPH = 1 << 0, /* launch the step's kernels one by one (no CUDA graph) */
+  HC_SESSION_NO_GRAPH = 1 << 0,      /* launch the step's kernels one by one (no CUDA graph) */
+  HC_SESSION_NO_MEGAKERNEL = 1 << 1, /* run decode steps as one kernel per operation, not as the
+                                      * persistent one-launch step */
+  HC_SESSION_PROFILE = 1 << 2,       /* time the phases of the persistent step (hc_profile_get) */
 };
 
 typedef struct hc_session_opts {
   uint32_t max_context;  /* positions a sequence may hold (Session.Cache) */
   uint32_t max_seqs;     /* sequence slots */
-  uint32_t max_step;     /* most tokens a sequence reads in one call (Session.Q) */
+  uint32_t max_step;     /* most tokens hc_speculate verifies in one call (1..8); hc_step reads
+                          * any number, in passes of up to 8 tokens over the weights */
   uint32_t kv_format;    /* HC_KV_* */
   uint32_t page_size;    /* positions a page (HC_KV_INT8_PAGED), 16 */
   uint32_t flags;        /* HC_SESSION_* */
@@ -290,6 +294,16 @@ typedef struct hc_stats {
 } hc_stats;
 
 HC_API char *hc_stats_get(hc_session *s, hc_stats *out);
+
+/* Per-phase timing of the last persistent step of a session opened with HC_SESSION_PROFILE (the
+ * role of decode/profile.go:13-40, per-part times of a step), from the slowest CTA of each mark:
+ * for phase i, us[4 i .. 4 i + 3] are the microseconds from the previous barrier's release to the
+ * phase's inputs in shared memory, to its weights consumed, to the last CTA's arrival at the next
+ * barrier, and to that barrier's release. Phases: embed, then 5 a layer (qkv, attention, o,
+ * gate/up, down), head; *n gets their number. With cap >= 4 n + 4, us[4 n .. 4 n + 3] are the
+ * step's mean SM cycles the stage producer waited for free stages, ran in all, and that the
+ * consumers waited for full stages, ran in all. */
+HC_API char *hc_profile_get(hc_session *s, double *us, uint32_t cap, uint32_t *n);
 
 /* Host-side fault injection for tests (the reference fakes its drivers instead, testdata/zemock):
  * "alloc:N" fails the N-th device allocation from now, "h2d:N" the N-th host-to-device copy,

@@ -78,6 +78,52 @@ def test_decode_matches_oracle(device, models, cfg, prompt, steps):
     ref.close()
 
 
+@pytest.mark.parametrize("cfg", [TINY, C1, C2_2L], ids=lambda c: c.name)
+def test_megakernel_matches_kernel_path(device, models, cfg):
+    # the persistent one-launch step and the one-kernel-per-operation step read the same logits
+    # (within their float32 summation orders) and make the same greedy choices
+    model = get(models, cfg)
+    lm = device.load_model(model)
+    a = lm.session(max_context=48, megakernel=True)
+    b = lm.session(max_context=48, megakernel=False)
+    toks = list(synth.tokens(31, cfg.vocab, 20))
+    la, lb = a.step_tokens(toks), b.step_tokens(toks)
+    t = int(np.argmax(lb))
+    for _ in range(6):
+        la, lb = a.step_tokens([t]), b.step_tokens([t])
+        assert np.abs(la - lb).max() <= 5e-3, np.abs(la - lb).max()
+        if top2_margin(lb) > 1e-2:
+            assert int(np.argmax(la)) == int(np.argmax(lb))
+        t = int(np.argmax(lb))
+    ga = a.generate(t, 12)
+    gb = b.generate(t, 12)
+    assert (ga == gb).mean() >= 0.9
+    a.close()
+    b.close()
+    lm.close()
+
+
+def test_megakernel_batch_of_four(device, models):
+    # four sequences reading one token each (one persistent step of 4 tokens) against each alone
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    batch = lm.session(max_context=40, max_seqs=4)
+    alone = [lm.session(max_context=40) for _ in range(4)]
+    prompts = [list(synth.tokens(50 + i, TINY.vocab, 5 + i)) for i in range(4)]
+    for i in range(4):
+        batch.step_batch([i], [prompts[i]])
+        alone[i].step_batch([0], [prompts[i]])
+    nxt = [7, 70, 700, 900]
+    lb, ab = batch.step_batch([0, 1, 2, 3], [[t] for t in nxt])
+    for i in range(4):
+        la, aa = alone[i].step_batch([0], [[nxt[i]]])
+        assert np.abs(synth.f16_values(lb[i]) - synth.f16_values(la[0])).max() <= 2e-3
+    for s in alone:
+        s.close()
+    batch.close()
+    lm.close()
+
+
 def test_all_rows_and_chunking(device, models):
     # 11 tokens in one call cross the 8-token chunks; every row against the oracle's
     model = get(models, TINY)
@@ -150,7 +196,7 @@ def test_ragged_batch_equals_single_sequences(device, models):
     for i in range(3):
         la, aa = alone[i].step_batch([0], [prompts[i]])
         assert ab[i] == aa[0]
-        assert np.abs(synth.f16_values(lb[i]) - synth.f16_values(la[0])).max() <= 1e-3
+        assert np.abs(synth.f16_values(lb[i]) - synth.f16_values(la[0])).max() <= 5e-3
     for s in alone:
         s.close()
     batch.close()
@@ -211,8 +257,8 @@ def test_injected_faults_leave_the_session_usable(device, models):
     A.check(A.lib().hc_set_fault(b"alloc:1"))
     with pytest.raises(hb.HcError, match="injected"):
         lm.session(max_context=32)
-    with pytest.raises(hb.HcError, match="max_step"):
-        s.step_tokens(list(range(8)) * 4)
+    with pytest.raises(hb.HcError, match="tokens"):
+        s.speculate_tokens(list(range(9)))
     with pytest.raises(hb.HcError, match="max_context"):
         s.generate(1, 40)
     with pytest.raises(hb.HcError, match="vocabulary"):
