@@ -119,6 +119,9 @@ SIGNATURES = {
     "hc_attention_run": (_err, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                 C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                 C.c_int32, _f32p, C.c_void_p]),
+    "hc_attention_run_static": (_err, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                       C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                       C.c_int32, _f32p, C.c_void_p]),
     "hc_argmax_run": (_err, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
     "hc_route_run": (_err, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                             C.c_void_p]),

@@ -372,6 +372,25 @@ HC_API char *hc_attention_run(const float *q, const uint16_t *kcache, const uint
                               int32_t kv_heads, int32_t head_dim, int32_t pos, int32_t cap,
                               int32_t window, const float *scale, void *stream);
 
+/* hc_attention_run with the same arguments, results and kernels, but it allocates nothing: no
+ * cudaMalloc, no cudaFree, no host-to-device copy. It has no counterpart in the reference (whose
+ * CPU attention needs no device scratch); it is for callers that may not allocate device memory
+ * per call, such as a serving loop whose device memory is all handed out up front, where a
+ * cudaMalloc can fail and a cudaFree stalls every stream of the device until the GPU is idle.
+ * Its scratch (step tokens, per-split partials, activation tiles) is one static device array of
+ * 8 MiB per device, shared by every call of the process and left holding the last call's
+ * contents; nothing in it needs to start at zero, since each call writes all it reads. A call
+ * whose scratch (ntok * heads * (16 * 4 * (head_dim + 2)) bytes plus tokens and activation
+ * tiles) exceeds 8 MiB is rejected with an error. The work is enqueued on stream and not waited
+ * for: errors of the launches are returned, errors of the execution show on the stream. Calls
+ * that overlap in time on one device (other streams or threads) share the scratch and race: run
+ * them on one stream. The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress, with that device current); make it before any stream capture. */
+HC_API char *hc_attention_run_static(const float *q, const uint16_t *kcache, const uint16_t *vcache,
+                                     const float *sinks, float *o, int32_t ntok, int32_t heads,
+                                     int32_t kv_heads, int32_t head_dim, int32_t pos, int32_t cap,
+                                     int32_t window, const float *scale, void *stream);
+
 /* Greedy choice over rows of fp16 logits (chat/sample.go:80-88: the first largest wins):
  * logits [rows][vocab] fp16 bits, out int32 [rows], device memory. */
 HC_API char *hc_argmax_run(const uint16_t *logits, int32_t rows, int32_t vocab, int32_t *out,
