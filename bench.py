@@ -147,6 +147,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chunk-trace", default=None,
                     help="with --phases: save CTA 0's per-chunk ring events of the last step (.npy)")
+    ap.add_argument("--mk", action="store_true",
+                    help="run the step as the persistent one-launch kernel (experimental) instead of the kernel sequence")
     ap.add_argument("--phases", action="store_true",
                     help="print the persistent step's per-phase timing (hc_profile_get) after a few steps and exit")
     ap.add_argument("--profile", type=int, default=0,
@@ -179,7 +181,8 @@ def main():
     model = build_model(args.workload)
     dev = hb.Device(local)
     lm = dev.load_model(model)
-    sess = lm.session(max_context=PROMPT + PASS + W + 8, max_step=8, profile=args.phases)
+    sess = lm.session(max_context=PROMPT + PASS + W + 8, max_step=8, profile=args.phases,
+                      megakernel=args.mk or args.phases)
     prompt = synth.tokens(1, model.cfg.vocab, PROMPT)
     first = sess.greedy(prompt)
     base = sess.pos()
@@ -200,9 +203,9 @@ def main():
             np.save(args.chunk_trace.replace(".npy", "_unit.npy"), sess.last_unit)
         L = model.cfg.layers
         names = ["qkv", "attention", "o", "gate/up", "down"]
-        per = {n: [round(float(x), 3) for x in acc[1 + i:1 + 5 * L:5].mean(axis=0)] for i, n in enumerate(names)}
-        print(json.dumps({"phase_us_per_layer_inputs_weights_epilogue_barrier": per, "embed": acc[0].tolist(),
-                          "head": acc[1 + 5 * L].tolist(), "total_us": float(acc.sum()),
+        per = {n: [round(float(x), 3) for x in acc[i:5 * L:5].mean(axis=0)] for i, n in enumerate(names)}
+        print(json.dumps({"phase_us_per_layer_inputs_weights_epilogue_barrier": per,
+                          "head": acc[5 * L].tolist(), "total_us": float(acc.sum()),
                           "cycles_producer_waited_busy_consumer_waited_busy": [float(x) for x in cyc]}), flush=True)
         return
     if args.profile:

@@ -9,8 +9,8 @@
 
 namespace hc {
 
-// mma.sync m16n8k32 with int32 accumulation: A (16x32, row) signed bytes, B (32x8, col)
-// unsigned (int4 codes 0..15) or signed (int8 codes, doubled e2m1 values) bytes.
+// mma.sync m16n8k32 with int32 accumulation: A (16x32, row), B (32x8, col), signed or unsigned
+// bytes as the name says (A first).
 __device__ __forceinline__ void mma_s8u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -24,6 +24,16 @@ __device__ __forceinline__ void mma_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// A (weights) unsigned bytes: int4 codes 0..15, or 16x them (see common.h).
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -74,27 +84,149 @@ __device__ __forceinline__ int warp_sum_i(int v) {
   return v;
 }
 
-// The float32 value of (row, col) of a repacked matrix, as dequant_kernel computes it.
+// The float32 value of (row, col) of a repacked matrix, with the format's own arithmetic: int8
+// q * s (palette Linear.Dequantize), int4 (float(q) - z) * s (milcpu shiftScale), e2m1 *
+// 2^(e-127) (mxfp4.Dequantize).
 __device__ __forceinline__ float tile_value(const uint8_t *tiles, const float *row_scale, int kind, int ktiles,
-                            int tile_bytes, int r, int col) {
-  const int rt = r / 8, g = r % 8, kt = col / kTileCols, cc = col % kTileCols;
-  const int grp = cc / 32, e = cc % 32, i4 = e / 4, p = e % 4;
-  const int c = grp & 3, hi = grp >> 2, lane = g * 4 + c, sl = grp * 4 + g / 2;
+                                            int tile_bytes, int r, int col) {
+  const int rt = r / kTileRows, kt = col / kTileCols;
+  const TilePos tp = tile_pos(kind != kKindInt8, kind == kKindMx, r % kTileRows, col % kTileCols);
   const uint8_t *tile = tiles + (size_t(rt) * ktiles + kt) * tile_bytes;
-  if (kind == kKindInt8) return float(int8_t(tile[lane * 64 + i4 * 8 + hi * 4 + p])) * row_scale[r];
+  if (kind == kKindInt8) return float(int8_t(tile[tp.byte])) * row_scale[r];
+  const int code = (tile[tp.byte] >> tp.shift) & 15;
   if (kind == kKindInt4) {
-    const uint8_t by = tile[lane * 32 + i4 * 4 + p];
-    const int q = hi ? (by >> 4) : (by & 15);
-    const uint16_t *sz = reinterpret_cast<const uint16_t *>(tile + kTileCodes4 + sl * 8);
-    const float s = __half2float(__ushort_as_half(sz[g & 1]));
-    const float z = __half2float(__ushort_as_half(sz[2 + (g & 1)]));
-    return __fmul_rn(__fsub_rn(float(q), z), s);
+    const uint16_t *sz = reinterpret_cast<const uint16_t *>(tile + kTileCodes4 + tp.lane * 16);
+    const float s = __half2float(__ushort_as_half(sz[tp.sidx]));
+    const float z = __half2float(__ushort_as_half(sz[4 + tp.sidx]));
+    return __fmul_rn(__fsub_rn(float(code), z), s);
   }
-  const uint8_t by = tile[lane * 32 + i4 * 4 + hi * 2 + p / 2];
-  const int code = (p & 1) ? (by >> 4) : (by & 15);
   const float mag[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
   const float val = (code & 8) ? -mag[code & 7] : mag[code & 7];
-  return __fmul_rn(val, __uint_as_float(uint32_t(tile[kTileCodes4 + sl * 2 + (g & 1)]) << 23));
+  return __fmul_rn(val, __uint_as_float(uint32_t(tile[kTileCodes4 + tp.lane * 4 + tp.sidx]) << 23));
+}
+
+// ---- one column tile of a GEMV (common.h's tile layout) -------------------------------------
+// The weight operand of one tile for one lane: the code words (int8: 8 MMAs x 4 registers; int4 /
+// mxfp4: 4 words, each two MMAs' registers) and the scale data of rows g, g+8 x groups c, 4+c.
+template <int KIND>
+struct WTile {
+  static constexpr int NW = KIND == kKindInt8 ? 32 : 16;
+  uint32_t w[NW];
+  uint32_t sd[4];  // int4: s,s,s,s,z,z,z,z as fp16 pairs; mxfp4: 4 exponent bytes in sd[0]
+  __device__ __forceinline__ void load(const uint8_t *tile, int lane) {
+    const uint4 *q = reinterpret_cast<const uint4 *>(tile) + lane;
+#pragma unroll
+    for (int i = 0; i < NW / 4; ++i) {
+      const uint4 v = q[32 * i];
+      w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+    }
+    if (KIND == kKindInt4) {
+      const uint4 v = *reinterpret_cast<const uint4 *>(tile + kTileCodes4 + lane * 16);
+      sd[0] = v.x; sd[1] = v.y; sd[2] = v.z; sd[3] = v.w;
+    } else if (KIND == kKindMx) {
+      sd[0] = *reinterpret_cast<const uint32_t *>(tile + kTileCodes4 + lane * 4);
+      sd[1] = sd[2] = sd[3] = 0u;
+    }
+  }
+};
+
+// The activation operand of one tile for one token and lane (g, c): B registers of the 8 MMAs
+// (lane (g, c) with g / 2 == c carries group 4h + c's hi (g even) or lo (g odd) bytes, the others
+// zeros; mxfp4 reads hi only, as mxfp4.Vec.Quantize has no residual), and the scale S and sum Xq
+// of the lane's groups c (h = 0) and 4 + c (h = 1). For int4 the h = 1 group carries S / 16 and
+// 16 Xq, undoing the 16x codes exactly (powers of two).
+template <int KIND>
+struct BFrag {
+  uint32_t b[8][2];
+  float S[2], Xq[2];
+  __device__ __forceinline__ void load(const uint8_t *at, int lane) {
+    const int g = lane >> 2, c = lane & 3;
+    const bool on = (g >> 1) == c && !(KIND == kKindMx && (g & 1));
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int G = 4 * h + c;
+      uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
+      if (on) {
+        const uint4 *ap = reinterpret_cast<const uint4 *>(at + G * 64 + (g & 1) * 32);
+        q0 = ap[0];
+        q1 = ap[1];
+      }
+      b[4 * h + 0][0] = q0.x; b[4 * h + 0][1] = q0.y;
+      b[4 * h + 1][0] = q0.z; b[4 * h + 1][1] = q0.w;
+      b[4 * h + 2][0] = q1.x; b[4 * h + 2][1] = q1.y;
+      b[4 * h + 3][0] = q1.z; b[4 * h + 3][1] = q1.w;
+      const float2 sx = *reinterpret_cast<const float2 *>(at + kGroupsPerTile * 64 + G * 8);
+      S[h] = sx.x;
+      Xq[h] = sx.y;
+      if (KIND == kKindInt4 && h == 1) {
+        S[h] *= 0.0625f;
+        Xq[h] *= 16.0f;
+      }
+    }
+  }
+  // an inactive tile: zero operands and scales, so every product is an exact zero
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) b[u][0] = b[u][1] = 0u;
+    S[0] = S[1] = Xq[0] = Xq[1] = 0.f;
+  }
+};
+
+// The 8 MMAs of one tile and their group scaling: adds to vg / vg8 this lane's values of rows g and
+// g + 8 over its groups c and 4 + c (int8: before the row scale; mxfp4: doubled, before the 1/2).
+template <int KIND>
+__device__ __forceinline__ void wa_mma(const WTile<KIND> &wt, const BFrag<KIND> &bf, float &vg, float &vg8) {
+  int D[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll
+  for (int o = 0; o < 4; ++o) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int u = 4 * h + o;
+      uint32_t a[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (KIND == kKindInt8) {
+          a[j] = wt.w[4 * u + j];
+        } else if (KIND == kKindInt4) {
+          a[j] = h ? (wt.w[4 * o + j] & 0xF0F0F0F0u) : (wt.w[4 * o + j] & 0x0F0F0F0Fu);
+        } else {
+          const uint32_t x = wt.w[4 * o + j], xs = x << 4;
+          a[j] = h ? e2m1x4(x, xs, 0xFBEAu, (x >> 16) & 0x7777u) : e2m1x4(x, xs, 0xD9C8u, x & 0x7777u);
+        }
+      }
+      if (KIND == kKindInt4) mma_u8s8(D[h], a[0], a[1], a[2], a[3], bf.b[u][0], bf.b[u][1]);
+      else mma_s8s8(D[h], a[0], a[1], a[2], a[3], bf.b[u][0], bf.b[u][1]);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (KIND == kKindMx) {
+      const uint32_t e4 = wt.sd[0];
+      const float sg = __uint_as_float(((e4 >> (16 * h)) & 0xffu) << 23);
+      const float sg8 = __uint_as_float(((e4 >> (16 * h + 8)) & 0xffu) << 23);
+      vg = fmaf(float(D[h][0]) * sg, bf.S[h], vg);
+      vg8 = fmaf(float(D[h][2]) * sg8, bf.S[h], vg8);
+    } else {
+      const float pg = fmaf(float(D[h][1]), 1.0f / 256.0f, float(D[h][0]));
+      const float pg8 = fmaf(float(D[h][3]), 1.0f / 256.0f, float(D[h][2]));
+      if (KIND == kKindInt4) {
+        const __half2 s2 = *reinterpret_cast<const __half2 *>(&wt.sd[h]);
+        const __half2 z2 = *reinterpret_cast<const __half2 *>(&wt.sd[2 + h]);
+        vg = fmaf(__low2float(s2) * bf.S[h], fmaf(-__low2float(z2), bf.Xq[h], pg), vg);
+        vg8 = fmaf(__high2float(s2) * bf.S[h], fmaf(-__high2float(z2), bf.Xq[h], pg8), vg8);
+      } else {
+        vg = fmaf(bf.S[h], pg, vg);
+        vg8 = fmaf(bf.S[h], pg8, vg8);
+      }
+    }
+  }
+}
+
+// Sums a lane value over the 4 lanes of one g (the groups c = 0..3): lane 4g ends with rows g, g+8.
+__device__ __forceinline__ float quad_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  return v;
 }
 
 }  // namespace hc

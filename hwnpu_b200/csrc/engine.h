@@ -83,9 +83,7 @@ struct hc_session {
   bool mk = false;
   int mk_ctas = 0;
   hc::MkLayer *mk_layers = nullptr;  // device [layers]
-  uint8_t *mk_act[2] = {nullptr, nullptr};
-  double *mk_sq = nullptr;
-  unsigned *mk_cnt = nullptr, *mk_bar = nullptr;
+  unsigned *mk_bar = nullptr;
   int *mk_status = nullptr, *mk_status_host = nullptr;
   unsigned long long *mk_trace = nullptr;  // HC_SESSION_PROFILE
   // captured step graphs by (tokens, accept kernel)

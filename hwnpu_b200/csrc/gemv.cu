@@ -1,12 +1,12 @@
 // gemv.cu: the decode GEMV over repacked integer tiles, and the activation quantiser it reads.
 //
-// One CTA (8 warps) owns 8 / wpr row tiles; the wpr warps of a row tile split its column tiles.
-// Per column tile a warp issues 8 integer MMAs (m16n8k32): B is the tile's 8 rows (codes straight
-// from HBM, unpacked in registers), A carries the activation of the 8 groups of 32 columns on
-// its 8 rows ("hi" bytes) and 8 more rows ("lo" bytes, the residual at 1/256), so that every
-// A row holds one group: after the 8 MMAs lane (g, c) holds group g's exact integer dot products
-// for output rows 2c and 2c+1, which it scales by the group's weight scale (and zero point) and
-// by the activation's group scale in float32.
+// One CTA (8 warps) owns 8 / wpr row tiles of 16 rows; the wpr warps of a row tile split its column
+// tiles. Per column tile a warp issues 8 integer MMAs (m16n8k32) whose A operand is the tile's codes
+// (unpacked in registers from HBM) and whose B operand is the activation: the hi bytes and the lo
+// bytes (the residual at 1/256) of one group on two of B's columns, so that each MMA adds, for 16
+// rows, the exact integer dot products of 8 columns of 4 groups at once (common.h). Lane (g, c)
+// then scales its rows g, g+8 by the weight scale (and zero point) and the activation's scale of
+// its groups c and 4 + c in float32; 2 shuffles add the 4 lanes of a row.
 #include "device.cuh"
 #include "kernels.h"
 
@@ -20,139 +20,63 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint8_t *__restrict__ t
                                                    const uint8_t *__restrict__ act, int rtiles,
                                                    int ktiles, int rows, int wpr, GemvOut out) {
   constexpr int TB = KIND == kKindInt8 ? kTileInt8 : (KIND == kKindInt4 ? kTileInt4 : kTileMx);
-  __shared__ float part[8][NT][8];
+  __shared__ float part[8][NT][kTileRows];
   __shared__ unsigned long long bmax[NT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int rpc = 8 / wpr;
   const int lrt = warp / wpr, ks = warp % wpr;
   const int rt = blockIdx.x * rpc + lrt;
-  const bool role0 = g == c, role1 = g == c + 4;
-  const int agrp = role0 ? c : g;  // the group whose activation bytes this lane puts in A
   if (threadIdx.x < NT) bmax[threadIdx.x] = 0ull;
-  float acc[NT][2];
+  float vg[NT], vg8[NT];
 #pragma unroll
-  for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = 0.f;
-
+  for (int t = 0; t < NT; ++t) vg[t] = vg8[t] = 0.f;
   if (rt < rtiles) {
     for (int kt = ks; kt < ktiles; kt += wpr) {
-      const uint8_t *tile = tiles + (size_t(rt) * ktiles + kt) * TB;
-      uint32_t b0[8], b1[8];
-      float s0 = 0.f, s1 = 0.f, z0 = 0.f, z1 = 0.f;
-      if (KIND == kKindInt8) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(tile + lane * 64);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 v = __ldg(p + q);
-          b0[2 * q] = v.x; b1[2 * q] = v.y; b0[2 * q + 1] = v.z; b1[2 * q + 1] = v.w;
-        }
-      } else {
-        const uint4 *p = reinterpret_cast<const uint4 *>(tile + lane * 32);
-        uint4 v0 = __ldg(p), v1 = __ldg(p + 1);
-        uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        if (KIND == kKindInt4) {
-          const uint2 sz = __ldg(reinterpret_cast<const uint2 *>(tile + kTileCodes4 + lane * 8));
-          const __half2 sh = *reinterpret_cast<const __half2 *>(&sz.x);
-          const __half2 zh = *reinterpret_cast<const __half2 *>(&sz.y);
-          s0 = __low2float(sh); s1 = __high2float(sh);
-          z0 = __low2float(zh); z1 = __high2float(zh);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) { b0[i] = w[i] & 0x0F0F0F0Fu; b1[i] = (w[i] >> 4) & 0x0F0F0F0Fu; }
-        } else {
-          const uint16_t e2 = __ldg(reinterpret_cast<const unsigned short *>(tile + kTileCodes4 + lane * 2));
-          s0 = __uint_as_float(uint32_t(e2 & 0xff) << 23);  // 2^(e-127)
-          s1 = __uint_as_float(uint32_t(e2 >> 8) << 23);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint32_t wsh = w[i] << 4;
-            b0[i] = e2m1x4(w[i], wsh, 0xD9C8u, w[i] & 0x7777u);
-            b1[i] = e2m1x4(w[i], wsh, 0xFBEAu, (w[i] >> 16) & 0x7777u);
-          }
-        }
-      }
+      WTile<KIND> wt;
+      wt.load(tiles + (size_t(rt) * ktiles + kt) * TB, lane);
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
-        const uint8_t *at = act + (size_t(t) * ktiles + kt) * kActTile;
-        uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0, l0 = h0, l1 = h0;
-        if (role0 || role1) {
-          const uint4 *ap = reinterpret_cast<const uint4 *>(at + agrp * 64);
-          h0 = ap[0]; h1 = ap[1];
-          if (KIND != kKindMx) { l0 = ap[2]; l1 = ap[3]; }
-        }
-        const float2 sx = *reinterpret_cast<const float2 *>(at + kGroupsPerTile * 64 + g * 8);
-        const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-        const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-        int d[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint32_t a0 = role0 ? hw[i] : 0u, a1 = role0 ? lw[i] : 0u;
-          const uint32_t a2 = role1 ? hw[i] : 0u, a3 = role1 ? lw[i] : 0u;
-          if (KIND == kKindInt4) mma_s8u8(d, a0, a1, a2, a3, b0[i], b1[i]);
-          else mma_s8s8(d, a0, a1, a2, a3, b0[i], b1[i]);
-        }
-        // d[0], d[1]: group g's dot with rows 2c, 2c+1 on the hi bytes; d[2], d[3]: on the lo
-        const float S = sx.x, Xq = sx.y;
-        if (KIND == kKindMx) {
-          acc[t][0] = fmaf(float(d[0]) * s0, S, acc[t][0]);
-          acc[t][1] = fmaf(float(d[1]) * s1, S, acc[t][1]);
-        } else {
-          const float p0 = fmaf(float(d[2]), 1.0f / 256.0f, float(d[0]));
-          const float p1 = fmaf(float(d[3]), 1.0f / 256.0f, float(d[1]));
-          if (KIND == kKindInt4) {
-            acc[t][0] = fmaf(s0 * S, fmaf(-z0, Xq, p0), acc[t][0]);
-            acc[t][1] = fmaf(s1 * S, fmaf(-z1, Xq, p1), acc[t][1]);
-          } else {
-            acc[t][0] = fmaf(S, p0, acc[t][0]);
-            acc[t][1] = fmaf(S, p1, acc[t][1]);
-          }
-        }
+        BFrag<KIND> bf;
+        bf.load(act + (size_t(t) * ktiles + kt) * kActTile, lane);
+        wa_mma<KIND>(wt, bf, vg[t], vg8[t]);
       }
     }
   }
-  // sum the 8 groups (lanes g = 0..7 of the same c)
 #pragma unroll
-  for (int t = 0; t < NT; ++t)
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      float v = acc[t][j];
-      v += __shfl_xor_sync(0xffffffffu, v, 4);
-      v += __shfl_xor_sync(0xffffffffu, v, 8);
-      v += __shfl_xor_sync(0xffffffffu, v, 16);
-      acc[t][j] = v;
-    }
-  if (g == 0) {
-#pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      part[warp][t][2 * c] = acc[t][0];
-      part[warp][t][2 * c + 1] = acc[t][1];
+  for (int t = 0; t < NT; ++t) {
+    const float a = quad_sum(vg[t]), b = quad_sum(vg8[t]);
+    if (c == 0) {
+      part[warp][t][g] = a;
+      part[warp][t][g + 8] = b;
     }
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < rpc * NT * 8; idx += blockDim.x) {
-    const int l2 = idx / (NT * 8), t = (idx / 8) % NT, r8 = idx % 8;
+  for (int idx = threadIdx.x; idx < rpc * NT * kTileRows; idx += blockDim.x) {
+    const int l2 = idx / (NT * kTileRows), t = (idx / kTileRows) % NT, r16 = idx % kTileRows;
     const int tile_r = blockIdx.x * rpc + l2;
     if (tile_r >= rtiles) continue;
     auto value = [&](int rr) {
       float v = 0.f;
       for (int k = 0; k < wpr; ++k) v += part[l2 * wpr + k][t][rr];
-      const int row = tile_r * 8 + rr;
+      const int row = tile_r * kTileRows + rr;
       if (KIND == kKindInt8) v *= row_scale[row];
       if (KIND == kKindMx) v *= 0.5f;  // the doubled e2m1 values (mxfp4.go:90)
       if (bias) v += bias[row];
       return v;
     };
     if (out.mode == kGlu) {
-      if (r8 >= 4) continue;
-      const int o = tile_r * 4 + r8;
+      if (r16 >= kTileRows / 2) continue;
+      const int o = tile_r * (kTileRows / 2) + r16;
       if (o >= rows) continue;
-      const float gv = value(r8), uv = value(r8 + 4);
+      const float gv = value(r16), uv = value(r16 + kTileRows / 2);
       // blocks.SiLU: x / (1 + exp(-x)) (internal/llm/blocks/blocks.go:395-399)
       out.y[size_t(t) * out.ldy + o] = gv / (1.0f + expf(-gv)) * uv;
       continue;
     }
-    const int row = tile_r * 8 + r8;
+    const int row = tile_r * kTileRows + r16;
     if (row >= rows) continue;
-    const float v = value(r8);
+    const float v = value(r16);
     if (out.mode == kStore) {
       out.y[size_t(t) * out.ldy + row] = v;
     } else if (out.mode == kAdd) {
@@ -311,46 +235,14 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict
   }
 }
 
-// Values of repacked rows with the format's own arithmetic: int8 q * s
-// (palette Linear.Dequantize), int4 (float(q) - z) * s (milcpu shiftScale), e2m1 * 2^(e-127)
-// (mxfp4.Dequantize).
+// Values of repacked rows with the format's own arithmetic (tile_value).
 __global__ void dequant_kernel(const uint8_t *__restrict__ tiles, const float *__restrict__ row_scale,
                                int kind, int ktiles, int tile_bytes, int cols, int row0, int nrows,
                                float *__restrict__ out) {
   const long total = long(nrows) * cols;
   for (long i = blockIdx.x * long(blockDim.x) + threadIdx.x; i < total; i += long(gridDim.x) * blockDim.x) {
     const int r = row0 + int(i / cols), col = int(i % cols);
-    const int rt = r / 8, g = r % 8, kt = col / kTileCols, cc = col % kTileCols;
-    const int grp = cc / 32, e = cc % 32, i4 = e / 4, p = e % 4;
-    const int c = grp & 3, hi = grp >> 2;  // group grp sits with lane c's low (grp < 4) or high part
-    const int lane = g * 4 + c;
-    const uint8_t *tile = tiles + (size_t(rt) * ktiles + kt) * tile_bytes;
-    float v;
-    if (kind == kKindInt8) {
-      const int8_t q = int8_t(tile[lane * 64 + i4 * 8 + hi * 4 + p]);
-      v = float(q) * row_scale[r];
-    } else {
-      // the scale data of (row r, group grp) sits with lane (grp, r%8 / 2)
-      const int sl = grp * 4 + g / 2;
-      if (kind == kKindInt4) {
-        const uint8_t by = tile[lane * 32 + i4 * 4 + p];
-        const int q = hi ? (by >> 4) : (by & 15);
-        const uint16_t *sz = reinterpret_cast<const uint16_t *>(tile + kTileCodes4 + sl * 8);
-        const float s = __half2float(__ushort_as_half(sz[g & 1]));
-        const float z = __half2float(__ushort_as_half(sz[2 + (g & 1)]));
-        float x = float(q);
-        x = __fsub_rn(x, z);
-        v = __fmul_rn(x, s);
-      } else {
-        const uint8_t by = tile[lane * 32 + i4 * 4 + hi * 2 + p / 2];
-        const int code = (p & 1) ? (by >> 4) : (by & 15);
-        const float mag[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
-        const float val = (code & 8) ? -mag[code & 7] : mag[code & 7];
-        const uint8_t ee = tile[kTileCodes4 + sl * 2 + (g & 1)];
-        v = __fmul_rn(val, __uint_as_float(uint32_t(ee) << 23));
-      }
-    }
-    out[i] = v;
+    out[i] = tile_value(tiles, row_scale, kind, ktiles, tile_bytes, r, col);
   }
 }
 

@@ -20,7 +20,7 @@ struct DevMat {
 enum GemvMode : int {
   kStore = 0,     // y[t][r] = v
   kAdd = 1,       // y[t][r] += v (the residual stream)
-  kGlu = 2,       // tile rows 0-3 gate, 4-7 up: y[t][o] = silu(gate) * up, o = 4 * rtile + j
+  kGlu = 2,       // tile rows 0-7 gate, 8-15 up: y[t][o] = silu(gate) * up, o = 8 * rtile + j
   kLogits = 3,    // fp16 logits[t][r] and the greedy choice folded into amax[t]
 };
 

@@ -1,22 +1,24 @@
 // mk.cu: the persistent decode kernel (see mk.h). One CTA per SM runs every phase of the step:
 //
-//   embed -> per layer: [qkv GEMV] -> [attention] -> [o GEMV + residual] -> [gate/up GEMV + SiLU]
-//            -> [down GEMV + residual] -> head GEMV + greedy choice
+//   per layer: [qkv GEMV] -> [attention units] -> [o GEMV + residual] -> [gate/up GEMV + SiLU]
+//              -> [down GEMV + residual];  then the head GEMV + greedy choice
 //
 // with a grid barrier between phases. A CTA is 8 consumer warps and 1 producer warp. The producer
 // walks the same static schedule as the consumers (the CTA's row tiles of every GEMV, its attention
-// unit's cached keys and values) and streams it from HBM into a ring of shared-memory stages with
+// units' cached keys and values) and streams it from HBM into a ring of shared-memory stages with
 // bulk copies (cp.async.bulk, an mbarrier per stage for "full" and one for "empty"), running ahead
 // of the grid barriers the consumers wait at, so HBM keeps streaming while they synchronise.
 // No wait is unbounded: a grid barrier or a stage that does not arrive within
 // MkParams::spin_limit cycles sets *status and the kernel returns.
 //
-// Activations reach a GEMV as int8 tiles (common.h's kActTile) written by the phase that produced
-// them: the o-proj and down producers own whole groups of 32 output rows, add the residual,
-// quantise x times the next norm's weight and store each group's sum of squares, from which
-// every consumer forms the norm's 1/rms (qwen3's normScaled, build.go:131-151) and applies it to
-// the group scales; the gate/up producer quantises silu(gate)*up; the attention's last split of a
-// head quantises the head's output.
+// Every GEMV spreads its 8-row tiles evenly over the CTAs and finishes each row tile where it is
+// computed (the last warp of the team that owns it applies the epilogue: the qkv rows, the
+// residual add into x, silu(gate) * up into h, or the fp16 logits and greedy key). The inputs of a
+// GEMV are built by every CTA for itself at the start of the phase: x (or h) is read back, times
+// the norm weight, and quantised to int8 tiles (common.h's kActTile) in shared memory, with the
+// norm's 1/rms (qwen3's normScaled, build.go:131-151) applied to the rows' results; the o
+// projection's input is the attention output, which every CTA merges from the units' per-split
+// partials.
 #include <algorithm>
 
 #include "device.cuh"
@@ -26,6 +28,9 @@ namespace hc {
 namespace {
 
 constexpr int kWarps = kMkThreads / 32;
+
+// Issues the ring's next copies whose stages are free (lane 0 of warp 0; defined with the producer).
+__device__ __forceinline__ void try_issue(const MkParams &p);
 
 // ---- grid barrier with a deadline ------------------------------------------------------------
 // Cycles between two looks at the status word (another CTA's failure) and the deadline in a wait.
@@ -43,21 +48,25 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Synchronises the 8 consumer warps (named barrier 1; the producer warp never joins).
+// Synchronises the 8 warps of the CTA (named barrier 1).
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kMkThreads) : "memory"); }
 
 // The grid barrier of the consumers: returns false when it (or an earlier one) gave up.
 // A sub-phase mark of the trace (thread 0): slot 0 when the phase's inputs are in smem, 1 when its
 // chunks are consumed.
-__device__ __forceinline__ void mark(const MkParams &p, unsigned epoch, int slot) {
+__shared__ unsigned s_epoch;  // grid barriers this CTA passed in the step (thread 0's count)
+
+__device__ __forceinline__ void mark(const MkParams &p, int slot) {
   if (p.trace && threadIdx.x == 0)
-    p.trace[size_t(2 + slot) * mk_phases(p.layers) * gridDim.x + size_t(epoch) * gridDim.x + blockIdx.x] = global_ns();
+    p.trace[size_t(2 + slot) * mk_phases(p.layers) * gridDim.x + size_t(s_epoch) * gridDim.x + blockIdx.x] =
+        global_ns();
 }
 
-__device__ bool grid_sync(const MkParams &p, unsigned &epoch) {
+__device__ __forceinline__ bool grid_sync(const MkParams &p) {
   __shared__ int ok;
   csync();
   if (threadIdx.x == 0) {
+    unsigned epoch = s_epoch;
     if (p.trace) p.trace[size_t(epoch) * gridDim.x + blockIdx.x] = global_ns();
     epoch += 1;
     const unsigned target = epoch * gridDim.x;
@@ -65,7 +74,9 @@ __device__ bool grid_sync(const MkParams &p, unsigned &epoch) {
     const long long t0 = clock64();
     long long next = t0 + kStatusPoll;
     int good = 1;
+    try_issue(p);
     while (ld_acquire(p.bar) < target) {
+      try_issue(p);  // stages freed by the phase's last chunks
       // the status word and the deadline are looked at every kStatusPoll cycles only, so that a
       // poll costs one L2 round trip
       const long long now = clock64();
@@ -79,6 +90,7 @@ __device__ bool grid_sync(const MkParams &p, unsigned &epoch) {
       }
     }
     if (p.trace) p.trace[size_t(mk_phases(p.layers) + epoch - 1) * gridDim.x + blockIdx.x] = global_ns();
+    s_epoch = epoch;
     ok = good;
   }
   csync();
@@ -91,70 +103,9 @@ __device__ __forceinline__ void my_units(int U, int &u0, int &u1) {
   u1 = int((long long)(blockIdx.x + 1) * U / gridDim.x);
 }
 
-// ---- activation quantisation of one group of 32 (one value a lane) --------------------------
-// hi = round_even(v * 127 / max), lo = the residual at 1/256 of the scale (common.h, kActTile).
-__device__ __forceinline__ void quant32(float v, uint8_t *tile, int gi, int lane) {
-  const float m = warp_max(fabsf(v));
-  int8_t hq = 0, lq = 0;
-  float S = 0.f;
-  int s256 = 0;
-  if (m > 0.f) {
-    const float inv = 127.0f / m;
-    S = m / 127.0f;
-    const float h = rintf(v * inv);
-    const float r = fmaf(-h, S, v);
-    const float l = fminf(fmaxf(rintf(r * (256.0f * inv)), -127.f), 127.f);
-    hq = int8_t(h);
-    lq = int8_t(l);
-    s256 = warp_sum_i(int(hq) * 256 + int(lq));
-  }
-  tile[gi * 64 + lane] = uint8_t(hq);
-  tile[gi * 64 + 32 + lane] = uint8_t(lq);
-  if (lane == 0)
-    *reinterpret_cast<float2 *>(tile + kGroupsPerTile * 64 + gi * 8) = make_float2(S, float(s256) * (1.0f / 256.0f));
-}
-
-// x (one value a lane, the group grp of a row of D) into the activation tiles of the next norm:
-// the tiles hold x*w, and sq[grp] the group's sum of (x/scale)^2 (float squares, summed in double
-// as milcpu's reduce_mean does, ops.go:861-920).
-__device__ __forceinline__ void quant_norm32(float x, float w, float scale, uint8_t *act, double *sq,
-                                             int grp, int lane) {
-  const float xs = scale == 1.f ? x : x * (1.f / scale);
-  double s = double(xs * xs);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) sq[grp] = s;
-  quant32(x * w, act + size_t(grp / kGroupsPerTile) * kActTile, grp % kGroupsPerTile, lane);
-}
-
-// The factor a consumer applies to the group scales of a normed input: r / scale with
-// r = float32(1 / sqrt(float64(mean) + eps16)) (milcpu rsqrt, ops.go:181-189). One warp; the
-// group sums (written by other CTAs in this launch) are read past L1.
-__device__ float norm_factor_warp(const double *sq, int groups, int n, float scale, float eps16, int lane) {
-  double s = 0;
-  for (int g = lane; g < groups; g += 32) s += __ldcg(sq + g);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  const float ms = float(s / double(n));
-  const float r = float(1.0 / sqrt(double(ms) + double(eps16)));
-  return r * (1.f / scale);
-}
-
-// Per-token norm factors into cf[t] (warp t does token t).
-template <int NT>
-__device__ __forceinline__ void norm_factors(float *cf, const double *sq, int groups, int n, float scale,
-                                             float eps16) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp < NT) {
-    const float f = norm_factor_warp(sq + size_t(warp) * groups, groups, n, scale, eps16, lane);
-    if (lane == 0) cf[warp] = f;
-  }
-}
-
 // ---- the stage ring -----------------------------------------------------------------------------
-constexpr int kStageBytes = 16384;  // one chunk: up to 8 column tiles of a row tile, or keys+values
-constexpr int kKr = 8;              // column tiles of a weight chunk (one a consumer warp)
-constexpr int kProducerWarp = kWarps;
+constexpr int kKr = 8;  // column tiles of a weight chunk (one a consumer warp); a stage holds one chunk
+                        // (8 tiles of the model's format, MkParams::stage_bytes) or keys + values
 
 __device__ __forceinline__ uint32_t saddr(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -168,32 +119,27 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *b, unsigned count) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *b, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
 }
+// try_wait with a suspend-time hint: a waiting thread sleeps in hardware (woken when the phase
+// completes, or after about kSuspendNs) instead of spinning on the issue slots the consumers need.
+constexpr unsigned kSuspendNs = 20000;
 __device__ __forceinline__ bool mbar_try(uint64_t *b, unsigned parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred P;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2;\n selp.u32 %0, 1, 0, P;\n}\n"
+      "{\n .reg .pred P;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2, %3;\n selp.u32 %0, 1, 0, P;\n}\n"
+      : "=r"(ok)
+      : "r"(saddr(b)), "r"(parity), "n"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+// Whether the phase of parity `parity` of b has completed, without waiting.
+__device__ __forceinline__ bool mbar_test(uint64_t *b, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred P;\n mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2;\n selp.u32 %0, 1, 0, P;\n}\n"
       : "=r"(ok)
       : "r"(saddr(b)), "r"(parity)
       : "memory");
   return ok != 0;
-}
-// Waits for the phase of parity `parity` of b; false (and *status set) past the deadline or when
-// another wait already failed.
-__device__ bool mbar_wait(uint64_t *b, unsigned parity, const MkParams &p, int code) {
-  if (mbar_try(b, parity)) return true;
-  const long long t0 = clock64();
-  long long next = t0 + kStatusPoll;
-  for (;;) {
-    if (mbar_try(b, parity)) return true;
-    const long long now = clock64();
-    if (now < next) continue;
-    next = now + kStatusPoll;
-    if (*reinterpret_cast<volatile int *>(p.status)) return false;
-    if (now - t0 > p.spin_limit) {
-      atomicCAS(p.status, 0, code);
-      return false;
-    }
-  }
 }
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(saddr(dst)),
@@ -204,16 +150,44 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
 struct Ring {
   uint8_t *stages;
   uint64_t *full, *empty;
-  int S;
+  int S, SB;  // stages, bytes a stage
 };
 
-// A GEMV phase of a CTA: row tiles [rt0, rt0 + nrt) of a matrix of ktiles column tiles; chunk
-// (i, kr), the (kr nrt + i)-th of the phase, holds column tiles [8 kr, 8 kr + 8) of row tile rt0 + i.
+// At most this many stages; the row partials use twice as many slots.
+constexpr int kMaxStages = 16;
+
+// The kernel's dynamic shared memory (mk_layout places its parts) and its small shared state. The
+// phases find everything from here and from the parameters, so that the kernel body keeps almost
+// nothing alive across them.
+extern __shared__ __align__(1024) uint8_t mk_smem[];
+__shared__ float s_cfac[kMkMaxTok];              // per-token factor of the phase's rows (the norm)
+__shared__ unsigned long long s_bmax[kMkMaxTok];  // this CTA's greedy keys in the head
+__shared__ unsigned s_rcnt[2 * kMaxStages];       // arrivals at each row partial slot
+__shared__ StepTok s_toks[kMkMaxTok];             // the step's tokens
+// The row scale and bias of the GEMV phase that runs (set before it; read by its epilogues).
+__shared__ const float *s_rscale;
+__shared__ const float *s_rbias;
+
+__device__ __forceinline__ Ring ring_of(const MkParams &p) {
+  Ring r;
+  r.S = p.stages;
+  r.SB = p.stage_bytes;
+  r.stages = mk_smem;
+  r.full = reinterpret_cast<uint64_t *>(mk_smem + p.off_bar);
+  r.empty = r.full + p.stages;
+  return r;
+}
+
+// A GEMV phase of a CTA: row tiles rt0 + i * stride (i < nrt) of a matrix of ktiles column tiles;
+// chunk (i, kr), the (i nkr + kr)-th of the phase, holds column tiles [8 kr, 8 kr + 8) of row tile
+// rt(i). The CTAs interleave (rt0 = the CTA, stride = the grid), so that at any moment the grid
+// reads neighbouring tiles, spread over all of HBM's channels.
 struct GemvPhase {
   const uint8_t *tiles;
-  int ktiles, rt0, nrt, tb;
+  int ktiles, rt0, nrt, tb, stride;
   __device__ int nkr() const { return (ktiles + kKr - 1) / kKr; }
   __device__ int chunks() const { return nrt * nkr(); }
+  __device__ int rt(int i) const { return rt0 + i * stride; }
 };
 
 // The cached keys of an attention unit: positions [k0, kc1) of (slot, kv head), in chunks of kc keys.
@@ -232,31 +206,16 @@ __device__ __forceinline__ int tile_bytes_of() {
 template <int KIND, int NT>
 struct Schedule {
   const MkParams &p;
-  __device__ GemvPhase qkv(int l) const {
-    int u0, u1;
-    my_units(p.rt_qkv, u0, u1);
-    return GemvPhase{p.L[l].qkv, p.kt_d, u0, u1 - u0, tile_bytes_of<KIND>()};
+  // every GEMV deals its row tiles out to the CTAs in turn
+  __device__ GemvPhase rows(const uint8_t *tiles, int rtiles, int ktiles) const {
+    const int b = blockIdx.x, G = gridDim.x;
+    return GemvPhase{tiles, ktiles, b, b < rtiles ? (rtiles - b + G - 1) / G : 0, tile_bytes_of<KIND>(), G};
   }
-  __device__ GemvPhase o(int l) const {
-    int u0, u1;
-    my_units(p.D / 32, u0, u1);
-    return GemvPhase{p.L[l].o, p.kt_o, 4 * u0, 4 * (u1 - u0), tile_bytes_of<KIND>()};
-  }
-  __device__ GemvPhase gu(int l) const {
-    int u0, u1;
-    my_units(p.F / 32, u0, u1);
-    return GemvPhase{p.L[l].gu, p.kt_d, 8 * u0, 8 * (u1 - u0), tile_bytes_of<KIND>()};
-  }
-  __device__ GemvPhase down(int l) const {
-    int u0, u1;
-    my_units(p.D / 32, u0, u1);
-    return GemvPhase{p.L[l].down, p.kt_f, 4 * u0, 4 * (u1 - u0), tile_bytes_of<KIND>()};
-  }
-  __device__ GemvPhase head() const {
-    int u0, u1;
-    my_units(p.rt_head, u0, u1);
-    return GemvPhase{p.head, p.kt_d, u0, u1 - u0, tile_bytes_of<KIND>()};
-  }
+  __device__ GemvPhase qkv(int l) const { return rows(p.L[l].qkv, p.rt_qkv, p.kt_d); }
+  __device__ GemvPhase o(int l) const { return rows(p.L[l].o, p.D / kTileRows, p.kt_o); }
+  __device__ GemvPhase gu(int l) const { return rows(p.L[l].gu, 2 * p.F / kTileRows, p.kt_d); }
+  __device__ GemvPhase down(int l) const { return rows(p.L[l].down, p.D / kTileRows, p.kt_f); }
+  __device__ GemvPhase head() const { return rows(p.head, p.rt_head, p.kt_d); }
   __device__ void units(int &a0, int &a1) const { my_units(NT * p.KV * p.splits, a0, a1); }
   __device__ AttPhase att(int l, int u) const {
     const int t = u / (p.KV * p.splits), kvh = (u / p.splits) % p.KV, s = u % p.splits;
@@ -268,7 +227,7 @@ struct Schedule {
     const int chunk = (n + p.splits - 1) / p.splits;
     const int k0 = lo + s * chunk, k1 = min(P + 1, k0 + chunk);
     const size_t base = (size_t(tk.slot) * p.KV + kvh) * size_t(p.cap) * p.hd;
-    return AttPhase{L.kc + base, L.vc + base, k0, min(k1, P), kStageBytes / (4 * p.hd), p.hd};
+    return AttPhase{L.kc + base, L.vc + base, k0, min(k1, P), p.stage_bytes / (4 * p.hd), p.hd};
   }
 };
 
@@ -291,86 +250,122 @@ __device__ __forceinline__ void utrace(const MkParams &p, int li, int k) {
         clock64();
 }
 
-// ---- the producer ---------------------------------------------------------------------------
-// Cycles the producer spent waiting for free stages (trace runs only).
-__device__ __forceinline__ bool produce_slot(const Ring &r, int j, const MkParams &p, long long &waited) {
-  const int s = j % r.S;
-  if (j < r.S) return true;
-  const long long t0 = clock64();
-  const bool ok = mbar_wait(&r.empty[s], ((j / r.S) + 1) & 1, p, 1000001);
-  waited += clock64() - t0;
-  return ok;
+// ---- the producer: lane 0 of warp 0 issues the ring's bulk copies, never blocking -------------
+// The walker over the step's chunks in the consumers' order: per layer the qkv rows, the attention
+// units' keys and values, the o, gate/up and down rows; then the head's rows.
+struct Prod {
+  int j;      // the next chunk's ring position
+  int q;      // its phase: 5 li + (0 qkv, 1 attention, 2 o, 3 gate/up, 4 down); 5 layers: the head
+  int i, kr;  // GEMV: row tile and column chunk; attention: unit (from the CTA's first) and key chunk
+};
+__shared__ Prod s_prod;
+
+__device__ __forceinline__ GemvPhase gemv_rows(const MkParams &p, const uint8_t *tiles, int rtiles, int ktiles) {
+  const int b = blockIdx.x, G = gridDim.x;
+  const int tb = p.kind == kKindInt8 ? kTileInt8 : (p.kind == kKindInt4 ? kTileInt4 : kTileMx);
+  return GemvPhase{tiles, ktiles, b, b < rtiles ? (rtiles - b + G - 1) / G : 0, tb, G};
 }
 
-// Chunks in consume_gemv's order (kr-major), or consume_head's (imajor).
-__device__ bool produce_gemv(const Ring &r, int &j, const GemvPhase &g, const MkParams &p, long long &waited,
-                             bool imajor = false) {
-  const int nkr = g.nkr();
-  for (int c = 0; c < g.chunks(); ++c, ++j) {
-    const int kr = imajor ? c % nkr : c / g.nrt, i = imajor ? c / nkr : c % g.nrt;
-    if (!produce_slot(r, j, p, waited)) return false;
-    const int s = j % r.S;
-    const int nk = min(kKr, g.ktiles - kr * kKr);
-    const unsigned bytes = unsigned(nk * g.tb);
-    ctrace(p, j, 0);
-    mbar_expect_tx(&r.full[s], bytes);
-    bulk_g2s(r.stages + size_t(s) * kStageBytes, g.tiles + (size_t(g.rt0 + i) * g.ktiles + kr * kKr) * g.tb, bytes,
-             &r.full[s]);
-  }
-  return true;
+// The cached keys of attention unit u of layer li (as Schedule::att).
+__device__ __forceinline__ AttPhase att_phase(const MkParams &p, int li, int u) {
+  const int t = u / (p.KV * p.splits), kvh = (u / p.splits) % p.KV, s = u % p.splits;
+  const StepTok tk = s_toks[t];
+  const int P = tk.pos;
+  const MkLayer &L = p.L[li];
+  const int lo = L.window > 0 ? max(0, P - L.window + 1) : 0;
+  const int n = P - lo + 1;
+  const int chunk = (n + p.splits - 1) / p.splits;
+  const int k0 = lo + s * chunk, k1 = min(P + 1, k0 + chunk);
+  const size_t base = (size_t(tk.slot) * p.KV + kvh) * size_t(p.cap) * p.hd;
+  return AttPhase{L.kc + base, L.vc + base, k0, min(k1, P), p.stage_bytes / (4 * p.hd), p.hd};
 }
 
-__device__ bool produce_att(const Ring &r, int &j, const AttPhase &a, const MkParams &p, long long &waited) {
-  const int n = a.chunks();
-  for (int c = 0; c < n; ++c, ++j) {
-    if (!produce_slot(r, j, p, waited)) return false;
-    const int s = j % r.S;
-    const int key0 = a.k0 + c * a.kc, nkeys = min(a.kc, a.kc1 - key0);
-    const unsigned bytes = unsigned(nkeys * a.hd * 2);
-    ctrace(p, j, 0);
-    mbar_expect_tx(&r.full[s], 2 * bytes);
-    uint8_t *dst = r.stages + size_t(s) * kStageBytes;
-    bulk_g2s(dst, a.kbase + size_t(key0) * a.hd, bytes, &r.full[s]);
-    bulk_g2s(dst + bytes, a.vbase + size_t(key0) * a.hd, bytes, &r.full[s]);
+// The next chunk's sources (one or two copies) from the walker's place, which it then passes;
+// false when the step has no more.
+__device__ __forceinline__ bool prod_next(const MkParams &p, Prod &w, const void *&s0, unsigned &b0, const void *&s1,
+                          unsigned &b1) {
+  const int L = p.layers;
+  for (;;) {
+    if (w.q > 5 * L) return false;
+    const int li = w.q / 5, ph = w.q % 5;
+    if (w.q == 5 * L || ph != 1) {
+      const GemvPhase g = w.q == 5 * L ? gemv_rows(p, p.head, p.rt_head, p.kt_d)
+                          : ph == 0    ? gemv_rows(p, p.L[li].qkv, p.rt_qkv, p.kt_d)
+                          : ph == 2    ? gemv_rows(p, p.L[li].o, p.D / kTileRows, p.kt_o)
+                          : ph == 3    ? gemv_rows(p, p.L[li].gu, 2 * p.F / kTileRows, p.kt_d)
+                                       : gemv_rows(p, p.L[li].down, p.D / kTileRows, p.kt_f);
+      if (w.i < g.nrt) {
+        const int nk = min(kKr, g.ktiles - w.kr * kKr);
+        s0 = g.tiles + (size_t(g.rt(w.i)) * g.ktiles + w.kr * kKr) * g.tb;
+        b0 = unsigned(nk * g.tb);
+        s1 = nullptr;
+        b1 = 0;
+        if (++w.kr == g.nkr()) { w.kr = 0; ++w.i; }
+        return true;
+      }
+    } else {
+      int a0, a1;
+      my_units(p.ntok * p.KV * p.splits, a0, a1);
+      if (a0 + w.i < a1) {
+        const AttPhase a = att_phase(p, li, a0 + w.i);
+        if (w.kr < a.chunks()) {
+          const int key0 = a.k0 + w.kr * a.kc, nkeys = min(a.kc, a.kc1 - key0);
+          s0 = a.kbase + size_t(key0) * a.hd;
+          s1 = a.vbase + size_t(key0) * a.hd;
+          b0 = b1 = unsigned(nkeys * a.hd * 2);
+          ++w.kr;
+          return true;
+        }
+        ++w.i;
+        w.kr = 0;
+        continue;
+      }
+    }
+    ++w.q;
+    w.i = 0;
+    w.kr = 0;
   }
-  return true;
 }
 
-template <int KIND, int NT>
-__device__ __noinline__ void producer(const Ring r, const MkParams &p) {
-  const Schedule<KIND, NT> sc{p};
-  const long long t0 = clock64();
-  long long waited = 0;
-  int j = 0;
-  bool ok = true;
-  for (int l = 0; l < p.layers && ok; ++l) {
-    ok = produce_gemv(r, j, sc.qkv(l), p, waited);
-    int a0, a1;
-    sc.units(a0, a1);
-    for (int u = a0; u < a1 && ok; ++u) ok = produce_att(r, j, sc.att(l, u), p, waited);
-    ok = ok && produce_gemv(r, j, sc.o(l), p, waited);
-    ok = ok && produce_gemv(r, j, sc.gu(l), p, waited);
-    ok = ok && produce_gemv(r, j, sc.down(l), p, waited);
+// Issues every chunk whose stage is free (the stage's previous chunk released by all 8 warps), in
+// order, without waiting. Lane 0 of warp 0 only: at each of its waits for a chunk, in the grid
+// barrier's poll, and when a step starts.
+__device__ __forceinline__ void try_issue(const MkParams &p) {
+  const Ring r = ring_of(p);
+  Prod w = s_prod;
+  for (;;) {
+    if (w.j >= r.S && !mbar_test(&r.empty[w.j % r.S], ((w.j / r.S) + 1) & 1)) break;
+    const void *s0, *s1;
+    unsigned b0, b1;
+    if (!prod_next(p, w, s0, b0, s1, b1)) break;
+    const int s = w.j % r.S;
+    ctrace(p, w.j, 0);
+    mbar_expect_tx(&r.full[s], b0 + b1);
+    uint8_t *dst = r.stages + size_t(s) * r.SB;
+    bulk_g2s(dst, s0, b0, &r.full[s]);
+    if (b1) bulk_g2s(dst + b0, s1, b1, &r.full[s]);
+    ++w.j;
   }
-  if (ok) produce_gemv(r, j, sc.head(), p, waited, true);
-  if (p.trace) {
-    // after the phase planes: [ctas][4] producer waited, producer busy, consumer waited, consumer busy
-    unsigned long long *st = p.trace + size_t(4) * mk_phases(p.layers) * gridDim.x + size_t(blockIdx.x) * 4;
-    st[0] = waited;
-    st[1] = clock64() - t0;
-  }
+  s_prod = w;
 }
 
 // Cycles warp 0 of the consumers waited for stages (trace runs).
 __shared__ long long s_cwait;
 
-// The slow path of mbar_wait_warp (kept out of line so the chunk loops stay call-free).
-__device__ __noinline__ bool mbar_wait_warp_slow(uint64_t *b, unsigned parity, const MkParams &p, int code) {
+// The slow path of mbar_wait_warp (kept out of line so the chunk loops stay call-free). Warp 0
+// keeps issuing the ring's copies while it waits (so it polls without sleeping); the other warps
+// sleep in try_wait.
+__device__ __forceinline__ bool mbar_wait_warp_slow(uint64_t *b, unsigned parity, const MkParams &p, int code) {
   const int lane = threadIdx.x & 31;
+  const bool issuer = threadIdx.x < 32;
   const long long t0 = clock64();
   long long next = t0 + kStatusPoll;
   for (;;) {
-    if (__all_sync(0xffffffffu, mbar_try(b, parity))) {
+    if (issuer) {
+      if (lane == 0) try_issue(p);
+      __syncwarp();
+    }
+    if (__all_sync(0xffffffffu, issuer ? mbar_test(b, parity) : mbar_try(b, parity))) {
       if (threadIdx.x == 0) s_cwait += clock64() - t0;
       return true;
     }
@@ -387,343 +382,407 @@ __device__ __noinline__ bool mbar_wait_warp_slow(uint64_t *b, unsigned parity, c
 }
 
 // mbar_wait for a whole warp: every lane leaves with the same answer (the MMAs that follow need
-// the warp converged).
+// the warp converged). Warp 0 first issues what it can.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t *b, unsigned parity, const MkParams &p, int code) {
-  if (__all_sync(0xffffffffu, mbar_try(b, parity))) return true;
+  if (threadIdx.x < 32) {
+    if (threadIdx.x == 0) try_issue(p);
+    __syncwarp();
+  }
+  if (__all_sync(0xffffffffu, mbar_test(b, parity))) return true;
   return mbar_wait_warp_slow(b, parity, p, code);
 }
 
 // ---- the consumers ----------------------------------------------------------------------------
-// Copies NT tokens' activation tiles (ktiles each) from global into smem (the 8 consumer warps).
-template <int NT>
-__device__ __forceinline__ void load_act(uint8_t *act_s, const uint8_t *act_g, int ktiles) {
-  const int n16 = NT * ktiles * kActTile / 16;
-  const uint4 *src = reinterpret_cast<const uint4 *>(act_g);
-  uint4 *dst = reinterpret_cast<uint4 *>(act_s);
-  for (int i = threadIdx.x; i < n16; i += kMkThreads) dst[i] = __ldcg(src + i);
-}
 
-// One column tile's B operands for one lane, read out of a stage so that the stage can be released
-// before the MMAs run.
-template <int KIND>
-struct BTile {
-  uint32_t w[KIND == kKindInt8 ? 16 : 8];
-  uint32_t sz[2];
-  __device__ __forceinline__ void load(const uint8_t *tile, int lane) {
-    if (KIND == kKindInt8) {
-      const uint4 *q = reinterpret_cast<const uint4 *>(tile + lane * 64);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint4 v = q[u];
-        w[4 * u] = v.x; w[4 * u + 1] = v.y; w[4 * u + 2] = v.z; w[4 * u + 3] = v.w;
-      }
-    } else {
-      const uint4 *q = reinterpret_cast<const uint4 *>(tile + lane * 32);
-      const uint4 v0 = q[0], v1 = q[1];
-      w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w; w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
-      if (KIND == kKindInt4) {
-        const uint2 q2 = *reinterpret_cast<const uint2 *>(tile + kTileCodes4 + lane * 8);
-        sz[0] = q2.x; sz[1] = q2.y;
-      } else {
-        sz[0] = *reinterpret_cast<const unsigned short *>(tile + kTileCodes4 + lane * 2);
-        sz[1] = 0;
-      }
-    }
-  }
+// The GEMV phases, and what the last warp of a row tile does with its 16 rows x NT tokens.
+enum Phase : int {
+  kPhQkv = 0,   // qkv[t][row] = v * cf[t] * scale[row] + bias[row]
+  kPhO = 1,     // x[t][row] += v * scale[row] + bias[row]       (the residual)
+  kPhGu = 2,    // h[t][rt*8 + r] = silu(gate) * up, rows r / r + 8 of tile rt
+  kPhDown = 3,  // x[t][row] += v * scale[row]                    (the residual)
+  kPhHead = 4,  // fp16 logits and the greedy key of every row below V
 };
 
-// The A fragments of one token's activation tile for the 8 integer MMAs of a column tile: lane
-// (g, c) feeds group c (g == c) or group g (g == c + 4) into A's rows, zeros elsewhere; and the
-// scale S and sum Xq of the group g the lane's results belong to. hi16: the B codes of groups 4..7
-// arrive multiplied by 16 (int4: w & 0xF0 instead of (w >> 4) & 0x0F), so those lanes carry S / 16
-// and 16 Xq, which leaves every product exactly as it was (powers of two).
-struct AFrag {
-  uint32_t a[8][4];
-  float S, Xq;
-  __device__ __forceinline__ void load(const uint8_t *at, int lane, bool mx, bool hi16) {
-    const int gq = lane >> 2, c = lane & 3;
-    const bool role0 = gq == c, role1 = gq == c + 4;
-    const int agrp = role0 ? c : gq;
-    uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0, l0 = h0, l1 = h0;
-    if (role0 || role1) {
-      const uint4 *ap = reinterpret_cast<const uint4 *>(at + agrp * 64);
-      h0 = ap[0]; h1 = ap[1];
-      if (!mx) { l0 = ap[2]; l1 = ap[3]; }
-    }
-    const float2 sx = *reinterpret_cast<const float2 *>(at + kGroupsPerTile * 64 + gq * 8);
-    S = sx.x;
-    Xq = sx.y;
-    if (hi16 && gq >= 4) {
-      S *= 0.0625f;
-      Xq *= 16.0f;
-    }
-    const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-    const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      a[u][0] = role0 ? hw[u] : 0u;
-      a[u][1] = role0 ? lw[u] : 0u;
-      a[u][2] = role1 ? hw[u] : 0u;
-      a[u][3] = role1 ? lw[u] : 0u;
-    }
-  }
-  // an inactive column tile: zero A and scales (its B is read from a valid tile, so every
-  // product is an exact zero)
-  __device__ __forceinline__ void zero() {
-#pragma unroll
-    for (int u = 0; u < 8; ++u) a[u][0] = a[u][1] = a[u][2] = a[u][3] = 0u;
-    S = 0.f;
-    Xq = 0.f;
-  }
-};
-
-// The MMAs of one column tile (B read from the stage) with cached A fragments; returns lane
-// (g, c)'s two rows' values for group g, scaled to float32.
-template <int KIND>
-__device__ __forceinline__ void tile_mma_cached(const uint8_t *tile, const AFrag &af, int lane, float &v0, float &v1) {
-  BTile<KIND> bt;
-  bt.load(tile, lane);
-  uint32_t b0[8], b1[8];
-  float s0 = 0.f, s1 = 0.f, z0 = 0.f, z1 = 0.f;
-  if (KIND == kKindInt8) {
-#pragma unroll
-    for (int u = 0; u < 8; ++u) { b0[u] = bt.w[2 * u]; b1[u] = bt.w[2 * u + 1]; }
-  } else if (KIND == kKindInt4) {
-    const __half2 sh = *reinterpret_cast<const __half2 *>(&bt.sz[0]);
-    const __half2 zh = *reinterpret_cast<const __half2 *>(&bt.sz[1]);
-    s0 = __low2float(sh); s1 = __high2float(sh);
-    z0 = __low2float(zh); z1 = __high2float(zh);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) { b0[u] = bt.w[u] & 0x0F0F0F0Fu; b1[u] = bt.w[u] & 0xF0F0F0F0u; }
-  } else {
-    s0 = __uint_as_float((bt.sz[0] & 0xff) << 23);
-    s1 = __uint_as_float(((bt.sz[0] >> 8) & 0xff) << 23);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const uint32_t wsh = bt.w[u] << 4;
-      b0[u] = e2m1x4(bt.w[u], wsh, 0xD9C8u, bt.w[u] & 0x7777u);
-      b1[u] = e2m1x4(bt.w[u], wsh, 0xFBEAu, (bt.w[u] >> 16) & 0x7777u);
-    }
-  }
-  int d[4] = {0, 0, 0, 0}, e[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int u = 0; u < 8; u += 2) {
-    if (KIND == kKindInt4) {
-      mma_s8u8(d, af.a[u][0], af.a[u][1], af.a[u][2], af.a[u][3], b0[u], b1[u]);
-      mma_s8u8(e, af.a[u + 1][0], af.a[u + 1][1], af.a[u + 1][2], af.a[u + 1][3], b0[u + 1], b1[u + 1]);
-    } else {
-      mma_s8s8(d, af.a[u][0], af.a[u][1], af.a[u][2], af.a[u][3], b0[u], b1[u]);
-      mma_s8s8(e, af.a[u + 1][0], af.a[u + 1][1], af.a[u + 1][2], af.a[u + 1][3], b0[u + 1], b1[u + 1]);
-    }
-  }
-#pragma unroll
-  for (int q = 0; q < 4; ++q) d[q] += e[q];
-  if (KIND == kKindMx) {
-    v0 = float(d[0]) * s0 * af.S;
-    v1 = float(d[1]) * s1 * af.S;
-  } else {
-    const float p0 = fmaf(float(d[2]), 1.0f / 256.0f, float(d[0]));
-    const float p1 = fmaf(float(d[3]), 1.0f / 256.0f, float(d[1]));
-    if (KIND == kKindInt4) {
-      v0 = (s0 * af.S) * fmaf(-z0, af.Xq, p0);
-      v1 = (s1 * af.S) * fmaf(-z1, af.Xq, p1);
-    } else {
-      v0 = af.S * p0;
-      v1 = af.S * p1;
-    }
-  }
-}
-
-// Sums lane values over the 8 groups (lanes g = 0..7 of the same c).
-__device__ __forceinline__ float group_sum(float v) {
-  v += __shfl_xor_sync(0xffffffffu, v, 4);
-  v += __shfl_xor_sync(0xffffffffu, v, 8);
-  v += __shfl_xor_sync(0xffffffffu, v, 16);
-  return v;
-}
-
-// GEMV work split: the 8 consumer warps are 2 teams of 4; team i % 2 takes row tile i, and in a
-// chunk (8 column tiles of one row tile) warp q of the team takes column tiles 2q and 2q + 1, so
-// each warp runs two independent MMA chains and one group reduction per row tile. A warp arrives
-// on the chunk's "empty" barrier with count 2 (4 warps make the 8 the barrier counts).
-constexpr int kTeamWarps = 4;
-
-// A warp's pair of column tiles of one chunk for token t: the group-scaled values of its lane
-// summed over the 8 groups (lanes (g, c), rows 2c and 2c + 1).
-template <int KIND>
-__device__ __forceinline__ void pair_mma(const uint8_t *stage, int q4, bool act1, const AFrag &f0, const AFrag &f1,
-                                         int lane, float &v0, float &v1) {
-  constexpr int TB = KIND == kKindInt8 ? kTileInt8 : (KIND == kKindInt4 ? kTileInt4 : kTileMx);
-  const uint8_t *t0 = stage + size_t(2 * q4) * TB;
-  const uint8_t *t1 = act1 ? t0 + TB : t0;  // an inactive second tile reads the first (f1 is zero)
-  float x0, x1, y0, y1;
-  tile_mma_cached<KIND>(t0, f0, lane, x0, x1);
-  tile_mma_cached<KIND>(t1, f1, lane, y0, y1);
-  v0 = group_sum(x0 + y0);
-  v1 = group_sum(x1 + y1);
-}
-
-// The column-tile pair (kt0, kt0 + 1) of a warp for token t: fragments from act_s (zero when out of
-// range).
-template <int KIND>
-__device__ __forceinline__ void load_pair(AFrag &f0, AFrag &f1, const uint8_t *act_s, int ktiles, int t, int kt0,
-                                          int lane) {
-  if (kt0 < ktiles) f0.load(act_s + (size_t(t) * ktiles + kt0) * kActTile, lane, KIND == kKindMx, KIND == kKindInt4);
-  else f0.zero();
-  if (kt0 + 1 < ktiles) f1.load(act_s + (size_t(t) * ktiles + kt0 + 1) * kActTile, lane, KIND == kKindMx, KIND == kKindInt4);
-  else f1.zero();
-}
-
-// The chunks of a GEMV phase (kr-major: chunk (i, kr) is the (kr nrt + i)-th), split as above. The
-// warp's fragments are built once per kr for a single token and per chunk otherwise. Warp q of
-// the team that has row tile i leaves its partial in part[q][i][t][8] (stored at kr = 0, added
-// to after); row_value() adds the 4 in order, so results do not depend on timing. Returns the
-// ring position after the phase.
-template <int KIND, int NT>
-__device__ __noinline__ int consume_gemv(const Ring r, int j, const GemvPhase g, const uint8_t *act_s, const MkParams &p,
-                                         float *part) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int team = warp / kTeamWarps, q4 = warp % kTeamWarps;
-  const int c = lane & 3;
-  const int nkr = g.nkr();
-  bool good = true;
-  for (int kr = 0; kr < nkr; ++kr) {
-    const int kt0 = kr * kKr + 2 * q4;
-    const bool any = kt0 < g.ktiles, act1 = kt0 + 1 < g.ktiles;
-    AFrag f0, f1;
-    if (NT == 1) load_pair<KIND>(f0, f1, act_s, g.ktiles, 0, kt0, lane);
-    for (int i = team; i < g.nrt; i += 2) {
-      const int jj = j + kr * g.nrt + i, s = jj % r.S;
-      if (good && !mbar_wait_warp(&r.full[s], (jj / r.S) & 1, p, 1000002)) good = false;
-      if (!good) continue;
-      ctrace_c(p, jj, false);
-      float *pw = part + (size_t(q4) * g.nrt + i) * NT * 8;
-      const uint8_t *stage = r.stages + size_t(s) * kStageBytes;
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        float v0 = 0.f, v1 = 0.f;
-        if (any) {
-          if (NT > 1) load_pair<KIND>(f0, f1, act_s, g.ktiles, t, kt0, lane);
-          pair_mma<KIND>(stage, q4, act1, f0, f1, lane, v0, v1);
-        }
-        if (lane < 4) {
-          if (kr == 0) {
-            pw[t * 8 + 2 * c] = v0;
-            pw[t * 8 + 2 * c + 1] = v1;
-          } else {
-            pw[t * 8 + 2 * c] += v0;
-            pw[t * 8 + 2 * c + 1] += v1;
-          }
-        }
-      }
-      ctrace_c(p, jj, true);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&r.empty[s], 2);
-    }
-  }
-  (void)good;
-  return j + g.chunks();
-}
-
-// The value of row r8 of local row tile i for token t: the 4 warps' partials in order.
+// The value of row r of partial slot `slot` (of NS) for token t: the 8 warps' partials in order.
 template <int NT>
-__device__ __forceinline__ float row_value(const float *part, int nrt, int i, int t, int r8) {
+__device__ __forceinline__ float slot_value(const float *part, int NS, int slot, int t, int r) {
   float v = 0.f;
 #pragma unroll
-  for (int q = 0; q < kTeamWarps; ++q) v += part[((size_t(q) * nrt + i) * NT + t) * 8 + r8];
+  for (int w = 0; w < kWarps; ++w)
+    v += *reinterpret_cast<const volatile float *>(part + ((size_t(w) * NS + slot) * NT + t) * kTileRows + r);
   return v;
 }
 
-// The head (i-major: chunk (i, kr) is the (i nkr + kr)-th): split as consume_gemv, into kHeadSlots
-// partial slots used round robin; the last of the team's 4 warps to finish row tile i (a shared
-// counter) adds the partials in order, writes the fp16 logits and folds them into bmax[t]. Slot
-// reuse is safe: no warp runs more than `stages` (<= 16) chunks ahead of the slowest, which
-// releases a row tile's last chunk only after that row tile's epilogue.
-constexpr int kHeadSlots = 32;
-template <int KIND, int NT>
-__device__ __noinline__ int consume_head(const Ring r, int j, const GemvPhase g, const uint8_t *act_s, const MkParams &p,
-                                         float *part, unsigned *cnt, const float *cf, unsigned long long *bmax) {
+// The row tiles of a GEMV phase (chunk (i, kr), the (i nkr + kr)-th of the phase, holds column
+// tiles [8 kr, 8 kr + 8) of row tile rt(i)). Warp w takes column tile 8 kr + w of every chunk:
+// its weights from the stage, its activation fragments built once for the phase when one chunk
+// covers the row (nkr == 1) and a single token runs, else per chunk. A warp releases the stage as
+// soon as its tile is in registers. The warps leave their rows' partials in 2 S slots (S the ring's
+// stages), used round robin (stored at kr = 0, added to after); the last of the 8 to finish row
+// tile i (a shared counter) adds them up in warp order (results do not depend on timing) and
+// applies the epilogue. Slot reuse is safe: a warp reaches row tile i + 2S only once every warp
+// released a chunk of row tile i + S, and the last warp of row tile i finishes its epilogue before
+// it goes on to row tile i + 1. Returns the ring position after the phase.
+template <int KIND, int NT, int PH>
+__device__ __forceinline__ int consume_rows(int j, int li, const MkParams &p) {
+  const Schedule<KIND, NT> sc{p};
+  const GemvPhase g = PH == kPhQkv ? sc.qkv(li)
+                      : PH == kPhO ? sc.o(li)
+                      : PH == kPhGu ? sc.gu(li)
+                      : PH == kPhDown ? sc.down(li)
+                                      : sc.head();
+  const Ring r = ring_of(p);
+  const uint8_t *act_s = mk_smem + p.off_act;
+  float *part = reinterpret_cast<float *>(mk_smem + p.off_rows);
+  unsigned *cnt = s_rcnt;
+  const float *cf = s_cfac;
+  unsigned long long *bmax = s_bmax;
+  constexpr int TB = KIND == kKindInt8 ? kTileInt8 : (KIND == kKindInt4 ? kTileInt4 : kTileMx);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int team = warp / kTeamWarps, q4 = warp % kTeamWarps;
-  const int c = lane & 3;
+  const int gq = lane >> 2, c = lane & 3;
   const int nkr = g.nkr();
+  const bool cached = nkr == 1 && NT == 1;
   bool good = true;
-  AFrag f0, f1;
-  if (nkr == 1 && NT == 1) load_pair<KIND>(f0, f1, act_s, g.ktiles, 0, 2 * q4, lane);
-  for (int i = team; i < g.nrt && good; i += 2) {
-    const int slot = i % kHeadSlots;
-    float *pw = part + (size_t(q4) * kHeadSlots + slot) * NT * 8;
+  BFrag<KIND> bf;
+  if (cached) {
+    if (warp < g.ktiles) bf.load(act_s + size_t(warp) * kActTile, lane);
+    else bf.zero();
+  }
+  for (int i = 0; i < g.nrt && good; ++i) {
+    const int NS = 2 * r.S, slot = i % NS;
+    float *pw = part + (size_t(warp) * NS + slot) * NT * kTileRows;
     for (int kr = 0; kr < nkr; ++kr) {
       const int jj = j + i * nkr + kr, s = jj % r.S;
       if (!mbar_wait_warp(&r.full[s], (jj / r.S) & 1, p, 1000004)) { good = false; break; }
       ctrace_c(p, jj, false);
-      const int kt0 = kr * kKr + 2 * q4;
-      const bool any = kt0 < g.ktiles, act1 = kt0 + 1 < g.ktiles;
-      const uint8_t *stage = r.stages + size_t(s) * kStageBytes;
+      const int kt = kr * kKr + warp;
+      const bool on = kt < g.ktiles;
+      float vg[NT], vg8[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) vg[t] = vg8[t] = 0.f;
+      WTile<KIND> wt;
+      if (on) wt.load(r.stages + size_t(s) * r.SB + size_t(warp) * TB, lane);
+      // release the stage as soon as its bytes are in registers
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&r.empty[s], 1);
+      if (on) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          if (!cached) bf.load(act_s + (size_t(t) * g.ktiles + kt) * kActTile, lane);
+          wa_mma<KIND>(wt, bf, vg[t], vg8[t]);
+        }
+      }
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
-        float v0 = 0.f, v1 = 0.f;
-        if (any) {
-          if (nkr != 1 || NT != 1) load_pair<KIND>(f0, f1, act_s, g.ktiles, t, kt0, lane);
-          pair_mma<KIND>(stage, q4, act1, f0, f1, lane, v0, v1);
-        }
-        if (lane < 4) {
+        const float a = quad_sum(vg[t]), b = quad_sum(vg8[t]);
+        if (c == 0) {
           if (kr == 0) {
-            pw[t * 8 + 2 * c] = v0;
-            pw[t * 8 + 2 * c + 1] = v1;
+            pw[t * kTileRows + gq] = a;
+            pw[t * kTileRows + gq + 8] = b;
           } else {
-            pw[t * 8 + 2 * c] += v0;
-            pw[t * 8 + 2 * c + 1] += v1;
+            pw[t * kTileRows + gq] += a;
+            pw[t * kTileRows + gq + 8] += b;
           }
         }
       }
       if (kr + 1 == nkr) {
-        // count this warp in; the team's last adds the partials up
         __syncwarp();
         unsigned last = 0;
         if (lane == 0) {
           __threadfence_block();
-          last = atomicAdd(&cnt[slot], 1u) == unsigned(kTeamWarps - 1);
+          last = atomicAdd(&cnt[slot], 1u) == unsigned(kWarps - 1);
         }
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
           __threadfence_block();
-          const int row0 = (g.rt0 + i) * 8;
-          for (int q = lane; q < NT * 8; q += 32) {
-            const int t = q / 8, row = row0 + q % 8;
-            float v = 0.f;
-#pragma unroll
-            for (int w = 0; w < kTeamWarps; ++w)
-              v += *reinterpret_cast<volatile float *>(part + (size_t(w) * kHeadSlots + slot) * NT * 8 + q);
-            v *= cf[t];
-            if (p.head_scale) v *= p.head_scale[row];
-            const uint16_t hb = __half_as_ushort(__float2half_rn(v));
-            if (row < p.V) {
-              if (p.logits) p.logits[size_t(t) * p.V + row] = hb;
-              atomicMax(&bmax[t], argmax_key(hb, row));
+          const int rt = g.rt(i);
+          const float half = KIND == kKindMx ? 0.5f : 1.f;  // the doubled e2m1 values (mxfp4.go:90)
+          if (PH == kPhGu) {
+            const float *gsc = *reinterpret_cast<const float *const volatile *>(&s_rscale);
+            for (int q = lane; q < NT * 8; q += 32) {
+              const int t = q / 8, r8 = q % 8, grow = rt * kTileRows + r8;
+              float gv = slot_value<NT>(part, NS, slot, t, r8) * half * cf[t];
+              float uv = slot_value<NT>(part, NS, slot, t, r8 + 8) * half * cf[t];
+              if (gsc) { gv *= gsc[grow]; uv *= gsc[grow + 8]; }
+              // blocks.SiLU: x / (1 + exp(-x)) (internal/llm/blocks/blocks.go:395-399)
+              p.h[size_t(t) * p.F + rt * 8 + r8] = gv / (1.0f + expf(-gv)) * uv;
+            }
+          } else {
+            const int W = (p.H + 2 * p.KV) * p.hd;
+            const int rows = PH == kPhQkv ? W : PH == kPhHead ? p.V : p.D;
+            const float *scale = *reinterpret_cast<const float *const volatile *>(&s_rscale);
+            const float *bias = *reinterpret_cast<const float *const volatile *>(&s_rbias);
+            for (int q = lane; q < NT * kTileRows; q += 32) {
+              const int t = q / kTileRows, row = rt * kTileRows + q % kTileRows;
+              if (row >= rows) continue;
+              float v = slot_value<NT>(part, NS, slot, t, q % kTileRows) * half * cf[t];
+              if (scale) v *= scale[row];
+              if (bias) v += bias[row];
+              if (PH == kPhHead) {
+                const uint16_t hb = __half_as_ushort(__float2half_rn(v));
+                if (p.logits) p.logits[size_t(t) * p.V + row] = hb;
+                atomicMax(&bmax[t], argmax_key(hb, row));
+              } else if (PH == kPhQkv) {
+                p.qkv[size_t(t) * W + row] = v;
+              } else {
+                float *yp = p.x + size_t(t) * p.D + row;
+                *yp = __ldcg(yp) + v;
+              }
             }
           }
           if (lane == 0) cnt[slot] = 0u;
         }
       }
       ctrace_c(p, jj, true);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&r.empty[s], 2);
     }
   }
   (void)good;
   return j + g.chunks();
 }
 
+// ---- activations built by every consumer CTA ------------------------------------------------
+// Quantises K groups of 32 at once with quant32's arithmetic (hi = round_even(v * 127 / max), lo
+// the residual at 1/256 of the scale, S = max / 127, Xq = sum(hi + lo / 256)): value v[k] of lane
+// `lane` is column lane of group `slot` of column tile kt0 + k of token row `at` (act_s + t * ktiles
+// tiles); groups with k >= nk are skipped. The K reductions are interleaved.
+template <int K>
+__device__ __forceinline__ void quant_tiles(const float (&v)[K], uint8_t *at, int kt0, int nk, int slot, int lane) {
+  float m[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) m[k] = fabsf(v[k]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+#pragma unroll
+    for (int k = 0; k < K; ++k) m[k] = fmaxf(m[k], __shfl_xor_sync(0xffffffffu, m[k], o));
+  int hq[K], lq[K], s[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    hq[k] = 0;
+    lq[k] = 0;
+    if (m[k] > 0.f) {
+      const float inv = 127.0f / m[k];
+      const float S = m[k] / 127.0f;
+      const float h = rintf(v[k] * inv);
+      const float rr = fmaf(-h, S, v[k]);
+      hq[k] = int(h);
+      lq[k] = int(fminf(fmaxf(rintf(rr * (256.0f * inv)), -127.f), 127.f));
+    }
+    s[k] = hq[k] * 256 + lq[k];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+#pragma unroll
+    for (int k = 0; k < K; ++k) s[k] += __shfl_xor_sync(0xffffffffu, s[k], o);
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    if (k >= nk) continue;
+    uint8_t *tile = at + size_t(kt0 + k) * kActTile;
+    tile[slot * 64 + lane] = uint8_t(int8_t(hq[k]));
+    tile[slot * 64 + 32 + lane] = uint8_t(int8_t(lq[k]));
+    if (lane == 0)
+      *reinterpret_cast<float2 *>(tile + kGroupsPerTile * 64 + slot * 8) =
+          make_float2(m[k] > 0.f ? m[k] / 127.0f : 0.f, float(s[k]) * (1.0f / 256.0f));
+  }
+}
+
+// The embedding of token `tok`, column col, as the reference's fp16 table holds it (the tied case
+// decodes the head's tile).
+template <int KIND>
+__device__ __forceinline__ float embed_value(const MkParams &p, int tok, int col) {
+  if (p.embed) return __half2float(__ushort_as_half(p.embed[size_t(tok) * p.D + col]));
+  const float v = tile_value(p.head, p.head_scale, KIND, p.kt_d, tile_bytes_of<KIND>(), tok, col);
+  return __half2float(__float2half_rn(v));
+}
+
+constexpr int kMaxKt = 24;  // column tiles of a GEMV input the step supports (F <= 6144)
+
+// Activation tiles of NT tokens for a GEMV whose input is n columns: x = src[t][col] (EMB: the
+// embedding of the step's token, also stored to src for the column tiles this CTA owns), times
+// the norm weight nw when there is one, quantised per group of 32 into act_s. Warp w takes group w
+// of every column tile, all of a token's loads at once. With a norm, sq_s[t][w] gets the warp's
+// sum of (x / scale)^2 in double (the reference sums the squares in float64, milcpu reduce_mean
+// ops.go:861-920; only the order differs).
+template <int KIND, int NT, bool EMB>
+__device__ __forceinline__ void build_act(float *src, int ld, int n, const float *nw, float scale, const MkParams &p) {
+  uint8_t *act_s = mk_smem + p.off_act;
+  double *sq_s = reinterpret_cast<double *>(mk_smem + p.off_sq);
+  const StepTok *toks = s_toks;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = n / kTileCols;
+  int own0 = 0, own1 = 0;
+  if (EMB) my_units(kt, own0, own1);
+  const float inv = scale == 1.f ? 1.f : 1.f / scale;
+  for (int t = 0; t < NT; ++t) {
+    float x[kMaxKt];
+    double ss = 0;
+#pragma unroll
+    for (int k = 0; k < kMaxKt; ++k) {
+      const int col = k * kTileCols + warp * 32 + lane;
+      x[k] = 0.f;
+      if (k < kt) {
+        if (EMB) {
+          x[k] = embed_value<KIND>(p, toks[t].token, col);
+          if (k >= own0 && k < own1) src[size_t(t) * ld + col] = x[k];
+        } else {
+          x[k] = __ldcg(src + size_t(t) * ld + col);
+        }
+      }
+    }
+    if (nw) {
+#pragma unroll
+      for (int k = 0; k < kMaxKt; ++k) {
+        if (k < kt) {
+          const float xs = scale == 1.f ? x[k] : x[k] * inv;
+          ss += double(xs * xs);
+          x[k] *= nw[k * kTileCols + warp * 32 + lane];
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) sq_s[t * kWarps + warp] = ss;
+    }
+    uint8_t *at = act_s + size_t(t) * kt * kActTile;
+#pragma unroll
+    for (int k0 = 0; k0 < kMaxKt; k0 += 8) {
+      if (k0 < kt) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = x[k0 + k];
+        quant_tiles<8>(v, at, k0, min(8, kt - k0), warp, lane);
+      }
+    }
+  }
+}
+
+// cf[t] = r / scale for a normed input of n columns (r = float32(1 / sqrt(float64(mean) + eps16)),
+// milcpu's rsqrt, ops.go:181-189), from the warps' sums build_act left in sq_s; 1 without a norm.
+template <int NT>
+__device__ __forceinline__ void norm_factors_s(const MkParams &p, int n, float scale, float eps16, bool normed) {
+  float *cf = s_cfac;
+  const double *sq_s = reinterpret_cast<const double *>(mk_smem + p.off_sq);
+  if (threadIdx.x < NT) {
+    const int t = threadIdx.x;
+    float f = 1.f;
+    if (normed) {
+      double s = 0;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) s += sq_s[t * kWarps + w];
+      const float ms = float(s / double(n));
+      const float r = float(1.0 / sqrt(double(ms) + double(eps16)));
+      f = r * (1.f / scale);
+    }
+    cf[t] = f;
+  }
+}
+
+// The attention output of NT tokens, merged from the units' per-split partials (Flash-Decoding's
+// merge, paged.go:227-310, with gpt-oss's sink in the denominator, gptoss/build.go:256-285) and
+// quantised into act_s as the o projection's input. A warp takes one (token, head): lane s holds
+// split s's weight, lane l accumulates elements [E l, E l + E) over the splits in split order, and
+// each group of 32 columns (32 / E lanes) is quantised with quant32's arithmetic.
+template <int NT, int HD>
+__device__ __forceinline__ void merge_attn(const MkParams &p, const float *sinks) {
+  uint8_t *act_s = mk_smem + p.off_act;
+  constexpr int E = HD / 32;   // elements a lane: 4 (hd 128) or 2 (hd 64)
+  constexpr int GL = 32 / E;   // lanes of one group of 32 columns
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.splits;      // <= 32 on this path
+  for (int th = warp; th < NT * p.H; th += kWarps) {
+    const int t = th / p.H, h = th % p.H;
+    const float *ml = p.part_ml + (size_t(t) * p.H + h) * S * 2;
+    float m0 = -INFINITY, l0 = 0.f;
+    if (lane < S) { m0 = __ldcg(ml + 2 * lane); l0 = __ldcg(ml + 2 * lane + 1); }
+    const float *po = p.part_o + (size_t(t) * p.H + h) * S * HD + lane * E;
+    constexpr int CH = 20;  // splits loaded at once (up to 20: the partials take one round trip)
+    float o[CH][E];
+    auto load = [&](int s0) {
+#pragma unroll
+      for (int u = 0; u < CH; ++u) {
+        if (s0 + u < S) {
+          if constexpr (E == 4) {
+            const float4 q = __ldcg(reinterpret_cast<const float4 *>(po + size_t(s0 + u) * HD));
+            o[u][0] = q.x; o[u][1] = q.y; o[u][2] = q.z; o[u][3] = q.w;
+          } else {
+            const float2 q = __ldcg(reinterpret_cast<const float2 *>(po + size_t(s0 + u) * HD));
+            o[u][0] = q.x; o[u][1] = q.y;
+          }
+        }
+      }
+    };
+    load(0);  // before the weights, so both loads are in flight together
+    float M = sinks ? sinks[h] : -INFINITY;
+    M = fmaxf(M, l0 > 0.f ? m0 : -INFINITY);
+    M = warp_max(M);
+    const float w0 = l0 > 0.f ? expf(m0 - M) : 0.f;
+    float Ls = warp_sum(l0 * w0);
+    if (sinks) Ls += expf(sinks[h] - M);
+    const float invl = Ls > 0.f ? 1.f / Ls : 0.f;
+    float acc[E];
+#pragma unroll
+    for (int k = 0; k < E; ++k) acc[k] = 0.f;
+    for (int s0 = 0; s0 < S; s0 += CH) {
+      if (s0 > 0) load(s0);
+#pragma unroll
+      for (int u = 0; u < CH; ++u) {
+        const float ws = __shfl_sync(0xffffffffu, w0, (s0 + u) & 31);
+        if (s0 + u < S) {
+#pragma unroll
+          for (int k = 0; k < E; ++k) acc[k] = fmaf(o[u][k], ws, acc[k]);
+        }
+      }
+    }
+    // quantise: the group of 32 columns of this lane is lanes [GL (lane / GL), + GL)
+    float v[E], m = 0.f;
+#pragma unroll
+    for (int k = 0; k < E; ++k) {
+      v[k] = acc[k] * invl;
+      m = fmaxf(m, fabsf(v[k]));
+    }
+#pragma unroll
+    for (int o = GL / 2; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    int sum = 0;
+    int8_t hq[E], lq[E];
+    float S32 = 0.f;
+#pragma unroll
+    for (int k = 0; k < E; ++k) {
+      hq[k] = 0;
+      lq[k] = 0;
+      if (m > 0.f) {
+        const float inv = 127.0f / m;
+        S32 = m / 127.0f;
+        const float hh = rintf(v[k] * inv);
+        const float rr = fmaf(-hh, S32, v[k]);
+        hq[k] = int8_t(hh);
+        lq[k] = int8_t(fminf(fmaxf(rintf(rr * (256.0f * inv)), -127.f), 127.f));
+      }
+      sum += int(hq[k]) * 256 + int(lq[k]);
+    }
+#pragma unroll
+    for (int o = GL / 2; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const int col0 = h * HD + lane * E, G = col0 / 32, within = col0 % 32;
+    uint8_t *tile = act_s + (size_t(t) * p.kt_o + G / kGroupsPerTile) * kActTile;
+    const int gi = G % kGroupsPerTile;
+#pragma unroll
+    for (int k = 0; k < E; ++k) {
+      tile[gi * 64 + within + k] = uint8_t(hq[k]);
+      tile[gi * 64 + 32 + within + k] = uint8_t(lq[k]);
+    }
+    if (within == 0)
+      *reinterpret_cast<float2 *>(tile + kGroupsPerTile * 64 + gi * 8) = make_float2(S32, float(sum) * (1.0f / 256.0f));
+  }
+}
+
 // The attention of one (token, kv head, split) unit (all 8 warps): q/k norms and RoPE of the heads it
 // needs (one warp a head; the new key and value of position P in float32, as the reference's step
 // rows are, written to the cache as fp16 by the unit that holds P), then an online softmax over its
-// cached keys, which arrive from the ring in chunks, by 32 groups of 8 lanes; partials out, and
-// the last split of (token, kv head) to arrive merges them (with the sink) and quantises the
-// heads' outputs for the o projection. Returns false when a wait gave up.
+// cached keys, which arrive from the ring in chunks, by 32 groups of 8 lanes; the split's (m, l, o)
+// partials go to global memory, merged by the o projection's consumers (merge_attn).
 template <int HD, int REP>
-__device__ __noinline__ int attention_unit(const Ring r, int j, const AttPhase a, const MkParams &p, const MkLayer &L, int t,
-                               int kvh, int s, uint8_t *scratch, uint8_t *act_next) {
+__device__ __forceinline__ int attention_unit(int j, const AttPhase a, const MkParams &p, const MkLayer &L, int t,
+                                           int kvh, int s) {
+  const Ring r = ring_of(p);
+  const StepTok *toks = s_toks;
+  uint8_t *scratch = mk_smem + p.off_att;
   constexpr int E = HD / 8;
   float *qs = reinterpret_cast<float *>(scratch);  // [REP][HD]
   float *kn = qs + REP * HD;                         // [HD]
@@ -731,12 +790,11 @@ __device__ __noinline__ int attention_unit(const Ring r, int j, const AttPhase a
   float *wm = vn + HD;                               // [8][REP]
   float *wl = wm + kWarps * REP;                     // [8][REP]
   float *wo = wl + kWarps * REP;                     // [8][REP][HD]
-  int *flag = reinterpret_cast<int *>(wo + kWarps * REP * HD);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grp = threadIdx.x >> 3, l8 = threadIdx.x & 7;
   const int li = int(&L - p.L);
   utrace(p, li, 0);
-  const StepTok tk = p.toks[t];
+  const StepTok tk = toks[t];
   const int P = tk.pos;
   const int lo = L.window > 0 ? max(0, P - L.window + 1) : 0;
   const int n = P - lo + 1;
@@ -752,9 +810,18 @@ __device__ __noinline__ int attention_unit(const Ring r, int j, const AttPhase a
     const float *src = is_q ? row + size_t(kvh * REP + task) * HD : row + size_t(p.H + kvh) * HD;
     const float *nw = is_q ? L.q_norm : L.k_norm;
     constexpr int E2 = HD / 32;
-    float x[E2];
+    const uint32_t *rt = p.rope + size_t(P) * (HD / 2);
+    float x[E2], nwv[E2], vv[E2];
+    uint32_t cs[E2];
+    // every load of the task first (one round trip)
 #pragma unroll
-    for (int k = 0; k < E2; ++k) x[k] = __ldcg(src + lane + 32 * k);
+    for (int k = 0; k < E2; ++k) {
+      const int e = lane + 32 * k;
+      x[k] = __ldcg(src + e);
+      nwv[k] = nw ? nw[e] : 1.f;
+      cs[k] = rt[e < HD / 2 ? e : e - HD / 2];
+      vv[k] = is_q ? 0.f : __ldcg(row + size_t(p.H + p.KV + kvh) * HD + e);
+    }
     if (nw) {
       const float inv = p.sc == 1.f ? 1.f : 1.f / p.sc;
       double ss = 0;
@@ -768,17 +835,14 @@ __device__ __noinline__ int attention_unit(const Ring r, int j, const AttPhase a
       const float ms = float(ss / double(HD));
       const float rr = float(1.0 / sqrt(double(ms) + double(p.eps)));
 #pragma unroll
-      for (int k = 0; k < E2; ++k) x[k] = __fmul_rn(__fmul_rn(x[k], rr), nw[lane + 32 * k]);
+      for (int k = 0; k < E2; ++k) x[k] = __fmul_rn(__fmul_rn(x[k], rr), nwv[k]);
     }
-    const uint32_t *rt = p.rope + size_t(P) * (HD / 2);
     float y[E2];
 #pragma unroll
     for (int k = 0; k < E2; ++k) {
       const int e = lane + 32 * k;
-      const int jr = e < HD / 2 ? e : e - HD / 2;
-      const uint32_t cs = rt[jr];
-      const float cv = __half2float(__ushort_as_half(uint16_t(cs & 0xffff)));
-      const float sv = __half2float(__ushort_as_half(uint16_t(cs >> 16)));
+      const float cv = __half2float(__ushort_as_half(uint16_t(cs[k] & 0xffff)));
+      const float sv = __half2float(__ushort_as_half(uint16_t(cs[k] >> 16)));
       const int kp = e < HD / 2 ? k + (HD / 64) : k - (HD / 64);
       const float rot = e < HD / 2 ? -x[kp] : x[kp];
       y[k] = __fadd_rn(__fmul_rn(x[k], cv), __fmul_rn(rot, sv));
@@ -787,15 +851,13 @@ __device__ __noinline__ int attention_unit(const Ring r, int j, const AttPhase a
 #pragma unroll
       for (int k = 0; k < E2; ++k) qs[task * HD + lane + 32 * k] = y[k];
     } else {
-      const float *vsrc = row + size_t(p.H + p.KV + kvh) * HD;
 #pragma unroll
       for (int k = 0; k < E2; ++k) {
         const int e = lane + 32 * k;
-        const float v = __ldcg(vsrc + e);
         kn[e] = y[k];
-        vn[e] = v;
+        vn[e] = vv[k];
         L.kc[base + size_t(P) * HD + e] = __half_as_ushort(__float2half_rn(y[k]));
-        L.vc[base + size_t(P) * HD + e] = __half_as_ushort(__float2half_rn(v));
+        L.vc[base + size_t(P) * HD + e] = __half_as_ushort(__float2half_rn(vv[k]));
       }
     }
   }
@@ -837,7 +899,7 @@ __device__ __noinline__ int attention_unit(const Ring r, int j, const AttPhase a
     const int jj = j + c, st = jj % r.S;
     if (!mbar_wait_warp(&r.full[st], (jj / r.S) & 1, p, 1000003)) { good = false; break; }
     ctrace_c(p, jj, false);
-    const uint8_t *stage = r.stages + size_t(st) * kStageBytes;
+    const uint8_t *stage = r.stages + size_t(st) * r.SB;
     const int key0 = a.k0 + c * a.kc, nkeys = min(a.kc, a.kc1 - key0);
     const uint16_t *ks = reinterpret_cast<const uint16_t *>(stage);
     const uint16_t *vs = ks + size_t(nkeys) * HD;
@@ -910,239 +972,148 @@ __device__ __noinline__ int attention_unit(const Ring r, int j, const AttPhase a
     if (e == 0) { p.part_ml[pi * 2] = M; p.part_ml[pi * 2 + 1] = Ls; }
     p.part_o[pi * HD + e] = acc;
   }
-  __threadfence();
-  csync();
+  csync();  // the scratch is reused by the CTA's next unit
   utrace(p, li, 4);
-  if (threadIdx.x == 0) {
-    const unsigned old = atomicAdd(&p.cnt[t * p.KV + kvh], 1u);
-    *flag = old == unsigned(p.splits - 1);
-  }
-  csync();
-  utrace(p, li, 5);
-  if (!*flag) return j;
-  __threadfence();
-  float *wsp = wo;               // [REP][64] split weights
-  float *invl = wsp + REP * 64;  // [REP]
-  float *ov = invl + REP;        // [REP][HD]
-  if (warp < REP) {
-    const int rr = warp, h = kvh * REP + rr;
-    const float *ml = p.part_ml + (size_t(t) * p.H + h) * p.splits * 2;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    if (lane < p.splits) { m0 = __ldcg(ml + 2 * lane); l0 = __ldcg(ml + 2 * lane + 1); }
-    if (lane + 32 < p.splits) { m1 = __ldcg(ml + 2 * (lane + 32)); l1 = __ldcg(ml + 2 * (lane + 32) + 1); }
-    float M = L.sinks ? L.sinks[h] : -INFINITY;
-    M = fmaxf(M, l0 > 0.f ? m0 : -INFINITY);
-    M = fmaxf(M, l1 > 0.f ? m1 : -INFINITY);
-    M = warp_max(M);
-    const float w0 = l0 > 0.f ? expf(m0 - M) : 0.f, w1 = l1 > 0.f ? expf(m1 - M) : 0.f;
-    float Ls = warp_sum(l0 * w0 + l1 * w1);
-    if (L.sinks) Ls += expf(L.sinks[h] - M);
-    if (lane < p.splits) wsp[rr * 64 + lane] = w0;
-    if (lane + 32 < p.splits) wsp[rr * 64 + lane + 32] = w1;
-    if (lane == 0) invl[rr] = Ls > 0.f ? 1.f / Ls : 0.f;
-  }
-  csync();
-  for (int idx = threadIdx.x; idx < REP * HD; idx += kMkThreads) {
-    const int rr = idx / HD, e = idx % HD, h = kvh * REP + rr;
-    const float *po = p.part_o + (size_t(t) * p.H + h) * p.splits * HD + e;
-    float acc = 0.f;
-    for (int sp = 0; sp < p.splits; ++sp) acc = fmaf(__ldcg(po + size_t(sp) * HD), wsp[rr * 64 + sp], acc);
-    ov[idx] = acc * invl[rr];
-  }
-  csync();
-  utrace(p, li, 6);
-  uint8_t *at = act_next + size_t(t) * p.kt_o * kActTile;
-  for (int gq = warp; gq < REP * HD / 32; gq += kWarps) {
-    const int grp32 = (kvh * REP * HD) / 32 + gq;
-    quant32(ov[gq * 32 + lane], at + size_t(grp32 / kGroupsPerTile) * kActTile, grp32 % kGroupsPerTile, lane);
-  }
-  if (threadIdx.x == 0) p.cnt[t * p.KV + kvh] = 0u;
-  utrace(p, li, 7);
   (void)good;
+  return j;
+}
+
+// The row scale and bias of phase ph of layer li for the epilogues (thread 0; a csync follows).
+__device__ __forceinline__ void set_rows(const MkParams &p, int ph, int li) {
+  if (threadIdx.x != 0) return;
+  const MkLayer &L = p.L[li];
+  s_rscale = ph == kPhQkv ? L.qkv_scale : ph == kPhO ? L.o_scale : ph == kPhGu ? L.gu_scale
+           : ph == kPhDown ? L.down_scale : p.head_scale;
+  s_rbias = ph == kPhQkv ? L.qkv_bias : ph == kPhO ? L.o_bias : nullptr;
+}
+
+// The phases of the step, each out of line and entered from a kernel loop that keeps only the layer
+// and the ring position, so that each is allocated its own registers. Each returns the ring
+// position after it; its grid barrier follows in the kernel.
+template <int KIND, int NT, int HD, int REP>
+__device__ __noinline__ int ph_qkv(const MkParams &p, int li, int j) {
+  // the input norm (layer 0: of the embedding, which this phase also stores as x)
+  if (li == 0) build_act<KIND, NT, true>(p.x, p.D, p.D, p.in_norm0, p.sc_in0, p);
+  else build_act<KIND, NT, false>(p.x, p.D, p.D, p.L[li - 1].next_norm, p.sc, p);
+  csync();
+  norm_factors_s<NT>(p, p.D, li == 0 ? p.sc_in0 : p.sc, li == 0 ? p.eps_in0 : p.eps, true);
+  set_rows(p, kPhQkv, li);
+  csync();
+  mark(p, 0);
+  j = consume_rows<KIND, NT, kPhQkv>(j, li, p);
+  mark(p, 1);
+  return j;
+}
+
+// This CTA's attention units write their partials.
+template <int KIND, int NT, int HD, int REP>
+__device__ __noinline__ int ph_att(const MkParams &p, int li, int j) {
+  const Schedule<KIND, NT> sc{p};
+  int a0, a1;
+  sc.units(a0, a1);
+  mark(p, 0);
+  for (int u = a0; u < a1; ++u) {
+    const int t = u / (p.KV * p.splits), kvh = (u / p.splits) % p.KV, s = u % p.splits;
+    j = attention_unit<HD, REP>(j, sc.att(li, u), p, p.L[li], t, kvh, s);
+  }
+  mark(p, 1);
+  return j;
+}
+
+// The o projection + residual: the heads' outputs merged from the units' partials.
+template <int KIND, int NT, int HD, int REP>
+__device__ __noinline__ int ph_o(const MkParams &p, int li, int j) {
+  merge_attn<NT, HD>(p, p.L[li].sinks);
+  if (threadIdx.x < NT) s_cfac[threadIdx.x] = 1.f;
+  set_rows(p, kPhO, li);
+  csync();
+  mark(p, 0);
+  j = consume_rows<KIND, NT, kPhO>(j, li, p);
+  mark(p, 1);
+  return j;
+}
+
+// gate/up + SiLU after the post-attention norm.
+template <int KIND, int NT, int HD, int REP>
+__device__ __noinline__ int ph_gu(const MkParams &p, int li, int j) {
+  utrace(p, li, 5);
+  build_act<KIND, NT, false>(p.x, p.D, p.D, p.L[li].post_norm, p.sc, p);
+  utrace(p, li, 6);
+  csync();
+  norm_factors_s<NT>(p, p.D, p.sc, p.eps, true);
+  set_rows(p, kPhGu, li);
+  csync();
+  utrace(p, li, 7);
+  mark(p, 0);
+  j = consume_rows<KIND, NT, kPhGu>(j, li, p);
+  mark(p, 1);
+  return j;
+}
+
+// down + residual.
+template <int KIND, int NT, int HD, int REP>
+__device__ __noinline__ int ph_down(const MkParams &p, int li, int j) {
+  build_act<KIND, NT, false>(p.h, p.F, p.F, nullptr, 1.f, p);
+  if (threadIdx.x < NT) s_cfac[threadIdx.x] = 1.f;
+  set_rows(p, kPhDown, li);
+  csync();
+  mark(p, 0);
+  j = consume_rows<KIND, NT, kPhDown>(j, li, p);
+  mark(p, 1);
+  return j;
+}
+
+// The head: the final norm, fp16 logits and this CTA's greedy keys (chat/sample.go:80-88).
+template <int KIND, int NT, int HD, int REP>
+__device__ __noinline__ int ph_head(const MkParams &p, int j) {
+  build_act<KIND, NT, false>(p.x, p.D, p.D, p.L[p.layers - 1].next_norm, p.sc_head, p);
+  if (threadIdx.x < NT) s_bmax[threadIdx.x] = 0ull;
+  csync();
+  norm_factors_s<NT>(p, p.D, p.sc_head, p.eps_head, true);
+  set_rows(p, kPhHead, 0);
+  csync();
+  mark(p, 0);
+  j = consume_rows<KIND, NT, kPhHead>(j, 0, p);
+  csync();
+  mark(p, 1);
+  if (threadIdx.x < NT)
+    atomicMax(&p.amax[threadIdx.x * kAmaxSlots + (blockIdx.x % kAmaxSlots)], s_bmax[threadIdx.x]);
   return j;
 }
 
 template <int KIND, int NT, int HD, int REP>
 __global__ void __launch_bounds__(kMkBlock, 1) mk_kernel(const __grid_constant__ MkParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ float cfac[kMkMaxTok];
-  __shared__ unsigned long long bmax[kMkMaxTok];
-  __shared__ unsigned hcnt[kHeadSlots];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  Ring r;
-  r.S = p.stages;
-  r.stages = smem;
-  r.full = reinterpret_cast<uint64_t *>(smem + p.off_bar);
-  r.empty = r.full + p.stages;
-  uint8_t *act_s = smem + p.off_act;
-  float *rows_s = reinterpret_cast<float *>(smem + p.off_rows);
-  uint8_t *att_s = smem + p.off_att;
   if (threadIdx.x == 0) {
+    const Ring r = ring_of(p);
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&r.full[s], 1);
-      mbar_init(&r.empty[s], kWarps);  // released by arrivals adding up to 8: 1 a warp (attention), 2 a warp of a team (GEMV)
+      mbar_init(&r.empty[s], kWarps);  // released by the 8 consumer warps
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (threadIdx.x < 2 * kMaxStages) s_rcnt[threadIdx.x] = 0u;
+  if (threadIdx.x < NT) s_toks[threadIdx.x] = p.toks[threadIdx.x];
+  if (threadIdx.x == 0) s_prod = Prod{0, 0, 0, 0};
   __syncthreads();
-  if (warp == kProducerWarp) {
-    if (lane == 0) producer<KIND, NT>(r, p);
-    return;
-  }
-  // ---------------- consumers: threads 0..255 ----------------
+  if (threadIdx.x == 0) try_issue(p);
   const long long c_t0 = clock64();
-  if (threadIdx.x == 0) s_cwait = 0;
-  unsigned epoch = 0;
-  const int Gd = p.D / 32, Gf = p.F / 32;
-  const int W = (p.H + 2 * p.KV) * HD;
-  const Schedule<KIND, NT> sc{p};
+  if (threadIdx.x == 0) { s_cwait = 0; s_epoch = 0; }
   int j = 0;  // ring position
-  int cur = 0;
-  // ---- embed: x and its quantised form for layer 0's input norm
-  {
-    int u0, u1;
-    my_units(NT * Gd, u0, u1);
-    for (int u = u0 + warp; u < u1; u += kWarps) {
-      const int t = u / Gd, gq = u % Gd, col = gq * 32 + lane;
-      const int tok = p.toks[t].token;
-      float v;
-      if (p.embed) {
-        v = __half2float(__ushort_as_half(p.embed[size_t(tok) * p.D + col]));
-      } else {
-        v = tile_value(p.head, p.head_scale, KIND, p.kt_d, tile_bytes_of<KIND>(), tok, col);
-        v = __half2float(__float2half_rn(v));
-      }
-      p.x[size_t(t) * p.D + col] = v;
-      quant_norm32(v, p.in_norm0[col], p.sc_in0, p.act[cur] + size_t(t) * p.kt_d * kActTile,
-                   p.sq + size_t(t) * Gd, gq, lane);
-    }
-  }
-  if (!grid_sync(p, epoch)) return;
   for (int li = 0; li < p.layers; ++li) {
-    const MkLayer &L = p.L[li];
-    // ---- qkv
-    {
-      load_act<NT>(act_s, p.act[cur], p.kt_d);
-      norm_factors<NT>(cfac, p.sq, Gd, p.D, li == 0 ? p.sc_in0 : p.sc, li == 0 ? p.eps_in0 : p.eps);
-      csync();
-      mark(p, epoch, 0);
-      const GemvPhase g = sc.qkv(li);
-      j = consume_gemv<KIND, NT>(r, j, g, act_s, p, rows_s);
-      csync();
-      mark(p, epoch, 1);
-      for (int idx = threadIdx.x; idx < g.nrt * 8 * NT; idx += kMkThreads) {
-        const int t = idx % NT, rr = idx / NT, i = rr / 8, r8 = rr % 8, row = (g.rt0 + i) * 8 + r8;
-        if (row >= W) continue;
-        float v = row_value<NT>(rows_s, g.nrt, i, t, r8) * cfac[t];
-        if (L.qkv_scale) v *= L.qkv_scale[row];
-        if (L.qkv_bias) v += L.qkv_bias[row];
-        p.qkv[size_t(t) * W + row] = v;
-      }
-    }
-    if (!grid_sync(p, epoch)) return;
-    // ---- attention
-    {
-      int a0, a1;
-      sc.units(a0, a1);
-      mark(p, epoch, 0);
-      for (int u = a0; u < a1; ++u) {
-        const int t = u / (p.KV * p.splits), kvh = (u / p.splits) % p.KV, s = u % p.splits;
-        j = attention_unit<HD, REP>(r, j, sc.att(li, u), p, L, t, kvh, s, att_s, p.act[cur ^ 1]);
-        csync();
-      }
-      mark(p, epoch, 1);
-    }
-    if (!grid_sync(p, epoch)) return;
-    cur ^= 1;
-    // ---- o projection + residual, quantised for the post-attention norm
-    {
-      load_act<NT>(act_s, p.act[cur], p.kt_o);
-      csync();
-      mark(p, epoch, 0);
-      const GemvPhase g = sc.o(li);
-      j = consume_gemv<KIND, NT>(r, j, g, act_s, p, rows_s);
-      csync();
-      mark(p, epoch, 1);
-      const int u0 = g.rt0 / 4, nu = g.nrt / 4;
-      for (int wu = warp; wu < nu * NT; wu += kWarps) {
-        const int ul = wu / NT, t = wu % NT, row = (u0 + ul) * 32 + lane;
-        float v = row_value<NT>(rows_s, g.nrt, ul * 4 + lane / 8, t, lane % 8);
-        if (L.o_scale) v *= L.o_scale[row];
-        if (L.o_bias) v += L.o_bias[row];
-        float *xp = p.x + size_t(t) * p.D + row;
-        const float xn = __ldcg(xp) + v;
-        *xp = xn;
-        quant_norm32(xn, L.post_norm[row], p.sc, p.act[cur ^ 1] + size_t(t) * p.kt_d * kActTile,
-                     p.sq + size_t(t) * Gd, u0 + ul, lane);
-      }
-    }
-    if (!grid_sync(p, epoch)) return;
-    cur ^= 1;
-    // ---- gate/up + SiLU, quantised for down
-    {
-      load_act<NT>(act_s, p.act[cur], p.kt_d);
-      norm_factors<NT>(cfac, p.sq, Gd, p.D, p.sc, p.eps);
-      csync();
-      mark(p, epoch, 0);
-      const GemvPhase g = sc.gu(li);
-      j = consume_gemv<KIND, NT>(r, j, g, act_s, p, rows_s);
-      csync();
-      mark(p, epoch, 1);
-      const int u0 = g.rt0 / 8, nu = g.nrt / 8;
-      for (int wu = warp; wu < nu * NT; wu += kWarps) {
-        const int ul = wu / NT, t = wu % NT;
-        const int rtl = ul * 8 + lane / 4, r8 = lane % 4;
-        const int grow = (g.rt0 + rtl) * 8 + r8, urow = grow + 4;
-        float gv = row_value<NT>(rows_s, g.nrt, rtl, t, r8) * cfac[t];
-        float uv = row_value<NT>(rows_s, g.nrt, rtl, t, r8 + 4) * cfac[t];
-        if (L.gu_scale) { gv *= L.gu_scale[grow]; uv *= L.gu_scale[urow]; }
-        // blocks.SiLU: x / (1 + exp(-x)) (internal/llm/blocks/blocks.go:395-399)
-        const float hv = gv / (1.0f + expf(-gv)) * uv;
-        const int gq = u0 + ul;
-        quant32(hv, p.act[cur ^ 1] + (size_t(t) * p.kt_f + gq / kGroupsPerTile) * kActTile, gq % kGroupsPerTile, lane);
-      }
-    }
-    if (!grid_sync(p, epoch)) return;
-    cur ^= 1;
-    // ---- down + residual, quantised for the next norm
-    {
-      load_act<NT>(act_s, p.act[cur], p.kt_f);
-      csync();
-      mark(p, epoch, 0);
-      const GemvPhase g = sc.down(li);
-      j = consume_gemv<KIND, NT>(r, j, g, act_s, p, rows_s);
-      csync();
-      mark(p, epoch, 1);
-      const int u0 = g.rt0 / 4, nu = g.nrt / 4;
-      for (int wu = warp; wu < nu * NT; wu += kWarps) {
-        const int ul = wu / NT, t = wu % NT, row = (u0 + ul) * 32 + lane;
-        float v = row_value<NT>(rows_s, g.nrt, ul * 4 + lane / 8, t, lane % 8);
-        if (L.down_scale) v *= L.down_scale[row];
-        float *xp = p.x + size_t(t) * p.D + row;
-        const float xn = __ldcg(xp) + v;
-        *xp = xn;
-        quant_norm32(xn, L.next_norm[row], p.sc, p.act[cur ^ 1] + size_t(t) * p.kt_d * kActTile,
-                     p.sq + size_t(t) * Gd, u0 + ul, lane);
-      }
-    }
-    if (!grid_sync(p, epoch)) return;
-    cur ^= 1;
+    j = ph_qkv<KIND, NT, HD, REP>(p, li, j);
+    if (!grid_sync(p)) return;
+    j = ph_att<KIND, NT, HD, REP>(p, li, j);
+    if (!grid_sync(p)) return;
+    j = ph_o<KIND, NT, HD, REP>(p, li, j);
+    if (!grid_sync(p)) return;
+    j = ph_gu<KIND, NT, HD, REP>(p, li, j);
+    if (!grid_sync(p)) return;
+    j = ph_down<KIND, NT, HD, REP>(p, li, j);
+    if (!grid_sync(p)) return;
   }
-  // ---- head: fp16 logits and the greedy choice (chat/sample.go:80-88)
-  {
-    load_act<NT>(act_s, p.act[cur], p.kt_d);
-    norm_factors<NT>(cfac, p.sq, Gd, p.D, p.sc, p.eps);
-    if (threadIdx.x < NT) bmax[threadIdx.x] = 0ull;
-    if (threadIdx.x < kHeadSlots) hcnt[threadIdx.x] = 0u;
-    csync();
-    mark(p, epoch, 0);
-    j = consume_head<KIND, NT>(r, j, sc.head(), act_s, p, rows_s, hcnt, cfac, bmax);
-    csync();
-    mark(p, epoch, 1);
-    if (threadIdx.x < NT)
-      atomicMax(&p.amax[threadIdx.x * kAmaxSlots + (blockIdx.x % kAmaxSlots)], bmax[threadIdx.x]);
-  }
-  if (!grid_sync(p, epoch)) return;
+  j = ph_head<KIND, NT, HD, REP>(p, j);
+  if (!grid_sync(p)) return;
   if (p.trace && threadIdx.x == 0) {
     unsigned long long *st = p.trace + size_t(4) * mk_phases(p.layers) * gridDim.x + size_t(blockIdx.x) * 4;
     st[2] = s_cwait;
@@ -1200,28 +1171,34 @@ cudaError_t prepare_t(size_t smem) {
 size_t mk_layout(MkParams &p, int ctas) {
   const size_t limit = 225 * 1024;
   const int ktmax = std::max(p.kt_d, std::max(p.kt_f, p.kt_o));
-  auto per = [&](int U) { return (U + ctas - 1) / ctas; };
-  const int unit_rows = std::max({4 * per(p.D / 32), 8 * per(p.F / 32), per(p.rt_qkv), kHeadSlots});
   const int rep = p.H / p.KV;
+  const int tb = p.kind == kKindInt8 ? kTileInt8 : (p.kind == kKindInt4 ? kTileInt4 : kTileMx);
+  p.stage_bytes = kKr * tb;
   const size_t act = size_t(p.ntok) * ktmax * kActTile;
-  const size_t rows = size_t(kTeamWarps) * unit_rows * p.ntok * 8 * 4;
   const size_t att = size_t(rep * p.hd + 2 * p.hd + 2 * kWarps * rep + kWarps * rep * p.hd) * 4 + 16;
+  const size_t sq = size_t(p.ntok) * kWarps * 8;
   auto al = [](size_t x) { return (x + 127) / 128 * 128; };
-  const size_t rest = al(act) + al(rows) + al(att);
-  if (rest + 2 * kStageBytes + 64 > limit) return 0;
-  int S = int((limit - rest - 16 * 32) / kStageBytes);
-  S = std::min(S, 16);
+  // a stage costs its bytes, two partial slots of every warp and two mbarriers
+  const size_t fixed = al(act) + al(att) + al(sq);
+  const size_t per_stage = size_t(p.stage_bytes) + size_t(2) * kWarps * p.ntok * kTileRows * 4 + 16;
+  if (fixed + 2 * per_stage + 256 > limit) return 0;
+  int S = int((limit - fixed - 256) / per_stage);
+  S = std::min(S, kMaxStages);
   p.stages = S;
-  size_t off = size_t(S) * kStageBytes;
+  const size_t rows = size_t(kWarps) * 2 * S * p.ntok * kTileRows * 4;
+  size_t off = size_t(S) * p.stage_bytes;
   p.off_act = int(off);
   off += al(act);
   p.off_rows = int(off);
   off += al(rows);
   p.off_att = int(off);
   off += al(att);
+  p.off_sq = int(off);
+  off += al(sq);
   p.off_bar = int(off);
   off += size_t(2) * S * 8;
-  return off;
+  (void)ctas;
+  return off <= limit ? off : 0;
 }
 
 size_t mk_smem(const MkParams &p, int ctas) {

@@ -1,5 +1,5 @@
 // repack.cpp: the reference's weight bytes (palette.Linear, shiftScale's offset form, MXFP4) into
-// the integer-MMA tiles of common.h. Every code is copied as it is, so the dequantisation of the
+// the integer-MMA tiles of common.h (tile_pos gives every code's place). Every code is copied as it is, so the dequantisation of the
 // tiles equals the format's own (checked by hc_linear_dequant).
 #include "repack.h"
 
@@ -26,14 +26,15 @@ std::vector<RowRef> rows_concat(const std::vector<const hc_linear_desc *> &ds) {
 std::vector<RowRef> rows_glu(const hc_linear_desc &gate, uint32_t gate_row0, uint32_t gate_step,
                              const hc_linear_desc &up, uint32_t up_row0, uint32_t up_step,
                              uint32_t n) {
+  constexpr uint32_t half = kTileRows / 2;
   std::vector<RowRef> v;
-  for (uint32_t t = 0; t < (n + 3) / 4; ++t) {
-    for (uint32_t j = 0; j < 4; ++j) {
-      uint32_t o = t * 4 + j;
+  for (uint32_t t = 0; t < (n + half - 1) / half; ++t) {
+    for (uint32_t j = 0; j < half; ++j) {
+      uint32_t o = t * half + j;
       v.push_back(o < n ? RowRef{&gate, gate_row0 + o * gate_step} : RowRef{nullptr, 0});
     }
-    for (uint32_t j = 0; j < 4; ++j) {
-      uint32_t o = t * 4 + j;
+    for (uint32_t j = 0; j < half; ++j) {
+      uint32_t o = t * half + j;
       v.push_back(o < n ? RowRef{&up, up_row0 + o * up_step} : RowRef{nullptr, 0});
     }
   }
@@ -122,56 +123,38 @@ char *repack(const std::vector<RowRef> &rows, Packed *out) {
     for (size_t i = 0; i < rows.size(); ++i)
       if (rows[i].d) P.row_scale[i] = f16_value(rows[i].d->scales[rows[i].row]);
   }
+  const int kind4 = P.kind != kKindInt8, mx = P.kind == kKindMx;
   auto work = [&](int rt0, int rt1) {
     RowRef pad{nullptr, 0};
     for (int rt = rt0; rt < rt1; ++rt) {
       const RowRef *rr[kTileRows];
-      for (int g = 0; g < kTileRows; ++g) {
-        size_t r = size_t(rt) * kTileRows + g;
-        rr[g] = r < rows.size() ? &rows[r] : &pad;
+      for (int r = 0; r < kTileRows; ++r) {
+        size_t row = size_t(rt) * kTileRows + r;
+        rr[r] = row < rows.size() ? &rows[row] : &pad;
       }
       for (int kt = 0; kt < P.ktiles; ++kt) {
         uint8_t *t = &P.tiles[(size_t(rt) * P.ktiles + kt) * P.tile_bytes];
         const uint32_t col0 = uint32_t(kt) * kTileCols;
-        for (int L = 0; L < 32; ++L) {
-          const int g = L / 4, c = L % 4;
-          for (int i = 0; i < 8; ++i) {
-            uint8_t a[4], b[4];
-            for (int p = 0; p < 4; ++p) {
-              a[p] = code_of(*rr[g], col0 + 32 * c + 4 * i + p);        // group c
-              b[p] = code_of(*rr[g], col0 + 32 * (c + 4) + 4 * i + p);  // group c + 4
-            }
-            for (int p = 0; p < 4; ++p) {
-              if (P.kind == kKindInt8) {
-                // b0 = the 4 bytes of group c, b1 those of group c + 4
-                t[L * 64 + i * 8 + p] = a[p];
-                t[L * 64 + i * 8 + 4 + p] = b[p];
-              } else if (P.kind == kKindInt4) {
-                // byte p: group c's code low, group c + 4's high (b0 = w & 0x0F0F0F0F)
-                t[L * 32 + i * 4 + p] = uint8_t((a[p] & 0xf) | ((b[p] & 0xf) << 4));
-              }
-            }
-            if (P.kind == kKindMx) {
-              // nibbles a0 a1 a2 a3 b0 b1 b2 b3 from the lowest: each half word is the
-              // selector of one byte permute (e2m1x4 in device.cuh)
-              t[L * 32 + i * 4 + 0] = uint8_t(a[0] | (a[1] << 4));
-              t[L * 32 + i * 4 + 1] = uint8_t(a[2] | (a[3] << 4));
-              t[L * 32 + i * 4 + 2] = uint8_t(b[0] | (b[1] << 4));
-              t[L * 32 + i * 4 + 3] = uint8_t(b[2] | (b[3] << 4));
+        for (int r = 0; r < kTileRows; ++r)
+          for (int cc = 0; cc < kTileCols; ++cc) {
+            const TilePos tp = tile_pos(kind4, mx, r, cc);
+            const uint8_t code = code_of(*rr[r], col0 + cc);
+            t[tp.byte] = uint8_t(t[tp.byte] | (kind4 ? uint8_t((code & 0xf) << tp.shift) : code));
+          }
+        if (!kind4) continue;
+        for (int r = 0; r < kTileRows; ++r)
+          for (int G = 0; G < kGroupsPerTile; ++G) {
+            const TilePos tp = tile_pos(kind4, mx, r, G * kGroup);
+            const uint32_t grp = uint32_t(kt) * kGroupsPerTile + G;
+            if (P.kind == kKindInt4) {
+              uint16_t sv, zv;
+              sz_of(*rr[r], grp, &sv, &zv);
+              std::memcpy(t + kTileCodes4 + tp.lane * 16 + 2 * tp.sidx, &sv, 2);
+              std::memcpy(t + kTileCodes4 + tp.lane * 16 + 8 + 2 * tp.sidx, &zv, 2);
+            } else {
+              t[kTileCodes4 + tp.lane * 4 + tp.sidx] = e_of(*rr[r], grp);
             }
           }
-          const uint32_t grp = uint32_t(kt) * kGroupsPerTile + g;
-          if (P.kind == kKindInt4) {
-            uint16_t s0, z0, s1, z1;
-            sz_of(*rr[2 * c], grp, &s0, &z0);
-            sz_of(*rr[2 * c + 1], grp, &s1, &z1);
-            uint16_t v[4] = {s0, s1, z0, z1};
-            std::memcpy(t + kTileCodes4 + L * 8, v, 8);
-          } else if (P.kind == kKindMx) {
-            t[kTileCodes4 + L * 2] = e_of(*rr[2 * c], grp);
-            t[kTileCodes4 + L * 2 + 1] = e_of(*rr[2 * c + 1], grp);
-          }
-        }
       }
     }
   };

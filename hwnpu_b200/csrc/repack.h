@@ -32,7 +32,7 @@ struct Packed {
 std::vector<RowRef> rows_of(const hc_linear_desc &d);
 // q rows, then k rows, then v rows (one fused projection).
 std::vector<RowRef> rows_concat(const std::vector<const hc_linear_desc *> &ds);
-// Tiles of 4 gate rows then the 4 up rows of the same outputs, for the SwiGLU epilogue:
+// Tiles of 8 gate rows then the 8 up rows of the same outputs, for the SwiGLU epilogue:
 // gate row j comes from (gate, gate_row0 + j * gate_step), up row j from (up, up_row0 + j * up_step).
 std::vector<RowRef> rows_glu(const hc_linear_desc &gate, uint32_t gate_row0, uint32_t gate_step,
                              const hc_linear_desc &up, uint32_t up_row0, uint32_t up_step,

@@ -19,7 +19,7 @@ hc_session::~hc_session() {
   for (auto &g : graphs) cudaGraphExecDestroy(g.second);
   if (gen_graph) cudaGraphExecDestroy(gen_graph);
   if (gen_out) cudaFree(gen_out);
-  for (void *p : {(void *)mk_layers, (void *)mk_act[0], (void *)mk_act[1], (void *)mk_sq, (void *)mk_cnt,
+  for (void *p : {(void *)mk_layers,
                   (void *)mk_bar, (void *)mk_status, (void *)mk_trace})
     if (p) cudaFree(p);
   if (mk_status_host) cudaFreeHost(mk_status_host);
@@ -126,11 +126,13 @@ hc::MkParams mk_params(hc_session *s, int n, bool gen) {
   p.kt_o = p.H * p.hd / hc::kTileCols;
   p.rt_qkv = m->layers[0].qkv->m.rtiles;
   p.rt_head = m->head->m.rtiles;
-  p.splits = std::max(1, std::min(kMaxSplits, s->mk_ctas / (n * p.KV)));
+  p.splits = std::max(1, std::min(hc::kMkMaxSplits, s->mk_ctas / (n * p.KV)));
   p.sc_in0 = m->norm_in0.scale;
   p.eps_in0 = m->norm_in0.eps16;
   p.sc = m->norm_mid.scale;
   p.eps = m->norm_mid.eps16;
+  p.sc_head = m->norm_head.scale;
+  p.eps_head = m->norm_head.eps16;
   p.score_scale = m->score_scale;
   p.L = s->mk_layers;
   p.head = m->head->m.tiles;
@@ -140,13 +142,10 @@ hc::MkParams mk_params(hc_session *s, int n, bool gen) {
   p.rope = s->rope;
   p.toks = s->toks_dev;
   p.x = s->x;
+  p.h = s->h;
   p.qkv = s->qkv;
-  p.act[0] = s->mk_act[0];
-  p.act[1] = s->mk_act[1];
-  p.sq = s->mk_sq;
   p.part_ml = s->part_ml;
   p.part_o = s->part_o;
-  p.cnt = s->mk_cnt;
   p.logits = s->logits_dev;
   p.amax = s->amax;
   p.am = s->am_dev;
@@ -251,7 +250,7 @@ char *wait_done(hc_session *s, uint32_t timeout_ms, int32_t *state) {
 char *mk_setup(hc_session *s) {
   hc_model *m = s->m;
   const auto &d = m->d;
-  if (s->o.flags & HC_SESSION_NO_MEGAKERNEL) return nullptr;
+  if (!(s->o.flags & HC_SESSION_MEGAKERNEL)) return nullptr;
   const int kind = m->head->m.kind, rep = int(d.heads / d.kv_heads);
   if (!hc::mk_supported(kind, 1, int(d.head_dim), rep)) return nullptr;
   if (d.hidden % hc::kTileCols || d.inter % hc::kTileCols || (d.heads * d.head_dim) % hc::kTileCols) return nullptr;
@@ -279,14 +278,6 @@ char *mk_setup(hc_session *s) {
   }
   if (char *e = alloc(&s->mk_layers, L.size(), "step layer table")) return e;
   HC_TRY_CUDA(cudaMemcpy(s->mk_layers, L.data(), sizeof(hc::MkLayer) * L.size(), cudaMemcpyHostToDevice));
-  const int ktmax = std::max({probe.kt_d, probe.kt_f, probe.kt_o});
-  for (int b = 0; b < 2; ++b) {
-    if (char *e = alloc(&s->mk_act[b], size_t(kMaxChunk) * ktmax * hc::kActTile, "activation tiles")) return e;
-    HC_TRY_CUDA(cudaMemset(s->mk_act[b], 0, size_t(kMaxChunk) * ktmax * hc::kActTile));
-  }
-  if (char *e = alloc(&s->mk_sq, size_t(kMaxChunk) * (d.hidden / 32), "norm partials")) return e;
-  if (char *e = alloc(&s->mk_cnt, size_t(kMaxChunk) * d.kv_heads, "split counters")) return e;
-  HC_TRY_CUDA(cudaMemset(s->mk_cnt, 0, sizeof(unsigned) * kMaxChunk * d.kv_heads));
   if (char *e = alloc(&s->mk_bar, 1, "grid barrier")) return e;
   if (char *e = alloc(&s->mk_status, 1, "step status")) return e;
   HC_TRY_CUDA(cudaMemset(s->mk_status, 0, sizeof(int)));

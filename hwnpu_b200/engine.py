@@ -96,8 +96,8 @@ class LoadedModel:
         return A.lib().hc_model_weight_bytes(self.h)
 
     def session(self, max_context, max_seqs=1, max_step=8, kv_format=A.HC_KV_F16, page_size=16, graphs=True,
-                megakernel=True, profile=False):
-        flags = (0 if graphs else A.HC_SESSION_NO_GRAPH) | (0 if megakernel else A.HC_SESSION_NO_MEGAKERNEL) | \
+                megakernel=False, profile=False):
+        flags = (0 if graphs else A.HC_SESSION_NO_GRAPH) | (A.HC_SESSION_MEGAKERNEL if megakernel else 0) | \
                 (A.HC_SESSION_PROFILE if profile else 0)
         return Session(self, max_context, max_seqs, max_step, kv_format, page_size, flags)
 

@@ -213,8 +213,8 @@ enum {
 };
 enum {
   HC_SESSION_NO_GRAPH = 1 << 0,      /* launch the step's kernels one by one (no CUDA graph) */
-  HC_SESSION_NO_MEGAKERNEL = 1 << 1, /* run decode steps as one kernel per operation, not as the
-                                      * persistent one-launch step */
+  HC_SESSION_MEGAKERNEL = 1 << 1,    /* run steps of one token a sequence as the persistent
+                                      * one-launch step instead of the kernel sequence (experimental) */
   HC_SESSION_PROFILE = 1 << 2,       /* time the phases of the persistent step (hc_profile_get) */
 };
 
