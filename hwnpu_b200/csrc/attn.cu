@@ -21,6 +21,8 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(const float *__restrict__
                                                        float *__restrict__ q_out,
                                                        uint16_t *__restrict__ kcache,
                                                        uint16_t *__restrict__ vcache) {
+  pdl_trigger();
+  pdl_wait();
   const int hd = E * 32, half = hd / 2;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -95,6 +97,8 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
                                                          const uint16_t *__restrict__ vcache,
                                                          int splits, float *__restrict__ part_ml,
                                                          float *__restrict__ part_o) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int E = HD / 8;  // elements a lane: 16 (hd 128) or 8 (hd 64)
   __shared__ float sm_m[4][REP], sm_l[4][REP];
   __shared__ float sm_o[4][REP][HD];
@@ -225,9 +229,11 @@ void qkv_post(const float *qkv, const StepTok *toks, int ntok, const AttnGeom &g
   const int warps = ntok * (g.heads + g.kv_heads);
   const int grid = (warps + 3) / 4;
   if (g.hd == 128)
-    qkv_post_kernel<4><<<grid, 128, 0, st>>>(qkv, toks, ntok, g, qn, kn, norm_scale, eps16, rope, q_out, kcache, vcache);
+    launch_pdl(qkv_post_kernel<4>, dim3(grid), dim3(128), 0, st, qkv, toks, ntok, g, qn, kn, norm_scale, eps16, rope,
+               q_out, kcache, vcache);
   else
-    qkv_post_kernel<2><<<grid, 128, 0, st>>>(qkv, toks, ntok, g, qn, kn, norm_scale, eps16, rope, q_out, kcache, vcache);
+    launch_pdl(qkv_post_kernel<2>, dim3(grid), dim3(128), 0, st, qkv, toks, ntok, g, qn, kn, norm_scale, eps16, rope,
+               q_out, kcache, vcache);
 }
 
 void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g,
@@ -237,8 +243,8 @@ void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g
   const int rep = g.heads / g.kv_heads;
 #define HC_ATT(D, R)                                                                         \
   if (g.hd == D && rep == R) {                                                               \
-    attn_split_kernel<D, R><<<grid, 128, 0, st>>>(q, toks, g, kcache, vcache, splits, part_ml, \
-                                                  part_o);                                   \
+    launch_pdl(attn_split_kernel<D, R>, grid, dim3(128), 0, st, q, toks, g, kcache, vcache, splits, \
+               part_ml, part_o);                                                             \
     return;                                                                                  \
   }
   HC_ATT(128, 1) HC_ATT(128, 2) HC_ATT(128, 4) HC_ATT(128, 8)

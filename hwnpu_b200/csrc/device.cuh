@@ -9,6 +9,15 @@
 
 namespace hc {
 
+// ---- programmatic dependent launch -----------------------------------------------------------
+// The step's kernels are launched with programmatic stream serialization (launch_pdl): a kernel
+// lets the next one start as soon as all of its CTAs run (pdl_trigger), and waits for the
+// previous one's results (pdl_wait) only right before it reads them, so that a GEMV's weight
+// loads overlap the tail of the kernel before it. Every kernel waits (before its first dependent
+// read, or before it ends), which keeps the whole sequence ordered.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // mma.sync m16n8k32 with int32 accumulation: A (16x32, row), B (32x8, col), signed or unsigned
 // bytes as the name says (A first).
 __device__ __forceinline__ void mma_s8u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,

@@ -27,20 +27,27 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint8_t *__restrict__ t
   const int rpc = 8 / wpr;
   const int lrt = warp / wpr, ks = warp % wpr;
   const int rt = blockIdx.x * rpc + lrt;
+  pdl_trigger();
   if (threadIdx.x < NT) bmax[threadIdx.x] = 0ull;
   float vg[NT], vg8[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) vg[t] = vg8[t] = 0.f;
-  if (rt < rtiles) {
+  // the first weight tile does not depend on the kernels before: load it before waiting for them
+  const bool mine = rt < rtiles && ks < ktiles;
+  WTile<KIND> wt;
+  if (mine) wt.load(tiles + (size_t(rt) * ktiles + ks) * TB, lane);
+  pdl_wait();
+  if (mine) {
     for (int kt = ks; kt < ktiles; kt += wpr) {
-      WTile<KIND> wt;
-      wt.load(tiles + (size_t(rt) * ktiles + kt) * TB, lane);
+      WTile<KIND> nx;  // the next tile in flight while this one computes
+      if (kt + wpr < ktiles) nx.load(tiles + (size_t(rt) * ktiles + kt + wpr) * TB, lane);
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         BFrag<KIND> bf;
         bf.load(act + (size_t(t) * ktiles + kt) * kActTile, lane);
         wa_mma<KIND>(wt, bf, vg[t], vg8[t]);
       }
+      wt = nx;
     }
   }
 #pragma unroll
@@ -102,8 +109,8 @@ void launch_kind(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &o
   switch (ntok) {
 #define HC_NT(n)                                                                          \
   case n:                                                                                 \
-    gemv_kernel<KIND, n><<<grid, 256, 0, st>>>(W.tiles, W.row_scale, W.bias, act, W.rtiles, \
-                                              W.ktiles, W.rows, wpr, out);               \
+    launch_pdl(gemv_kernel<KIND, n>, dim3(grid), dim3(256), 0, st, W.tiles, W.row_scale, W.bias, act, \
+               W.rtiles, W.ktiles, W.rows, wpr, out);                                    \
     break;
     HC_NT(1) HC_NT(2) HC_NT(3) HC_NT(4) HC_NT(5) HC_NT(6) HC_NT(7) HC_NT(8)
 #undef HC_NT
@@ -161,6 +168,8 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const float *__restrict_
                                                         float scale, float eps16,
                                                         uint8_t *__restrict__ act, int ktiles) {
   __shared__ double red[32];
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.y, kt = blockIdx.x;
   const float *xt = x + size_t(t) * ldx;
   const float inv = scale == 1.f ? 1.f : 1.f / scale;
@@ -201,6 +210,8 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict
                                                          float *__restrict__ o_out) {
   __shared__ float wsh[64];
   __shared__ float stat[2];
+  pdl_trigger();
+  pdl_wait();
   const int h = blockIdx.x, t = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float *ml = part_ml + (size_t(t) * heads + h) * splits * 2;
@@ -261,7 +272,7 @@ void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cud
 
 void act_quant(const float *x, int ldx, int n, int ntok, const float *norm_w, float scale,
                float eps16, uint8_t *act, int ktiles, cudaStream_t st) {
-  act_quant_kernel<<<dim3(ktiles, ntok), 256, 0, st>>>(x, ldx, n, norm_w, scale, eps16, act, ktiles);
+  launch_pdl(act_quant_kernel, dim3(ktiles, ntok), dim3(256), 0, st, x, ldx, n, norm_w, scale, eps16, act, ktiles);
 }
 
 void attn_merge_quant(const float *part_ml, const float *part_o, const float *sinks, int ntok,
@@ -273,8 +284,8 @@ void attn_merge_quant(const float *part_ml, const float *part_o, const float *si
     for (int t = 0; t < ntok; ++t)
       cudaMemsetAsync(act + (size_t(t) * ktiles + ktiles - 1) * kActTile, 0, kActTile, st);
   }
-  attn_merge_kernel<<<dim3(heads, ntok), hd, 0, st>>>(part_ml, part_o, sinks, heads, hd, splits, act,
-                                                     ktiles, o_out);
+  launch_pdl(attn_merge_kernel, dim3(heads, ntok), dim3(hd), 0, st, part_ml, part_o, sinks, heads, hd, splits, act,
+             ktiles, o_out);
 }
 
 void dequant(const DevMat &W, int row0, int nrows, float *out, cudaStream_t st) {

@@ -4,7 +4,27 @@
 
 #include "common.h"
 
+#include <utility>
+
 namespace hc {
+
+// Launches k on st with programmatic stream serialization (device.cuh's pdl_trigger/pdl_wait): the
+// kernel may start while the one before it in the stream finishes.
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
 
 // A repacked matrix on the device (repack.h's Packed after the copy).
 struct DevMat {

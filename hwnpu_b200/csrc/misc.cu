@@ -11,6 +11,8 @@ __global__ void embed_kernel(const StepTok *__restrict__ toks, const uint16_t *_
                              const uint8_t *__restrict__ tiles, const float *__restrict__ row_scale,
                              int kind, int ktiles, int tile_bytes, int hidden,
                              float *__restrict__ x, unsigned long long *__restrict__ amax) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.y;
   const int tok = toks[t].token;
   for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < hidden; c += blockDim.x * gridDim.x) {
@@ -29,6 +31,8 @@ __global__ void embed_kernel(const StepTok *__restrict__ toks, const uint16_t *_
 
 __global__ void amax_index_kernel(const unsigned long long *__restrict__ amax, int ntok,
                                   int32_t *__restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x, lane = threadIdx.x;
   unsigned long long k = 0;
   for (int i = lane; i < kAmaxSlots; i += 32) k = max(k, amax[t * kAmaxSlots + i]);
@@ -39,6 +43,8 @@ __global__ void amax_index_kernel(const unsigned long long *__restrict__ amax, i
 
 __global__ void argmax_kernel(const uint16_t *__restrict__ logits, int vocab,
                               int32_t *__restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ unsigned long long best;
   if (threadIdx.x == 0) best = 0ull;
   __syncthreads();
@@ -57,6 +63,8 @@ __global__ void argmax_kernel(const uint16_t *__restrict__ logits, int vocab,
 // of k, renormalised by the float32 sum of the chosen plus 1e-6. One thread a row.
 __global__ void route_kernel(const float *__restrict__ logits, int rows, int n, int k,
                              int32_t *__restrict__ idx, float *__restrict__ w) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
   const float *lg = logits + size_t(r) * n;
@@ -88,6 +96,8 @@ __global__ void route_kernel(const float *__restrict__ logits, int rows, int n, 
 // chat/engine.go:1044-1058: keep draft i while the greedy pick after token i equals it.
 __global__ void spec_accept_kernel(const int32_t *__restrict__ am, const StepTok *__restrict__ toks,
                                    int n, int32_t *__restrict__ res) {
+  pdl_trigger();
+  pdl_wait();
   int kept = n, next = am[n - 1];
   for (int i = 0; i + 1 < n; ++i) {
     if (am[i] != toks[i + 1].token) { kept = i + 1; next = am[i]; break; }
@@ -98,6 +108,8 @@ __global__ void spec_accept_kernel(const int32_t *__restrict__ am, const StepTok
 
 __global__ void advance_kernel(StepTok *__restrict__ toks, const int32_t *__restrict__ am,
                                int32_t *__restrict__ out, int32_t *__restrict__ count) {
+  pdl_trigger();
+  pdl_wait();
   const int i = *count;
   out[i] = am[0];
   toks[0].token = am[0];
@@ -108,23 +120,22 @@ __global__ void advance_kernel(StepTok *__restrict__ toks, const int32_t *__rest
 }  // namespace
 
 void advance(StepTok *toks, const int32_t *am, int32_t *out, int32_t *count, cudaStream_t st) {
-  advance_kernel<<<1, 1, 0, st>>>(toks, am, out, count);
+  launch_pdl(advance_kernel, dim3(1), dim3(1), 0, st, toks, am, out, count);
 }
 
 void embed(const StepTok *toks, int ntok, const uint16_t *table, const DevMat *head, int hidden,
            float *x, unsigned long long *amax, cudaStream_t st) {
-  embed_kernel<<<dim3((hidden + 255) / 256, ntok), 256, 0, st>>>(toks, table, head ? head->tiles : nullptr,
-                                     head ? head->row_scale : nullptr, head ? head->kind : 0,
-                                     head ? head->ktiles : 0, head ? head->tile_bytes : 0, hidden,
-                                     x, amax);
+  launch_pdl(embed_kernel, dim3((hidden + 255) / 256, ntok), dim3(256), 0, st, toks, table,
+             head ? head->tiles : nullptr, head ? head->row_scale : nullptr, head ? head->kind : 0,
+             head ? head->ktiles : 0, head ? head->tile_bytes : 0, hidden, x, amax);
 }
 
 void amax_to_index(const unsigned long long *amax, int ntok, int32_t *out, cudaStream_t st) {
-  amax_index_kernel<<<ntok, 32, 0, st>>>(amax, ntok, out);
+  launch_pdl(amax_index_kernel, dim3(ntok), dim3(32), 0, st, amax, ntok, out);
 }
 
 void argmax_rows(const uint16_t *logits, int rows, int vocab, int32_t *out, cudaStream_t st) {
-  argmax_kernel<<<rows, 1024, 0, st>>>(logits, vocab, out);
+  launch_pdl(argmax_kernel, dim3(rows), dim3(1024), 0, st, logits, vocab, out);
 }
 
 void route(const float *logits, int rows, int n, int k, int32_t *idx, float *w, cudaStream_t st) {
@@ -133,7 +144,7 @@ void route(const float *logits, int rows, int n, int k, int32_t *idx, float *w, 
 
 void spec_accept(const int32_t *amax_idx, const StepTok *toks, int n, int32_t *res,
                  cudaStream_t st) {
-  spec_accept_kernel<<<1, 1, 0, st>>>(amax_idx, toks, n, res);
+  launch_pdl(spec_accept_kernel, dim3(1), dim3(1), 0, st, amax_idx, toks, n, res);
 }
 
 }  // namespace hc
