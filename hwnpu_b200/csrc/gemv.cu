@@ -215,6 +215,13 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict
   const int h = blockIdx.x, t = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float *ml = part_ml + (size_t(t) * heads + h) * splits * 2;
+  // the partials of this thread's element first (independent of the weights: one round trip)
+  constexpr int kPre = 32;
+  float pv[kPre];
+  const int d0 = threadIdx.x;
+  const float *po0 = part_o + ((size_t(t) * heads + h) * splits) * hd + d0;
+#pragma unroll
+  for (int s = 0; s < kPre; ++s) pv[s] = (s < splits && d0 < hd) ? po0[size_t(s) * hd] : 0.f;
   if (warp == 0) {
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     if (lane < splits) { m0 = ml[2 * lane]; l0 = ml[2 * lane + 1]; }
@@ -235,8 +242,14 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     const float *po = part_o + ((size_t(t) * heads + h) * splits) * hd + d;
     float o = 0.f;
-#pragma unroll 8
-    for (int s = 0; s < splits; ++s) o = fmaf(po[size_t(s) * hd], wsh[s], o);
+    if (d == d0) {
+#pragma unroll
+      for (int s = 0; s < kPre; ++s)
+        if (s < splits) o = fmaf(pv[s], wsh[s], o);
+      for (int s = kPre; s < splits; ++s) o = fmaf(po[size_t(s) * hd], wsh[s], o);
+    } else {
+      for (int s = 0; s < splits; ++s) o = fmaf(po[size_t(s) * hd], wsh[s], o);
+    }
     o *= invL;
     if (o_out) o_out[(size_t(t) * heads + h) * hd + d] = o;
     // one warp a group of 32: warp w of this head holds columns h*hd + 32w .. + 31
