@@ -6,7 +6,7 @@
  * internal/mxfp4, internal/llm/{qwen3,gptoss,experts,paged,decode}, internal/chat/sample.go).
  * Each function cites the reference file:line it follows. The Go reference cannot be built in
  * this environment (no Go toolchain, dependencies not vendored), so parity is pinned by the
- * reference's own known-answer tests, ported in tests/test_oracle_*.py.
+ * reference's own known-answer tests, ported in tests/test_oracle.py.
  *
  * Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg (and its --impl
  * reference arm) may load this library; the product never does.
