@@ -127,6 +127,101 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_c4(args, rank, world, local, dist):
+    """C4: greedy speculative decoding, the C1-shaped int8 draft (vocab
+    151936) drafting k = 4 tokens a round and the C2 target verifying the 5 rows in one hc_speculate
+    call with greedy acceptance (chat/engine.go:1044-1058); 512 tokens from a 512-id prompt. The
+    output must equal plain greedy decoding of the target, which is checked here. One replica a
+    GPU; the whole-job tokens/s sums the replicas over the slowest one's time."""
+    import numpy as np
+    import torch
+
+    import hwnpu_b200 as hb
+    from hwnpu_b200 import synth
+
+    P, OUT, k = 512, 512, 4
+    dev = hb.Device(local)
+    lt = dev.load_model(hb.Model(hb.C2, seed=0))
+    ld = dev.load_model(hb.Model(hb.C4_DRAFT, seed=1))
+    ctx = P + OUT + 2 * k + 8
+    prompt = synth.tokens(3, hb.C2.vocab, P)
+
+    # plain greedy decoding of the target: the stream speculation must reproduce, and its speed
+    plain = lt.session(max_context=ctx)
+    first = plain.greedy(prompt)
+    base = plain.pos()
+    plain.generate(first, 8)
+    plain.truncate(base)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ref = [first] + [int(x) for x in plain.generate(first, OUT - 1)]
+    plain_s = time.perf_counter() - t0
+    plain.close()
+
+    def speculate_run():
+        ts = lt.session(max_context=ctx, max_step=k + 1)
+        ds = ld.session(max_context=ctx)
+        out = [ts.greedy(prompt)]
+        ds.greedy(prompt)
+        pending, rounds, accepted = [], 0, 0
+        while len(out) < OUT:
+            last = out[-1]
+            if pending:
+                ds.greedy(pending)  # an accepted draft the draft model has not read yet
+            d = [int(x) for x in ds.generate(last, k)]  # reads last, d1..d3; d4 is only written
+            kept, nxt, _ = ts.speculate_tokens([last] + d)
+            acc = kept - 1
+            out.extend(d[:acc])
+            out.append(nxt)
+            p_last = ds.pos() - k  # the draft cache's position of `last`
+            if acc < k:
+                ds.truncate(p_last + 1 + acc)
+                pending = []
+            else:
+                pending = [d[k - 1]]
+            rounds += 1
+            accepted += acc
+        ts.close()
+        ds.close()
+        return out[:OUT], rounds, accepted
+
+    speculate_run()  # warm-up (graphs of every shape)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    out, rounds, accepted = speculate_run()
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    t_max = dt
+    if dist:
+        tt = torch.tensor([dt], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_max = float(tt.item())
+    same = out == ref[:OUT]
+    if rank != 0:
+        return
+    round_bytes = 4 * (45.2e6 + 155.6e6) + 1.0755e9 + 5 * 112 * 1024 * (P + OUT / 2)
+    line = {"metric": "speculative decode tokens/s", "value": world * OUT / t_max, "unit": "tokens/s",
+            "n_gpus": world, "steps": rounds, "warmup": 1, "ms_per_step": 1e3 * t_max / rounds,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8/int4 x int8(hi+lo) MMA -> int32, f32 scaling",
+            "data": "synthetic (seeded N(0,0.02) weights; draft and target independent, so drafts rarely match)",
+            "config": {"workload": "C4 speculative decode: C1-shaped int8 draft (V151936) -> C2 target, k=4, "
+                                   "512 tokens from a 512-id prompt, bs1", "global_batch": world,
+                       "parallelism": f"replicas x{world}", "k": k, "prompt": P, "tokens": OUT},
+            "rounds": rounds, "accepted_per_round": accepted / rounds,
+            "tokens_per_round": OUT / rounds, "identical_to_greedy": same,
+            "plain_greedy_tokens_per_s": OUT / plain_s,
+            "e2e": {"value": world * OUT / t_max, "unit": "tokens/s", "h2d_bytes_per_step": 4 * (k + 1) + 4 * k,
+                    "d2h_bytes_per_step": 4 * k + 8,
+                    "api": "hc_generate (draft) + hc_speculate (target verify) per round, host-driven"},
+            "round_bytes_model": round_bytes}
+    print(json.dumps(line), flush=True)
+    if not same:
+        raise SystemExit("speculative output differs from plain greedy decoding")
+
+
 def workload_config(args):
     return {"workload": f"{args.workload.upper()} bs1 greedy decode: 1024-id random prompt, passes of 256 steps "
                         f"(context 1024-1280)",
@@ -142,7 +237,9 @@ def main():
     ap.add_argument("--steps", type=int, default=2560)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c1"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c1", "c4"], default="c2",
+                    help="c2: the headline bs1 decode; c1: the small int8 model; c4: speculative decoding "
+                         "(C1-shaped int8 draft with V151936 -> C2 target, k=4, 512 tokens from a 512-id prompt)")
     ap.add_argument("--e2e-steps", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chunk-trace", default=None,
@@ -176,6 +273,11 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    if args.workload == "c4":
+        run_c4(args, rank, world, local, dist)
+        if dist:
+            dist.destroy_process_group()
+        return
     W = max(3, args.warmup)
     K = args.steps
     model = build_model(args.workload)
