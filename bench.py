@@ -193,11 +193,9 @@ def run_c4(args, rank, world, local, dist):
     out, rounds, accepted = speculate_run()
     torch.cuda.synchronize()
     dt = time.perf_counter() - t0
-    t_max = dt
-    if dist:
-        tt = torch.tensor([dt], device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_max = float(tt.item())
+    from hwnpu_b200 import replicas
+
+    t_max = replicas.job_time(dt, dist, "cuda")
     same = out == ref[:OUT]
     if rank != 0:
         return
@@ -381,11 +379,11 @@ def main():
     A.lib().hc_linear_free(h)
     head_bytes = model.head.data.nbytes + model.head.scales.nbytes + (model.head.zeros.nbytes if model.head.zeros is not None else 0)
 
-    t_max = ms
-    if dist:
-        tt = torch.tensor([ms, ms_e2e], device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_max, ms_e2e = float(tt[0]), float(tt[1])
+    from hwnpu_b200 import replicas
+
+    # the job's time is the slowest replica's (every rank runs the same K steps of its own replica)
+    t_max = replicas.job_time(ms, dist, "cuda")
+    ms_e2e = replicas.job_time(ms_e2e, dist, "cuda")
     cfg = model.cfg
     kv_per_pos = cfg.layers * cfg.kv_heads * cfg.head_dim * 2 * 2
     mean_ctx = PROMPT + (PASS + 1) / 2.0
