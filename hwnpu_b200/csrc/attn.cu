@@ -20,7 +20,8 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(const float *__restrict__
                                                        const uint32_t *__restrict__ rope,
                                                        float *__restrict__ q_out,
                                                        uint16_t *__restrict__ kcache,
-                                                       uint16_t *__restrict__ vcache) {
+                                                       uint16_t *__restrict__ vcache,
+                                                       float *__restrict__ kv_stage) {
   pdl_trigger();
   pdl_wait();
   const int hd = E * 32, half = hd / 2;
@@ -75,8 +76,19 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(const float *__restrict__
       for (int k = 0; k < E; ++k) dst[lane + 32 * k] = y[k];
       return;
     }
-    const size_t row = ((size_t(tk.slot) * g.kv_heads + kvh) * g.cap + tk.pos) * hd;
     const float *vs = qkv + size_t(t) * width + size_t(g.heads + g.kv_heads + kvh) * hd;
+    if (!kcache) {
+      // paged int8 cache: the rows go to kv_append_int8 in float32 ([t][k|v][kv head][hd])
+      float *kd = kv_stage + ((size_t(t) * 2) * g.kv_heads + kvh) * hd;
+      float *vd = kd + size_t(g.kv_heads) * hd;
+#pragma unroll
+      for (int k = 0; k < E; ++k) {
+        kd[lane + 32 * k] = y[k];
+        vd[lane + 32 * k] = vs[lane + 32 * k];
+      }
+      return;
+    }
+    const size_t row = ((size_t(tk.slot) * g.kv_heads + kvh) * g.cap + tk.pos) * hd;
 #pragma unroll
     for (int k = 0; k < E; ++k) {
       kcache[row + lane + 32 * k] = __half_as_ushort(__float2half_rn(y[k]));
@@ -89,12 +101,13 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(const float *__restrict__
 // cover the key's head_dim in 16-byte loads, so a warp has 4 keys in flight), keeping an online
 // softmax for every query head of the kv head's group (GQA: heads kvh*REP .. kvh*REP+REP-1);
 // the groups then merge, first within a warp by shuffles, then across the 4 warps in smem.
-template <int HD, int REP>
+template <int HD, int REP, bool PAGED>
 __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict__ q,
                                                          const StepTok *__restrict__ toks,
                                                          AttnGeom g,
                                                          const uint16_t *__restrict__ kcache,
                                                          const uint16_t *__restrict__ vcache,
+                                                         PagedKV pk,
                                                          int splits, float *__restrict__ part_ml,
                                                          float *__restrict__ part_o) {
   pdl_trigger();
@@ -136,20 +149,48 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
     const int j = j0 + grp;
     const bool valid = j < k1;
     float kf[E], vf[E];
-#pragma unroll
-    for (int u = 0; u < E / 8; ++u) {
-      uint4 kk = make_uint4(0, 0, 0, 0), vv = kk;
+    if (PAGED) {
+      // key j of the sequence: row j % 16 of its page, int8 times the (page, head) scale
+      float ks = 0.f, vsc = 0.f;
+      const int8_t *kr = nullptr, *vr = nullptr;
       if (valid) {
-        kk = reinterpret_cast<const uint4 *>(kcache + base + size_t(j) * HD + l8 * E)[u];
-        vv = reinterpret_cast<const uint4 *>(vcache + base + size_t(j) * HD + l8 * E)[u];
+        const int page = pk.btab[size_t(tk.slot) * pk.max_pages + j / kPage];
+        const size_t ph = size_t(page) * g.kv_heads + kvh;
+        ks = __half2float(__ushort_as_half(pk.kscale[ph]));
+        vsc = __half2float(__ushort_as_half(pk.vscale[ph]));
+        kr = pk.k + (ph * kPage + j % kPage) * HD + l8 * E;
+        vr = pk.v + (ph * kPage + j % kPage) * HD + l8 * E;
       }
-      const uint32_t kw[4] = {kk.x, kk.y, kk.z, kk.w}, vw[4] = {vv.x, vv.y, vv.z, vv.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const __half2 k2 = *reinterpret_cast<const __half2 *>(&kw[i]);
-        const __half2 v2 = *reinterpret_cast<const __half2 *>(&vw[i]);
-        kf[8 * u + 2 * i] = __low2float(k2); kf[8 * u + 2 * i + 1] = __high2float(k2);
-        vf[8 * u + 2 * i] = __low2float(v2); vf[8 * u + 2 * i + 1] = __high2float(v2);
+      for (int u = 0; u < E / 8; ++u) {
+        uint2 kk = make_uint2(0, 0), vv = kk;
+        if (valid) {
+          kk = reinterpret_cast<const uint2 *>(kr)[u];
+          vv = reinterpret_cast<const uint2 *>(vr)[u];
+        }
+        const uint32_t kw[2] = {kk.x, kk.y}, vw[2] = {vv.x, vv.y};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          kf[8 * u + i] = float(int8_t((kw[i / 4] >> (8 * (i % 4))) & 0xff)) * ks;
+          vf[8 * u + i] = float(int8_t((vw[i / 4] >> (8 * (i % 4))) & 0xff)) * vsc;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < E / 8; ++u) {
+        uint4 kk = make_uint4(0, 0, 0, 0), vv = kk;
+        if (valid) {
+          kk = reinterpret_cast<const uint4 *>(kcache + base + size_t(j) * HD + l8 * E)[u];
+          vv = reinterpret_cast<const uint4 *>(vcache + base + size_t(j) * HD + l8 * E)[u];
+        }
+        const uint32_t kw[4] = {kk.x, kk.y, kk.z, kk.w}, vw[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __half2 k2 = *reinterpret_cast<const __half2 *>(&kw[i]);
+          const __half2 v2 = *reinterpret_cast<const __half2 *>(&vw[i]);
+          kf[8 * u + 2 * i] = __low2float(k2); kf[8 * u + 2 * i + 1] = __high2float(k2);
+          vf[8 * u + 2 * i] = __low2float(v2); vf[8 * u + 2 * i + 1] = __high2float(v2);
+        }
       }
     }
 #pragma unroll
@@ -225,31 +266,102 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
 
 void qkv_post(const float *qkv, const StepTok *toks, int ntok, const AttnGeom &g, const float *qn,
               const float *kn, float norm_scale, float eps16, const uint32_t *rope, float *q_out,
-              uint16_t *kcache, uint16_t *vcache, cudaStream_t st) {
+              uint16_t *kcache, uint16_t *vcache, float *kv_stage, cudaStream_t st) {
   const int warps = ntok * (g.heads + g.kv_heads);
   const int grid = (warps + 3) / 4;
   if (g.hd == 128)
     launch_pdl(qkv_post_kernel<4>, dim3(grid), dim3(128), 0, st, qkv, toks, ntok, g, qn, kn, norm_scale, eps16, rope,
-               q_out, kcache, vcache);
+               q_out, kcache, vcache, kv_stage);
   else
     launch_pdl(qkv_post_kernel<2>, dim3(grid), dim3(128), 0, st, qkv, toks, ntok, g, qn, kn, norm_scale, eps16, rope,
-               q_out, kcache, vcache);
+               q_out, kcache, vcache, kv_stage);
 }
 
 void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g,
                 const uint16_t *kcache, const uint16_t *vcache, int splits, float *part_ml,
-                float *part_o, cudaStream_t st) {
+                float *part_o, cudaStream_t st, const PagedKV *paged) {
   dim3 grid(splits, g.kv_heads, ntok);
   const int rep = g.heads / g.kv_heads;
-#define HC_ATT(D, R)                                                                         \
-  if (g.hd == D && rep == R) {                                                               \
-    launch_pdl(attn_split_kernel<D, R>, grid, dim3(128), 0, st, q, toks, g, kcache, vcache, splits, \
-               part_ml, part_o);                                                             \
-    return;                                                                                  \
+  const PagedKV pk = paged ? *paged : PagedKV{};
+#define HC_ATT(D, R)                                                                          \
+  if (g.hd == D && rep == R) {                                                                \
+    if (paged)                                                                                \
+      launch_pdl(attn_split_kernel<D, R, true>, grid, dim3(128), 0, st, q, toks, g, kcache,   \
+                 vcache, pk, splits, part_ml, part_o);                                        \
+    else                                                                                      \
+      launch_pdl(attn_split_kernel<D, R, false>, grid, dim3(128), 0, st, q, toks, g, kcache,  \
+                 vcache, pk, splits, part_ml, part_o);                                        \
+    return;                                                                                   \
   }
   HC_ATT(128, 1) HC_ATT(128, 2) HC_ATT(128, 4) HC_ATT(128, 8)
   HC_ATT(64, 1) HC_ATT(64, 2) HC_ATT(64, 4) HC_ATT(64, 8)
 #undef HC_ATT
+}
+
+// Appends the chunk's new key and value rows (float32 from qkv_post) to the paged int8 cache. One
+// warp a (kv head, key | value) walks the tokens in order, so the rows of one page are never
+// written by two warps at once. A page's scale is the fp16 rounding up of max|x| / 127 over its
+// rows; when a new row needs a larger scale, the rows already in the page are requantised to it
+// (q' = round_even(q * s_old / s_new)), so every value stays within [-127, 127].
+template <int HD>
+__global__ void __launch_bounds__(128) kv_append_int8_kernel(const float *__restrict__ stage,
+                                                            const StepTok *__restrict__ toks, int ntok,
+                                                            int kv_heads, PagedKV pk) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int E = HD / 32;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (gw >= 2 * kv_heads) return;
+  const int kvh = gw >> 1, is_v = gw & 1;
+  int8_t *pool = const_cast<int8_t *>(is_v ? pk.v : pk.k);
+  uint16_t *scales = const_cast<uint16_t *>(is_v ? pk.vscale : pk.kscale);
+  for (int t = 0; t < ntok; ++t) {
+    const StepTok tk = toks[t];
+    const int page = pk.btab[size_t(tk.slot) * pk.max_pages + tk.pos / kPage], off = tk.pos % kPage;
+    const size_t ph = size_t(page) * kv_heads + kvh;
+    const float *src = stage + ((size_t(t) * 2 + is_v) * kv_heads + kvh) * HD;
+    float x[E], m = 0.f;
+#pragma unroll
+    for (int k = 0; k < E; ++k) {
+      x[k] = src[lane + 32 * k];
+      m = fmaxf(m, fabsf(x[k]));
+    }
+    m = warp_max(m);
+    const float s_old = off == 0 ? 0.f : __half2float(__ushort_as_half(scales[ph]));
+    float s_new = s_old;
+    if (m / 127.0f > s_old) {
+      s_new = __half2float(__float2half_ru(m / 127.0f));
+      if (off > 0 && s_old > 0.f) {
+        // requantise the page's earlier rows to the larger scale
+        const float f = s_old / s_new;
+        for (int r = 0; r < off; ++r) {
+          int8_t *row = pool + (ph * kPage + r) * HD;
+#pragma unroll
+          for (int k = 0; k < E; ++k) {
+            const int e = lane + 32 * k;
+            row[e] = int8_t(fminf(fmaxf(rintf(float(row[e]) * f), -127.f), 127.f));
+          }
+        }
+      }
+      if (lane == 0) scales[ph] = __half_as_ushort(__float2half_rn(s_new));
+    }
+    int8_t *row = pool + (ph * kPage + off) * HD;
+    const float inv = s_new > 0.f ? 1.0f / s_new : 0.f;
+#pragma unroll
+    for (int k = 0; k < E; ++k)
+      row[lane + 32 * k] = int8_t(fminf(fmaxf(rintf(x[k] * inv), -127.f), 127.f));
+    __syncwarp();
+  }
+}
+
+void kv_append_int8(const float *stage, const StepTok *toks, int ntok, int kv_heads, int hd, const PagedKV &pk,
+                    cudaStream_t st) {
+  const int warps = 2 * kv_heads, grid = (warps + 3) / 4;
+  if (hd == 128)
+    launch_pdl(kv_append_int8_kernel<128>, dim3(grid), dim3(128), 0, st, stage, toks, ntok, kv_heads, pk);
+  else
+    launch_pdl(kv_append_int8_kernel<64>, dim3(grid), dim3(128), 0, st, stage, toks, ntok, kv_heads, pk);
 }
 
 }  // namespace hc

@@ -66,6 +66,17 @@ struct hc_session {
   int cap = 0, splits = 1;
   uint16_t *kc = nullptr, *vc = nullptr;  // [layers][slots][kv_heads][cap][hd] fp16
   size_t layer_kv = 0;                    // elements of one layer's cache
+  // HC_KV_INT8_PAGED: page pools [layers][pages][kv_heads][16][hd] int8, scales
+  // [layers][pages][kv_heads] fp16, the block table [slots][max_pages] (device, and its host copy)
+  // and the free pages
+  bool paged = false;
+  int8_t *kp = nullptr, *vp = nullptr;
+  uint16_t *kps = nullptr, *vps = nullptr;
+  int32_t *btab_dev = nullptr;
+  std::vector<int32_t> btab;
+  std::vector<int32_t> free_pages;
+  int max_pages = 0, n_pages = 0;
+  float *kv_stage = nullptr;              // [max_step][2][kv_heads][hd] the new rows before quantisation
   uint32_t *rope = nullptr;               // [cap][hd/2] (cos, sin) fp16 pairs
   std::vector<int> pos;                   // per slot
   std::vector<bool> poisoned;             // per slot: a failed step may have half written it

@@ -85,16 +85,31 @@ struct AttnGeom {
 // RMS norm of q and k (when qn/kn are set), RoPE with the fp16 tables rope[pos][hd/2] (cos, sin
 // pairs as fp16 bits), q into q_out (float32 [ntok][heads][hd]) and k, v as fp16 into the
 // cache at (slot, kv_head, pos).
+// The paged int8 KV cache of one layer (HC_KV_INT8_PAGED): pages of kPage positions, each
+// [kv_heads][kPage][hd] int8 for keys and values, an fp16 scale per (page, head) for each, and
+// the block table [slots][max_pages] of page ids.
+constexpr int kPage = 16;
+struct PagedKV {
+  const int8_t *k = nullptr, *v = nullptr;
+  const uint16_t *kscale = nullptr, *vscale = nullptr;
+  const int32_t *btab = nullptr;
+  int max_pages = 0;
+};
+
 void qkv_post(const float *qkv, const StepTok *toks, int ntok, const AttnGeom &g,
               const float *qn, const float *kn, float norm_scale, float eps16,
               const uint32_t *rope, float *q_out, uint16_t *kcache, uint16_t *vcache,
-              cudaStream_t st);
+              float *kv_stage, cudaStream_t st);
+// With kcache NULL (the paged int8 cache) qkv_post leaves the new rows in kv_stage
+// ([ntok][2][kv_heads][hd] float32) and kv_append_int8 quantises them into the pages.
+void kv_append_int8(const float *stage, const StepTok *toks, int ntok, int kv_heads, int hd, const PagedKV &pk,
+                    cudaStream_t st);
 
 // Split-K decode attention over the fp16 cache: token t attends keys [lo, pos] of its slot
 // (lo = pos - window + 1 with a window); `splits` partials of (m, l) and unnormalised o.
 void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g,
                 const uint16_t *kcache, const uint16_t *vcache, int splits, float *part_ml,
-                float *part_o, cudaStream_t st);
+                float *part_o, cudaStream_t st, const PagedKV *paged = nullptr);
 
 // Embedding rows of the step's tokens into x (float32 [ntok][hidden]): from an fp16 table, or
 // (table nullptr) from the tied head's tiles, dequantised and rounded to fp16. Also resets amax.

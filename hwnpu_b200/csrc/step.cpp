@@ -24,6 +24,8 @@ hc_session::~hc_session() {
     if (p) cudaFree(p);
   if (mk_status_host) cudaFreeHost(mk_status_host);
   if (gen_count) cudaFree(gen_count);
+  for (void *p : {(void *)kp, (void *)vp, (void *)kps, (void *)vps, (void *)btab_dev, (void *)kv_stage})
+    if (p) cudaFree(p);
   for (void *p : {(void *)kc, (void *)vc, (void *)rope, (void *)x, (void *)qkv, (void *)q, (void *)h,
                   (void *)act, (void *)part_ml, (void *)part_o, (void *)toks_dev, (void *)logits_dev,
                   (void *)amax, (void *)am_dev, (void *)res_dev})
@@ -59,6 +61,53 @@ hc::AttnGeom geom(const hc_session *s, int window) {
   return hc::AttnGeom{int(d.heads), int(d.kv_heads), int(d.head_dim), s->cap, window, s->m->score_scale};
 }
 
+// The paged int8 cache of layer li.
+hc::PagedKV paged_of(const hc_session *s, size_t li) {
+  const auto &d = s->m->d;
+  const size_t per = size_t(s->n_pages) * d.kv_heads;
+  hc::PagedKV pk;
+  pk.k = s->kp + li * per * hc::kPage * d.head_dim;
+  pk.v = s->vp + li * per * hc::kPage * d.head_dim;
+  pk.kscale = s->kps + li * per;
+  pk.vscale = s->vps + li * per;
+  pk.btab = s->btab_dev;
+  pk.max_pages = s->max_pages;
+  return pk;
+}
+
+// Gives sequence `seq` pages for positions [p0, p1) (paged cache) and copies the changed part of
+// its block table to the device, ordered on the session's stream before the step that writes them.
+char *ensure_pages(hc_session *s, int seq, int p0, int p1) {
+  if (!s->paged || p1 <= p0) return nullptr;
+  int32_t *row = s->btab.data() + size_t(seq) * s->max_pages;
+  const int g0 = p0 / hc::kPage, g1 = (p1 - 1) / hc::kPage;
+  bool changed = false;
+  for (int g = g0; g <= g1; ++g) {
+    if (row[g] >= 0) continue;
+    if (s->free_pages.empty()) return hc::make_error("step: no free KV page");
+    row[g] = s->free_pages.back();
+    s->free_pages.pop_back();
+    changed = true;
+  }
+  if (changed) {
+    HC_TRY_CUDA(cudaMemcpyAsync(s->btab_dev + size_t(seq) * s->max_pages + g0, row + g0,
+                                sizeof(int32_t) * (g1 - g0 + 1), cudaMemcpyHostToDevice, s->st));
+    HC_TRY_CUDA(cudaStreamSynchronize(s->st));  // the host row may change again at the next call
+  }
+  return nullptr;
+}
+
+// Returns the pages of `seq` past its first `len` positions to the free list.
+void release_pages(hc_session *s, int seq, int len) {
+  if (!s->paged) return;
+  int32_t *row = s->btab.data() + size_t(seq) * s->max_pages;
+  for (int g = (len + hc::kPage - 1) / hc::kPage; g < s->max_pages; ++g)
+    if (row[g] >= 0) {
+      s->free_pages.push_back(row[g]);
+      row[g] = -1;
+    }
+}
+
 // Enqueues one chunk of n tokens (already in toks_dev) on the session's stream; returns the
 // number of kernels launched.
 int enqueue_chunk(hc_session *s, int n, bool accept) {
@@ -75,15 +124,21 @@ int enqueue_chunk(hc_session *s, int n, bool accept) {
   for (size_t li = 0; li < m->layers.size(); ++li) {
     const hc::LayerW &w = m->layers[li];
     const hc::NormCfg nc = li == 0 ? m->norm_in0 : m->norm_mid;
-    uint16_t *kcl = s->kc + li * s->layer_kv, *vcl = s->vc + li * s->layer_kv;
+    uint16_t *kcl = s->paged ? nullptr : s->kc + li * s->layer_kv;
+    uint16_t *vcl = s->paged ? nullptr : s->vc + li * s->layer_kv;
+    const hc::PagedKV pk = s->paged ? paged_of(s, li) : hc::PagedKV{};
     const hc::AttnGeom g = geom(s, w.window);
     hc::act_quant(s->x, D, D, n, w.in_norm, nc.scale, nc.eps16, s->act, w.qkv->m.ktiles, st);
     hc::GemvOut o1;
     o1.mode = hc::kStore; o1.y = s->qkv; o1.ldy = W;
     hc::gemv(w.qkv->m, s->act, n, o1, st);
     hc::qkv_post(s->qkv, s->toks_dev, n, g, w.q_norm, w.k_norm, m->norm_mid.scale, m->norm_mid.eps16,
-                 s->rope, s->q, kcl, vcl, st);
-    hc::attn_split(s->q, s->toks_dev, n, g, kcl, vcl, splits, s->part_ml, s->part_o, st);
+                 s->rope, s->q, kcl, vcl, s->kv_stage, st);
+    if (s->paged) {
+      hc::kv_append_int8(s->kv_stage, s->toks_dev, n, KV, hd, pk, st);
+      ++k;
+    }
+    hc::attn_split(s->q, s->toks_dev, n, g, kcl, vcl, splits, s->part_ml, s->part_o, st, s->paged ? &pk : nullptr);
     hc::attn_merge_quant(s->part_ml, s->part_o, w.sinks, n, H, hd, splits, s->act, w.o->m.ktiles, nullptr, st);
     hc::GemvOut o2;
     o2.mode = hc::kAdd; o2.y = s->x; o2.ldy = D;
@@ -177,6 +232,8 @@ bool mk_chunk(const hc_session *s, int n) {
 
 // The whole chunk: tokens in, greedy choices (and the accept result) out, as one graph.
 char *run_chunk(hc_session *s, int n, bool accept) {
+  for (int i = 0; i < n; ++i)
+    if (char *e = ensure_pages(s, s->toks_host[i].slot, s->toks_host[i].pos, s->toks_host[i].pos + 1)) return e;
   cudaStream_t st = s->st;
   const bool use_graph = !(s->o.flags & HC_SESSION_NO_GRAPH);
   const bool mk = !accept && mk_chunk(s, n);
@@ -250,7 +307,7 @@ char *wait_done(hc_session *s, uint32_t timeout_ms, int32_t *state) {
 char *mk_setup(hc_session *s) {
   hc_model *m = s->m;
   const auto &d = m->d;
-  if (!(s->o.flags & HC_SESSION_MEGAKERNEL)) return nullptr;
+  if (!(s->o.flags & HC_SESSION_MEGAKERNEL) || s->paged) return nullptr;
   const int kind = m->head->m.kind, rep = int(d.heads / d.kv_heads);
   if (!hc::mk_supported(kind, 1, int(d.head_dim), rep)) return nullptr;
   if (d.hidden % hc::kTileCols || d.inter % hc::kTileCols || (d.heads * d.head_dim) % hc::kTileCols) return nullptr;
@@ -302,7 +359,10 @@ HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session
   *out = nullptr;
   const hc_session_opts &o = *opts;
   if (!o.max_context || !o.max_seqs || !o.max_step) return hc::make_error("hc_session_new: zero size");
-  if (o.kv_format != HC_KV_F16) return hc::make_error("hc_session_new: KV format " + std::to_string(o.kv_format) + " is not supported by this build");
+  if (o.kv_format != HC_KV_F16 && o.kv_format != HC_KV_INT8_PAGED)
+    return hc::make_error("hc_session_new: KV format " + std::to_string(o.kv_format) + " is not supported by this build");
+  if (o.kv_format == HC_KV_INT8_PAGED && o.page_size != uint32_t(hc::kPage))
+    return hc::make_error("hc_session_new: the paged int8 cache has pages of " + std::to_string(hc::kPage) + " positions");
   HC_TRY_CUDA(cudaSetDevice(m->ordinal));
   auto s = std::make_unique<hc_session>();
   s->m = m;
@@ -310,12 +370,30 @@ HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session
   s->cap = int(o.max_context);
   const auto &d = m->d;
   const int D = int(d.hidden), F = int(d.inter), H = int(d.heads), KV = int(d.kv_heads), hd = int(d.head_dim);
-  s->layer_kv = size_t(o.max_seqs) * KV * s->cap * hd;
-  const size_t kv_elems = s->layer_kv * d.layers;
-  if (char *e = alloc(&s->kc, kv_elems, "key cache")) return e;
-  if (char *e = alloc(&s->vc, kv_elems, "value cache")) return e;
-  HC_TRY_CUDA(cudaMemset(s->kc, 0, kv_elems * 2));
-  HC_TRY_CUDA(cudaMemset(s->vc, 0, kv_elems * 2));
+  s->paged = o.kv_format == HC_KV_INT8_PAGED;
+  if (s->paged) {
+    // every slot can hold max_context positions: the pool is slots x pages of max_context
+    s->max_pages = (s->cap + hc::kPage - 1) / hc::kPage;
+    s->n_pages = int(o.max_seqs) * s->max_pages;
+    const size_t rows = size_t(d.layers) * s->n_pages * KV;
+    if (char *e = alloc(&s->kp, rows * hc::kPage * hd, "key pages")) return e;
+    if (char *e = alloc(&s->vp, rows * hc::kPage * hd, "value pages")) return e;
+    if (char *e = alloc(&s->kps, rows, "key page scales")) return e;
+    if (char *e = alloc(&s->vps, rows, "value page scales")) return e;
+    HC_TRY_CUDA(cudaMemset(s->kps, 0, rows * 2));
+    HC_TRY_CUDA(cudaMemset(s->vps, 0, rows * 2));
+    if (char *e = alloc(&s->btab_dev, size_t(o.max_seqs) * s->max_pages, "block table")) return e;
+    s->btab.assign(size_t(o.max_seqs) * s->max_pages, -1);
+    HC_TRY_CUDA(cudaMemcpy(s->btab_dev, s->btab.data(), s->btab.size() * 4, cudaMemcpyHostToDevice));
+    for (int p = s->n_pages - 1; p >= 0; --p) s->free_pages.push_back(p);
+  } else {
+    s->layer_kv = size_t(o.max_seqs) * KV * s->cap * hd;
+    const size_t kv_elems = s->layer_kv * d.layers;
+    if (char *e = alloc(&s->kc, kv_elems, "key cache")) return e;
+    if (char *e = alloc(&s->vc, kv_elems, "value cache")) return e;
+    HC_TRY_CUDA(cudaMemset(s->kc, 0, kv_elems * 2));
+    HC_TRY_CUDA(cudaMemset(s->vc, 0, kv_elems * 2));
+  }
   // blocks.RopeValues (blocks.go:412-427) as fp16 inputs (qwen3 StepInputs, arch.go:117-137)
   std::vector<uint32_t> rope(size_t(s->cap) * (hd / 2));
   for (int p = 0; p < s->cap; ++p)
@@ -335,6 +413,8 @@ HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session
   const int T = kMaxChunk;
   if (char *e = alloc(&s->x, size_t(T) * D, "hidden states")) return e;
   if (char *e = alloc(&s->qkv, size_t(T) * (H + 2 * KV) * hd, "qkv")) return e;
+  if (s->paged)
+    if (char *e = alloc(&s->kv_stage, size_t(T) * 2 * KV * hd, "new key and value rows")) return e;
   if (char *e = alloc(&s->q, size_t(T) * H * hd, "queries")) return e;
   if (char *e = alloc(&s->h, size_t(T) * F, "mlp activations")) return e;
   if (char *e = alloc(&s->act, size_t(T) * ktiles * hc::kActTile, "activation tiles")) return e;
@@ -475,6 +555,7 @@ HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, i
   if (first < 0 || first >= int(s->m->d.vocab)) return hc::make_error("hc_generate: token out of the vocabulary");
   if (hc::fault_fires(hc::kFaultStep)) return hc::make_error("injected fault: step");
   HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
+  if (char *e = ensure_pages(s, seq, s->pos[seq], s->pos[seq] + n)) return e;
   cudaStream_t st = s->st;
   s->toks_host[0] = hc::StepTok{first, seq, s->pos[seq], 0};
   const bool mk = s->mk && hc::mk_supported(s->m->head->m.kind, 1, int(s->m->d.head_dim),
@@ -535,6 +616,7 @@ HC_API char *hc_seq_reset(hc_session *s, int32_t seq) {
   if (!s || seq < 0 || seq >= int(s->o.max_seqs)) return hc::make_error("hc_seq_reset: bad sequence");
   s->pos[seq] = 0;
   s->poisoned[seq] = false;
+  release_pages(s, seq, 0);
   return nullptr;
 }
 
@@ -542,6 +624,7 @@ HC_API char *hc_seq_truncate(hc_session *s, int32_t seq, int32_t len) {
   if (!s || seq < 0 || seq >= int(s->o.max_seqs)) return hc::make_error("hc_seq_truncate: bad sequence");
   if (len < 0 || len > s->pos[seq]) return hc::make_error("hc_seq_truncate: length out of range");
   s->pos[seq] = len;
+  release_pages(s, seq, len);
   return nullptr;
 }
 
@@ -573,6 +656,7 @@ HC_API char *hc_seq_export_rows(hc_session *s, int32_t seq, int32_t start, int32
                                 uint64_t cap, uint64_t *need) {
   if (!s || seq < 0 || seq >= int(s->o.max_seqs)) return hc::make_error("hc_seq_export_rows: bad sequence");
   if (start < 0 || n < 0 || start + n > s->pos[seq]) return hc::make_error("hc_seq_export_rows: rows out of range");
+  if (s->paged) return hc::make_error("hc_seq_export_rows: not available for the paged int8 cache");
   const auto &d = s->m->d;
   const uint64_t bytes = uint64_t(d.layers) * 2 * d.kv_heads * n * d.head_dim * 2;
   if (need) *need = bytes;
@@ -587,6 +671,7 @@ HC_API char *hc_seq_import_rows(hc_session *s, int32_t seq, int32_t start, int32
                                 const void *src, uint64_t size) {
   if (!s || !src || seq < 0 || seq >= int(s->o.max_seqs)) return hc::make_error("hc_seq_import_rows: bad argument");
   if (start < 0 || n < 0 || start > s->pos[seq] || start + n > s->cap) return hc::make_error("hc_seq_import_rows: rows out of range");
+  if (s->paged) return hc::make_error("hc_seq_import_rows: not available for the paged int8 cache");
   const auto &d = s->m->d;
   const uint64_t bytes = uint64_t(d.layers) * 2 * d.kv_heads * n * d.head_dim * 2;
   if (size != bytes) return hc::make_error("hc_seq_import_rows: size does not match the rows");

@@ -209,7 +209,12 @@ HC_API uint64_t hc_model_weight_bytes(hc_model *m);
 
 enum {
   HC_KV_F16 = 0,        /* fp16 keys and values, (kv_heads, positions, head_dim) per layer */
-  HC_KV_INT8_PAGED = 1, /* int8 in pages of page_size positions, one fp16 scale a (head, page) */
+  /* int8 in pages of page_size (16) positions from a pool with a block table per sequence, one
+   * fp16 scale a (page, head) for keys and one for values (BASELINE C5; the reference has no
+   * such cache). A page's scale is the fp16 rounding up of max|x| / 127 over its rows; when a new
+   * row needs more, the page's rows are requantised to the new scale. Truncating inside a page
+   * keeps its scale; truncated pages return to the pool. Export/import of rows is not offered. */
+  HC_KV_INT8_PAGED = 1,
 };
 enum {
   HC_SESSION_NO_GRAPH = 1 << 0,      /* launch the step's kernels one by one (no CUDA graph) */

@@ -1,0 +1,108 @@
+"""The paged int8 KV cache (HC_KV_INT8_PAGED: 16-position pages, an fp16 scale per (page, head)).
+
+The reference has no int8 paged cache (its parity is unpinned), so the check is against the fp16
+cache on the same model and tokens: the int8 rounding of keys and values may move the logits a
+little (tolerance below), but sequences in a ragged batch must read exactly what they read alone,
+pages must be reusable after a truncation, and decoding across page boundaries (where a page's
+scale grows and its rows are requantised) must stay close to the fp16 cache."""
+
+import numpy as np
+import pytest
+
+from hwnpu_b200 import _abi as A
+from hwnpu_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+# int8 keys and values against fp16 ones: logits within this fraction of the largest |logit|
+# (measured on B200: up to 3.4 % on the tiny model, 2.5 % on C2's layers) and this cosine
+# (measured >= 0.9996)
+PAGED_REL = 5e-2
+PAGED_COS = 0.999
+
+TINY = synth.Config("tiny-qwen3", 2, 256, 512, 4, 2, 64, 1000, A.HC_FMT_INT4_ASYM_G32, tied=True, qk_norm=True,
+                    rope_theta=1e6, std=0.05)
+C2_2L = synth.Config("c2-2layers", 2, 2048, 6144, 16, 8, 128, 151936, A.HC_FMT_INT4_ASYM_G32, tied=True,
+                     qk_norm=True, rope_theta=1e6)
+
+
+def cosine(a, b):
+    a, b = a.astype(np.float64), b.astype(np.float64)
+    return float(a @ b / np.sqrt((a @ a) * (b @ b)))
+
+
+@pytest.fixture(scope="module")
+def models():
+    return {}
+
+
+def get(models, cfg):
+    if cfg.name not in models:
+        models[cfg.name] = synth.Model(cfg, seed=0, norm_std=0.1)
+    return models[cfg.name]
+
+
+def paged(lm, **kw):
+    return lm.session(kv_format=A.HC_KV_INT8_PAGED, page_size=16, **kw)
+
+
+@pytest.mark.parametrize("cfg,prompt,steps", [(TINY, 37, 30), (C2_2L, 40, 20)], ids=lambda v: getattr(v, "name", str(v)))
+def test_paged_int8_close_to_fp16(device, models, cfg, prompt, steps):
+    model = get(models, cfg)
+    lm = device.load_model(model)
+    ref = lm.session(max_context=prompt + steps + 4)
+    pg = paged(lm, max_context=prompt + steps + 4)
+    toks = list(synth.tokens(5, cfg.vocab, prompt))
+    a, b = ref.step_tokens(toks), pg.step_tokens(toks)
+    for i in range(steps):  # crosses page boundaries: scales grow, rows get requantised
+        assert np.abs(a - b).max() <= PAGED_REL * np.abs(a).max(), (i, np.abs(a - b).max(), np.abs(a).max())
+        assert cosine(a, b) >= PAGED_COS
+        t = int(np.argmax(a))
+        a, b = ref.step_tokens([t]), pg.step_tokens([t])
+    ref.close()
+    pg.close()
+    lm.close()
+
+
+def test_paged_ragged_batch_equals_single_sequences(device, models):
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    batch = paged(lm, max_context=64, max_seqs=3, max_step=8)
+    alone = [paged(lm, max_context=64) for _ in range(3)]
+    prompts = [list(synth.tokens(40 + i, TINY.vocab, n)) for i, n in enumerate((20, 7, 33))]
+    for i in range(3):
+        batch.step_batch([i], [prompts[i]])
+        alone[i].step_batch([0], [prompts[i]])
+    nxt = [[int(t)] for t in synth.tokens(9, TINY.vocab, 3)]
+    for _ in range(4):
+        lb, ab = batch.step_batch([0, 1, 2], nxt)
+        for i in range(3):
+            la, aa = alone[i].step_batch([0], [nxt[i]])
+            assert ab[i] == aa[0]
+            assert np.abs(synth.f16_values(lb[i]) - synth.f16_values(la[0])).max() <= 1e-6
+        nxt = [[int(t)] for t in ab]
+    for s in alone:
+        s.close()
+    batch.close()
+    lm.close()
+
+
+def test_paged_pages_reused_after_truncate(device, models):
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    s = paged(lm, max_context=48)
+    fresh = paged(lm, max_context=48)
+    toks = list(synth.tokens(11, TINY.vocab, 40))
+    s.step_tokens(toks)          # 3 pages
+    s.truncate(16)               # keep page 1 whole: pages 2 and 3 return to the pool
+    other = list(synth.tokens(12, TINY.vocab, 30))
+    got = s.step_tokens(other)   # positions 16..45, on reused pages
+    want = fresh.step_tokens(toks[:16] + other)
+    assert np.abs(got - want).max() <= 1e-6
+    s.reset()
+    assert s.pos() == 0
+    with pytest.raises(A.HcError):
+        s.export_rows(0, 0)
+    s.close()
+    fresh.close()
+    lm.close()
