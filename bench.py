@@ -220,6 +220,146 @@ def run_c4(args, rank, world, local, dist):
         raise SystemExit("speculative output differs from plain greedy decoding")
 
 
+C5_SEQS, C5_STEPS, C5_NEW_PROMPT = 64, 128, 512
+C5_KV_POS = 28 * (8 * 128 * 2 + 2 * 8 * 2 / 16)  # int8 K and V rows + fp16 page scales, per position
+
+
+def run_c5(args, rank, world, local, dist):
+    """C5: continuous-batched ragged decode of the C2 model over a paged
+    int8 KV cache (16-position pages, fp16 scale per page and KV head). 64 sequences with contexts
+    drawn uniform on 128..8192 (PCG64, seed 2), each owed 128 decode steps; the owed counts are
+    staggered (sequence i has 128 - 2i left) so that sequences finish at different steps, and a
+    finished one is replaced in its slot by a new sequence whose 512-id prompt is read in the same
+    batched step as the others' decode tokens. The 64 sequences are sharded round robin over the
+    ranks (replicas.shard), weights replicated, no collective on the path.
+
+    A timed step is one hc_step call over every slot of the rank (each slot's next token, or a new
+    prompt). value: the decoded tokens of all ranks / the slowest rank's device time (the sum of the
+    call's chunk graphs, CUDA events). e2e: the same tokens over CUDA events around the whole host
+    loop (token lists in, greedy choices out, slot replacement), max over ranks."""
+    import numpy as np
+    import torch
+
+    import hwnpu_b200 as hb
+    from hwnpu_b200 import _abi as A
+    from hwnpu_b200 import replicas, synth
+
+    ctx_all = np.random.default_rng(2).integers(128, 8192, size=C5_SEQS, endpoint=True)
+    mine = replicas.shard(C5_SEQS, rank, world)
+    n = len(mine)
+    dev = hb.Device(local)
+    model = hb.Model(hb.C2, seed=0)
+    lm = dev.load_model(model)
+    max_ctx = int(ctx_all.max()) + C5_STEPS + 16
+    warm = n  # an extra slot that runs the chunk shapes once before the timed steps
+    sess = lm.session(max_context=max_ctx, max_seqs=n + 1, kv_format=A.HC_KV_INT8_PAGED)
+    for k in range(1, 9):
+        sess.step_batch([warm], [synth.tokens(7, hb.C2.vocab, k)], want_logits=False)
+    sess.reset(warm)
+
+    # the starting state: every slot's context read as a prompt (untimed)
+    t_fill = time.perf_counter()
+    last, owed, ctx_tok = [], [], 0
+    for i, gi in enumerate(mine):
+        _, am = sess.step_batch([i], [synth.tokens(100 + gi, hb.C2.vocab, int(ctx_all[gi]))], want_logits=False)
+        last.append(int(am[0]))
+        owed.append(C5_STEPS - 2 * gi)
+        ctx_tok += int(ctx_all[gi])
+    torch.cuda.synchronize()
+    fill_s = time.perf_counter() - t_fill
+    stream = torch.cuda.ExternalStream(sess.stream())
+    new_seed = [1000 + gi * 64 for gi in mine]
+
+    def run(steps, timed):
+        """`steps` batched steps; returns (decoded tokens, prompt tokens, device ms, kv bytes)."""
+        dec = prm = 0
+        dev_ms = kv = 0.0
+        for _ in range(steps):
+            lists, fresh = [], []
+            for i in range(n):
+                if owed[i] <= 0:  # finished: a new sequence takes the slot
+                    sess.reset(i)
+                    new_seed[i] += 1
+                    lists.append(synth.tokens(new_seed[i], hb.C2.vocab, C5_NEW_PROMPT))
+                    owed[i] = C5_STEPS
+                    fresh.append(i)
+                else:
+                    lists.append([last[i]])
+            pos0 = [sess.pos(i) for i in range(n)] if timed else None
+            _, am = sess.step_batch(list(range(n)), lists, want_logits=False)
+            for i in range(n):
+                last[i] = int(am[i])
+                owed[i] -= 1
+            dec += n
+            prm += sum(len(l) - 1 for l in lists)
+            if timed:
+                dev_ms += sess.stats()["last_step_us"] / 1e3
+                for i in range(n):  # KV positions each token attends to (its own row included)
+                    m = len(lists[i])
+                    kv += C5_KV_POS * (m * pos0[i] + m * (m + 1) / 2)
+        return dec, prm, dev_ms, kv
+
+    W = max(3, args.warmup)
+    run(W, False)
+    launches0 = sess.stats()["launches"]
+    clocks = Clocks(local)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    dec, prm, dev_ms, kv = run(C5_STEPS, True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    e2e_ms = e0.elapsed_time(e1)
+    launches = sess.stats()["launches"] - launches0
+    t_dev = replicas.job_time(dev_ms, dist, "cuda")
+    t_e2e = replicas.job_time(e2e_ms, dist, "cuda")
+    dec_all = replicas.job_total(dec, dist, "cuda")
+    prm_all = replicas.job_total(prm, dist, "cuda")
+    kv_all = replicas.job_total(int(kv), dist, "cuda")
+    weight_bytes = lm.weight_bytes
+    sess.close()
+    lm.close()
+    dev.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, peak_kind = peaks()
+    # algorithmic bytes: each rank reads its weights once per step, plus the KV every token touches
+    step_bytes = world * C5_STEPS * weight_bytes + kv_all
+    ach = step_bytes / (t_dev / 1e3) / 1e9 / world  # per GPU
+    line = {
+        "metric": "decode tokens/s", "value": dec_all / (t_dev / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": C5_STEPS, "warmup": W, "ms_per_step": t_dev / C5_STEPS, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "int4 x int8(hi+lo) MMA -> int32, f32 scaling; int8 KV x fp16 page scales",
+        "data": "synthetic (seeded N(0,0.02) weights, uniform ids)",
+        "config": {"workload": "C5 continuous-batched ragged decode: 64 sequences, contexts U[128,8192] (seed 2), "
+                               "128 steps owed each (staggered), finished ones replaced by 512-id prompts; "
+                               "paged int8 KV (16-position pages)",
+                   "model": "C2 28L d2048 16q/8kv hd128 FFN6144 V151936 tied, int4 asym g32",
+                   "global_batch": C5_SEQS, "parallelism": f"sequence shards x{world} (replicated weights)",
+                   "l2": "inputs larger than L2 (1.1 GB of weights and ~15 GB of KV a step)"},
+        "decoded_tokens": dec_all, "prompt_tokens_read": prm_all,
+        "prompt_tokens_per_s": prm_all / (t_dev / 1e3),
+        "e2e": {"value": dec_all / (t_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 16 * (dec_all + prm_all) // C5_STEPS,
+                "d2h_bytes_per_step": 4 * dec_all // C5_STEPS,
+                "api": "hc_step over every slot per step (host-built token lists, greedy choices out)"},
+        "gpu_launches": int(launches),
+        "step_roofline": {"bytes_per_step": step_bytes / C5_STEPS, "achieved_gbs_per_gpu": ach, "peak": peak,
+                          "peak_kind": peak_kind, "frac": ach / peak,
+                          "weights_bytes_per_rank_step": weight_bytes, "kv_bytes_per_step": kv_all / C5_STEPS},
+        "fill": {"context_tokens_rank0": ctx_tok, "seconds_rank0": fill_s},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def workload_config(args):
     return {"workload": f"{args.workload.upper()} bs1 greedy decode: 1024-id random prompt, passes of 256 steps "
                         f"(context 1024-1280)",
@@ -235,9 +375,10 @@ def main():
     ap.add_argument("--steps", type=int, default=2560)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c1", "c4"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c1", "c4", "c5"], default="c2",
                     help="c2: the headline bs1 decode; c1: the small int8 model; c4: speculative decoding "
-                         "(C1-shaped int8 draft with V151936 -> C2 target, k=4, 512 tokens from a 512-id prompt)")
+                         "(C1-shaped int8 draft with V151936 -> C2 target, k=4, 512 tokens from a 512-id prompt); "
+                         "c5: 64 ragged sequences over a paged int8 KV cache, sharded over the ranks")
     ap.add_argument("--e2e-steps", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chunk-trace", default=None,
@@ -275,6 +416,9 @@ def main():
         run_c4(args, rank, world, local, dist)
         if dist:
             dist.destroy_process_group()
+        return
+    if args.workload == "c5":
+        run_c5(args, rank, world, local, dist)
         return
     W = max(3, args.warmup)
     K = args.steps

@@ -144,53 +144,68 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
   }
   const size_t base = (size_t(tk.slot) * g.kv_heads + kvh) * size_t(g.cap) * HD;
   // the trip count is the same for every lane (the shuffles below take the whole warp); a group
-  // whose key is past the chunk's end loads nothing and leaves its softmax as it is
-  for (int j0 = k0; j0 < k1; j0 += 16) {
-    const int j = j0 + grp;
-    const bool valid = j < k1;
-    float kf[E], vf[E];
+  // whose key is past the chunk's end loads nothing and leaves its softmax as it is. The loads of
+  // a group's next key are issued before the current key's arithmetic (one key in flight ahead).
+  constexpr int KW = PAGED ? E / 4 : E / 2;  // 32-bit words of a lane's part of a K (or V) row
+  struct Raw {
+    uint32_t k[KW], v[KW];
+    float ks, vs;
+  };
+  auto fetch = [&](int j, Raw &r) {
+#pragma unroll
+    for (int i = 0; i < KW; ++i) r.k[i] = r.v[i] = 0u;
+    r.ks = r.vs = 0.f;
+    if (j >= k1) return;
+    const uint32_t *kp, *vp;
     if (PAGED) {
       // key j of the sequence: row j % 16 of its page, int8 times the (page, head) scale
-      float ks = 0.f, vsc = 0.f;
-      const int8_t *kr = nullptr, *vr = nullptr;
-      if (valid) {
-        const int page = pk.btab[size_t(tk.slot) * pk.max_pages + j / kPage];
-        const size_t ph = size_t(page) * g.kv_heads + kvh;
-        ks = __half2float(__ushort_as_half(pk.kscale[ph]));
-        vsc = __half2float(__ushort_as_half(pk.vscale[ph]));
-        kr = pk.k + (ph * kPage + j % kPage) * HD + l8 * E;
-        vr = pk.v + (ph * kPage + j % kPage) * HD + l8 * E;
-      }
+      const int page = pk.btab[size_t(tk.slot) * pk.max_pages + j / kPage];
+      const size_t ph = size_t(page) * g.kv_heads + kvh;
+      r.ks = __half2float(__ushort_as_half(pk.kscale[ph]));
+      r.vs = __half2float(__ushort_as_half(pk.vscale[ph]));
+      kp = reinterpret_cast<const uint32_t *>(pk.k + (ph * kPage + j % kPage) * HD + l8 * E);
+      vp = reinterpret_cast<const uint32_t *>(pk.v + (ph * kPage + j % kPage) * HD + l8 * E);
+    } else {
+      kp = reinterpret_cast<const uint32_t *>(kcache + base + size_t(j) * HD + l8 * E);
+      vp = reinterpret_cast<const uint32_t *>(vcache + base + size_t(j) * HD + l8 * E);
+    }
+    if (KW % 4 == 0) {
 #pragma unroll
-      for (int u = 0; u < E / 8; ++u) {
-        uint2 kk = make_uint2(0, 0), vv = kk;
-        if (valid) {
-          kk = reinterpret_cast<const uint2 *>(kr)[u];
-          vv = reinterpret_cast<const uint2 *>(vr)[u];
-        }
-        const uint32_t kw[2] = {kk.x, kk.y}, vw[2] = {vv.x, vv.y};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          kf[8 * u + i] = float(int8_t((kw[i / 4] >> (8 * (i % 4))) & 0xff)) * ks;
-          vf[8 * u + i] = float(int8_t((vw[i / 4] >> (8 * (i % 4))) & 0xff)) * vsc;
-        }
+      for (int i = 0; i < KW / 4; ++i) {
+        const uint4 a = reinterpret_cast<const uint4 *>(kp)[i], b = reinterpret_cast<const uint4 *>(vp)[i];
+        r.k[4 * i] = a.x; r.k[4 * i + 1] = a.y; r.k[4 * i + 2] = a.z; r.k[4 * i + 3] = a.w;
+        r.v[4 * i] = b.x; r.v[4 * i + 1] = b.y; r.v[4 * i + 2] = b.z; r.v[4 * i + 3] = b.w;
       }
     } else {
 #pragma unroll
-      for (int u = 0; u < E / 8; ++u) {
-        uint4 kk = make_uint4(0, 0, 0, 0), vv = kk;
-        if (valid) {
-          kk = reinterpret_cast<const uint4 *>(kcache + base + size_t(j) * HD + l8 * E)[u];
-          vv = reinterpret_cast<const uint4 *>(vcache + base + size_t(j) * HD + l8 * E)[u];
-        }
-        const uint32_t kw[4] = {kk.x, kk.y, kk.z, kk.w}, vw[4] = {vv.x, vv.y, vv.z, vv.w};
+      for (int i = 0; i < KW / 2; ++i) {
+        const uint2 a = reinterpret_cast<const uint2 *>(kp)[i], b = reinterpret_cast<const uint2 *>(vp)[i];
+        r.k[2 * i] = a.x; r.k[2 * i + 1] = a.y;
+        r.v[2 * i] = b.x; r.v[2 * i + 1] = b.y;
+      }
+    }
+  };
+  Raw cur;
+  fetch(k0 + grp, cur);
+  for (int j0 = k0; j0 < k1; j0 += 16) {
+    const int j = j0 + grp;
+    const bool valid = j < k1;
+    Raw nxt;
+    fetch(j + 16, nxt);
+    float kf[E], vf[E];
+    if (PAGED) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const __half2 k2 = *reinterpret_cast<const __half2 *>(&kw[i]);
-          const __half2 v2 = *reinterpret_cast<const __half2 *>(&vw[i]);
-          kf[8 * u + 2 * i] = __low2float(k2); kf[8 * u + 2 * i + 1] = __high2float(k2);
-          vf[8 * u + 2 * i] = __low2float(v2); vf[8 * u + 2 * i + 1] = __high2float(v2);
-        }
+      for (int i = 0; i < E; ++i) {
+        kf[i] = float(int8_t((cur.k[i / 4] >> (8 * (i % 4))) & 0xff)) * cur.ks;
+        vf[i] = float(int8_t((cur.v[i / 4] >> (8 * (i % 4))) & 0xff)) * cur.vs;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < E / 2; ++i) {
+        const __half2 k2 = *reinterpret_cast<const __half2 *>(&cur.k[i]);
+        const __half2 v2 = *reinterpret_cast<const __half2 *>(&cur.v[i]);
+        kf[2 * i] = __low2float(k2); kf[2 * i + 1] = __high2float(k2);
+        vf[2 * i] = __low2float(v2); vf[2 * i + 1] = __high2float(v2);
       }
     }
 #pragma unroll
@@ -211,6 +226,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
         m[r] = mn;
       }
     }
+    cur = nxt;
   }
   // merge the 4 groups of the warp (lanes differing in bits 3 and 4)
 #pragma unroll
@@ -298,11 +314,13 @@ void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g
 #undef HC_ATT
 }
 
-// Appends the chunk's new key and value rows (float32 from qkv_post) to the paged int8 cache. One
-// warp a (kv head, key | value) walks the tokens in order, so the rows of one page are never
-// written by two warps at once. A page's scale is the fp16 rounding up of max|x| / 127 over its
-// rows; when a new row needs a larger scale, the rows already in the page are requantised to it
-// (q' = round_even(q * s_old / s_new)), so every value stays within [-127, 127].
+// Appends the chunk's new key and value rows (float32 from qkv_post) to the paged int8 cache. The
+// tokens of one sequence are consecutive in a chunk (a sequence is listed once a call), so the
+// chunk splits into runs of tokens that write the same page; one warp a (kv head, key | value, run)
+// walks its run in order, and the rows of one page are never written by two warps at once. A
+// page's scale is the fp16 rounding up of max|x| / 127 over its rows; when a new row needs a
+// larger scale, the rows already in the page are requantised to it (q' = round_even(q * s_old /
+// s_new)), so every value stays within [-127, 127].
 template <int HD>
 __global__ void __launch_bounds__(128) kv_append_int8_kernel(const float *__restrict__ stage,
                                                             const StepTok *__restrict__ toks, int ntok,
@@ -312,11 +330,13 @@ __global__ void __launch_bounds__(128) kv_append_int8_kernel(const float *__rest
   constexpr int E = HD / 32;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (gw >= 2 * kv_heads) return;
-  const int kvh = gw >> 1, is_v = gw & 1;
+  if (gw >= 2 * kv_heads * ntok) return;
+  const int t0 = gw / (2 * kv_heads), kvh = (gw >> 1) % kv_heads, is_v = gw & 1;
+  auto same_page = [&](const StepTok &a, const StepTok &b) { return a.slot == b.slot && a.pos / kPage == b.pos / kPage; };
+  if (t0 > 0 && same_page(toks[t0 - 1], toks[t0])) return;  // not the first token of its run
   int8_t *pool = const_cast<int8_t *>(is_v ? pk.v : pk.k);
   uint16_t *scales = const_cast<uint16_t *>(is_v ? pk.vscale : pk.kscale);
-  for (int t = 0; t < ntok; ++t) {
+  for (int t = t0; t < ntok && (t == t0 || same_page(toks[t0], toks[t])); ++t) {
     const StepTok tk = toks[t];
     const int page = pk.btab[size_t(tk.slot) * pk.max_pages + tk.pos / kPage], off = tk.pos % kPage;
     const size_t ph = size_t(page) * kv_heads + kvh;
@@ -357,7 +377,7 @@ __global__ void __launch_bounds__(128) kv_append_int8_kernel(const float *__rest
 
 void kv_append_int8(const float *stage, const StepTok *toks, int ntok, int kv_heads, int hd, const PagedKV &pk,
                     cudaStream_t st) {
-  const int warps = 2 * kv_heads, grid = (warps + 3) / 4;
+  const int warps = 2 * kv_heads * ntok, grid = (warps + 3) / 4;
   if (hd == 128)
     launch_pdl(kv_append_int8_kernel<128>, dim3(grid), dim3(128), 0, st, stage, toks, ntok, kv_heads, pk);
   else

@@ -15,7 +15,7 @@ namespace hc {
 int device_ordinal(const hc_device *d);
 int device_sms(const hc_device *d);
 
-constexpr int kMaxChunk = 8;  // tokens one pass of the GEMVs reads the weights for
+constexpr int kMaxChunk = 64;  // tokens one pass of the GEMVs reads the weights for
 
 // One repacked matrix in HBM.
 struct DevLinear {

@@ -13,6 +13,59 @@
 namespace hc {
 namespace {
 
+// The end of both GEMV kernels: part[w][t][r] holds warp w's sum for token t and row r of its row
+// tile; the wpr warps of a row tile are added, scaled and written as out.mode says, for tokens
+// t < nt. Ends with the argmax atomics of kLogits (bmax is the CTA's per-token key, zeroed before).
+template <int KIND, int NT>
+__device__ __forceinline__ void gemv_finish(float (*part)[NT][kTileRows], unsigned long long *bmax, int nt,
+                                            const float *__restrict__ row_scale, const float *__restrict__ bias,
+                                            int rtiles, int rows, int wpr, const GemvOut &out) {
+  const int rpc = 8 / wpr;
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < rpc * NT * kTileRows; idx += blockDim.x) {
+    const int l2 = idx / (NT * kTileRows), t = (idx / kTileRows) % NT, r16 = idx % kTileRows;
+    const int tile_r = blockIdx.x * rpc + l2;
+    if (tile_r >= rtiles || t >= nt) continue;
+    auto value = [&](int rr) {
+      float v = 0.f;
+      for (int k = 0; k < wpr; ++k) v += part[l2 * wpr + k][t][rr];
+      const int row = tile_r * kTileRows + rr;
+      if (KIND == kKindInt8) v *= row_scale[row];
+      if (KIND == kKindMx) v *= 0.5f;  // the doubled e2m1 values (mxfp4.go:90)
+      if (bias) v += bias[row];
+      return v;
+    };
+    if (out.mode == kGlu) {
+      if (r16 >= kTileRows / 2) continue;
+      const int o = tile_r * (kTileRows / 2) + r16;
+      if (o >= rows) continue;
+      const float gv = value(r16), uv = value(r16 + kTileRows / 2);
+      // blocks.SiLU: x / (1 + exp(-x)) (internal/llm/blocks/blocks.go:395-399)
+      out.y[size_t(t) * out.ldy + o] = gv / (1.0f + expf(-gv)) * uv;
+      continue;
+    }
+    const int row = tile_r * kTileRows + r16;
+    if (row >= rows) continue;
+    const float v = value(r16);
+    if (out.mode == kStore) {
+      out.y[size_t(t) * out.ldy + row] = v;
+    } else if (out.mode == kAdd) {
+      float *p = out.y + size_t(t) * out.ldy + row;
+      *p = *p + v;
+    } else {
+      const __half h = __float2half_rn(v);
+      const uint16_t hb = __half_as_ushort(h);
+      if (out.logits) out.logits[size_t(t) * out.ldy + row] = hb;
+      atomicMax(&bmax[t], argmax_key(hb, uint32_t(row)));
+    }
+  }
+  if (out.mode == kLogits) {
+    __syncthreads();
+    if (threadIdx.x < nt)
+      atomicMax(&out.amax[threadIdx.x * kAmaxSlots + (blockIdx.x % kAmaxSlots)], bmax[threadIdx.x]);
+  }
+}
+
 template <int KIND, int NT>
 __global__ void __launch_bounds__(256) gemv_kernel(const uint8_t *__restrict__ tiles,
                                                    const float *__restrict__ row_scale,
@@ -58,49 +111,145 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint8_t *__restrict__ t
       part[warp][t][g + 8] = b;
     }
   }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < rpc * NT * kTileRows; idx += blockDim.x) {
-    const int l2 = idx / (NT * kTileRows), t = (idx / kTileRows) % NT, r16 = idx % kTileRows;
-    const int tile_r = blockIdx.x * rpc + l2;
-    if (tile_r >= rtiles) continue;
-    auto value = [&](int rr) {
-      float v = 0.f;
-      for (int k = 0; k < wpr; ++k) v += part[l2 * wpr + k][t][rr];
-      const int row = tile_r * kTileRows + rr;
-      if (KIND == kKindInt8) v *= row_scale[row];
-      if (KIND == kKindMx) v *= 0.5f;  // the doubled e2m1 values (mxfp4.go:90)
-      if (bias) v += bias[row];
-      return v;
-    };
-    if (out.mode == kGlu) {
-      if (r16 >= kTileRows / 2) continue;
-      const int o = tile_r * (kTileRows / 2) + r16;
-      if (o >= rows) continue;
-      const float gv = value(r16), uv = value(r16 + kTileRows / 2);
-      // blocks.SiLU: x / (1 + exp(-x)) (internal/llm/blocks/blocks.go:395-399)
-      out.y[size_t(t) * out.ldy + o] = gv / (1.0f + expf(-gv)) * uv;
-      continue;
-    }
-    const int row = tile_r * kTileRows + r16;
-    if (row >= rows) continue;
-    const float v = value(r16);
-    if (out.mode == kStore) {
-      out.y[size_t(t) * out.ldy + row] = v;
-    } else if (out.mode == kAdd) {
-      float *p = out.y + size_t(t) * out.ldy + row;
-      *p = *p + v;
-    } else {
-      const __half h = __float2half_rn(v);
-      const uint16_t hb = __half_as_ushort(h);
-      if (out.logits) out.logits[size_t(t) * out.ldy + row] = hb;
-      atomicMax(&bmax[t], argmax_key(hb, uint32_t(row)));
+  gemv_finish<KIND, NT>(part, bmax, NT, row_scale, bias, rtiles, rows, wpr, out);
+}
+
+// ---- the batched GEMV: tokens on the MMA's n ----------------------------------------------
+// For 9..64 tokens the same tiles are read once for all of them. Per group G of a tile a warp
+// gathers the m16n8k32 A operand whose k is G's 32 columns (tile_pos: lane (g, c) takes rows g,
+// g + 8 and columns 4c..4c+3, 16+4c..19+4c, which lane 4g + G % 4 of the tile layout holds as the
+// two words j = 2 (c & 1), +1 of pieces c / 2 and 2 + c / 2; int8 pieces 4 (G / 4) + those), and
+// B is 8 tokens' hi (then lo) bytes of G. D is then, exactly, the group's integer dot product of
+// 16 rows x 8 tokens, which lane (g, c) scales for rows g, g + 8 and tokens 2c, 2c + 1 with the
+// same float32 arithmetic as the token-a-column GEMV (wa_mma): s S (hi + lo/256 - z Xq) for int4,
+// S (hi + lo/256) for int8, 2^(e-127) S hi for mxfp4.
+__device__ __forceinline__ uint32_t ldg32(const uint8_t *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
+__device__ __forceinline__ uint2 ldg64(const uint8_t *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
+
+template <int KIND, int NB>
+__global__ void __launch_bounds__(256) gemm_tn_kernel(const uint8_t *__restrict__ tiles,
+                                                      const float *__restrict__ row_scale,
+                                                      const float *__restrict__ bias,
+                                                      const uint8_t *__restrict__ act, int ntok,
+                                                      int rtiles, int ktiles, int rows, int wpr,
+                                                      GemvOut out) {
+  constexpr int TB = KIND == kKindInt8 ? kTileInt8 : (KIND == kKindInt4 ? kTileInt4 : kTileMx);
+  constexpr int NT = 8 * NB;
+  __shared__ float part[8][NT][kTileRows];
+  __shared__ unsigned long long bmax[NT];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int rpc = 8 / wpr;
+  const int lrt = warp / wpr, ks = warp % wpr;
+  const int rt = blockIdx.x * rpc + lrt;
+  pdl_trigger();
+  if (threadIdx.x < NT) bmax[threadIdx.x] = 0ull;
+  float acc[NB][4];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.f;
+  const bool mine = rt < rtiles && ks < ktiles;
+  // the first weight tile does not depend on the kernels before: bring it towards L2 meanwhile
+  constexpr int kLines = (TB + 127) / 128;
+  if (mine && lane < kLines)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(tiles + (size_t(rt) * ktiles + ks) * TB + lane * 128));
+  pdl_wait();
+  if (mine) {
+    for (int kt = ks; kt < ktiles; kt += wpr) {
+      const uint8_t *tile = tiles + (size_t(rt) * ktiles + kt) * TB;
+      if (kt + wpr < ktiles && lane < kLines)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(tile + size_t(wpr) * TB + lane * 128));
+      const uint8_t *at = act + size_t(kt) * kActTile;  // token t's tile at + t * ktiles * kActTile
+      const size_t tstride = size_t(ktiles) * kActTile;
+#pragma unroll 1
+      for (int G = 0; G < kGroupsPerTile; ++G) {
+        const int h = G >> 2, Ls = 4 * g + (G & 3);
+        const int piece0 = (KIND == kKindInt8 ? 4 * h : 0) + (c >> 1);
+        const uint2 w01 = ldg64(tile + (piece0 * 32 + Ls) * 16 + 8 * (c & 1));
+        const uint2 w23 = ldg64(tile + ((piece0 + 2) * 32 + Ls) * 16 + 8 * (c & 1));
+        uint32_t a[4];
+        float s0 = 1.f, s8 = 1.f, z0 = 0.f, z8 = 0.f;
+        if (KIND == kKindInt8) {
+          a[0] = w01.x; a[1] = w01.y; a[2] = w23.x; a[3] = w23.y;
+        } else if (KIND == kKindInt4) {
+          const int sh = 4 * h;
+          a[0] = (w01.x >> sh) & 0x0F0F0F0Fu; a[1] = (w01.y >> sh) & 0x0F0F0F0Fu;
+          a[2] = (w23.x >> sh) & 0x0F0F0F0Fu; a[3] = (w23.y >> sh) & 0x0F0F0F0Fu;
+          const uint32_t sz = ldg32(tile + kTileCodes4 + Ls * 16 + 4 * h);      // s(g), s(g+8)
+          const uint32_t zz = ldg32(tile + kTileCodes4 + Ls * 16 + 8 + 4 * h);  // z(g), z(g+8)
+          const __half2 s2 = *reinterpret_cast<const __half2 *>(&sz);
+          const __half2 z2 = *reinterpret_cast<const __half2 *>(&zz);
+          s0 = __low2float(s2); s8 = __high2float(s2);
+          z0 = __low2float(z2); z8 = __high2float(z2);
+        } else {
+          const uint32_t w[4] = {w01.x, w01.y, w23.x, w23.y};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t x = w[j], xs = x << 4;
+            a[j] = h ? e2m1x4(x, xs, 0xFBEAu, (x >> 16) & 0x7777u) : e2m1x4(x, xs, 0xD9C8u, x & 0x7777u);
+          }
+          const uint32_t e4 = ldg32(tile + kTileCodes4 + Ls * 4);
+          s0 = __uint_as_float(((e4 >> (16 * h)) & 0xffu) << 23);
+          s8 = __uint_as_float(((e4 >> (16 * h + 8)) & 0xffu) << 23);
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          const int tb = 8 * b + g;        // the token of this lane's B column
+          const int t0 = 8 * b + 2 * c;    // the tokens of this lane's D columns: t0, t0 + 1
+          uint32_t bh0 = 0, bh1 = 0, bl0 = 0, bl1 = 0;
+          if (tb < ntok) {
+            const uint8_t *ab = at + tb * tstride + G * 64 + 4 * c;
+            bh0 = ldg32(ab);
+            bh1 = ldg32(ab + 16);
+            if (KIND != kKindMx) {
+              bl0 = ldg32(ab + 32);
+              bl1 = ldg32(ab + 48);
+            }
+          }
+          float2 x0 = make_float2(0.f, 0.f), x1 = x0;
+          if (t0 < ntok) x0 = __ldg(reinterpret_cast<const float2 *>(at + t0 * tstride + kGroupsPerTile * 64 + G * 8));
+          if (t0 + 1 < ntok) x1 = __ldg(reinterpret_cast<const float2 *>(at + (t0 + 1) * tstride + kGroupsPerTile * 64 + G * 8));
+          int dh[4] = {0, 0, 0, 0};
+          if (KIND == kKindInt4) mma_u8s8(dh, a[0], a[1], a[2], a[3], bh0, bh1);
+          else mma_s8s8(dh, a[0], a[1], a[2], a[3], bh0, bh1);
+          if (KIND == kKindMx) {
+            // d: (row g, t0), (g, t0+1), (g+8, t0), (g+8, t0+1)
+            acc[b][0] = fmaf(float(dh[0]) * s0, x0.x, acc[b][0]);
+            acc[b][1] = fmaf(float(dh[1]) * s0, x1.x, acc[b][1]);
+            acc[b][2] = fmaf(float(dh[2]) * s8, x0.x, acc[b][2]);
+            acc[b][3] = fmaf(float(dh[3]) * s8, x1.x, acc[b][3]);
+          } else {
+            int dl[4] = {0, 0, 0, 0};
+            if (KIND == kKindInt4) mma_u8s8(dl, a[0], a[1], a[2], a[3], bl0, bl1);
+            else mma_s8s8(dl, a[0], a[1], a[2], a[3], bl0, bl1);
+            const float p0 = fmaf(float(dl[0]), 1.0f / 256.0f, float(dh[0]));
+            const float p1 = fmaf(float(dl[1]), 1.0f / 256.0f, float(dh[1]));
+            const float p2 = fmaf(float(dl[2]), 1.0f / 256.0f, float(dh[2]));
+            const float p3 = fmaf(float(dl[3]), 1.0f / 256.0f, float(dh[3]));
+            if (KIND == kKindInt4) {
+              acc[b][0] = fmaf(s0 * x0.x, fmaf(-z0, x0.y, p0), acc[b][0]);
+              acc[b][1] = fmaf(s0 * x1.x, fmaf(-z0, x1.y, p1), acc[b][1]);
+              acc[b][2] = fmaf(s8 * x0.x, fmaf(-z8, x0.y, p2), acc[b][2]);
+              acc[b][3] = fmaf(s8 * x1.x, fmaf(-z8, x1.y, p3), acc[b][3]);
+            } else {
+              acc[b][0] = fmaf(x0.x, p0, acc[b][0]);
+              acc[b][1] = fmaf(x1.x, p1, acc[b][1]);
+              acc[b][2] = fmaf(x0.x, p2, acc[b][2]);
+              acc[b][3] = fmaf(x1.x, p3, acc[b][3]);
+            }
+          }
+        }
+      }
     }
   }
-  if (out.mode == kLogits) {
-    __syncthreads();
-    if (threadIdx.x < NT)
-      atomicMax(&out.amax[threadIdx.x * kAmaxSlots + (blockIdx.x % kAmaxSlots)], bmax[threadIdx.x]);
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const int t0 = 8 * b + 2 * c;
+    part[warp][t0][g] = acc[b][0];
+    part[warp][t0 + 1][g] = acc[b][1];
+    part[warp][t0][g + 8] = acc[b][2];
+    part[warp][t0 + 1][g + 8] = acc[b][3];
   }
+  gemv_finish<KIND, NT>(part, bmax, ntok, row_scale, bias, rtiles, rows, wpr, out);
 }
 
 template <int KIND>
@@ -114,6 +263,17 @@ void launch_kind(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &o
     break;
     HC_NT(1) HC_NT(2) HC_NT(3) HC_NT(4) HC_NT(5) HC_NT(6) HC_NT(7) HC_NT(8)
 #undef HC_NT
+    default: {
+      switch ((ntok + 7) / 8) {
+#define HC_NB(b)                                                                                      \
+  case b:                                                                                             \
+    launch_pdl(gemm_tn_kernel<KIND, b>, dim3(grid), dim3(256), 0, st, W.tiles, W.row_scale, W.bias, act, \
+               ntok, W.rtiles, W.ktiles, W.rows, wpr, out);                                          \
+    break;
+        HC_NB(2) HC_NB(3) HC_NB(4) HC_NB(5) HC_NB(6) HC_NB(7) HC_NB(8)
+#undef HC_NB
+      }
+    }
   }
 }
 

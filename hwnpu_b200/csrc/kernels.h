@@ -52,7 +52,8 @@ struct GemvOut {
   unsigned long long *amax = nullptr;   // kLogits: [t], see argmax_key in misc.cu
 };
 
-// y = x W^T for ntok (1..8) tokens whose activations act_quant wrote into act.
+// y = x W^T for ntok (1..64) tokens whose activations act_quant wrote into act: up to 8 tokens a
+// token per MMA column group (gemv_kernel), 9..64 tokens on the MMA's n (gemm_tn_kernel).
 void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cudaStream_t st);
 
 // Quantises ntok rows of x (float32, stride ldx, n columns) into the GEMV's activation tiles

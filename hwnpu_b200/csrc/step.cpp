@@ -42,10 +42,22 @@ namespace {
 
 constexpr int kMaxSplits = 64;
 
-int splits_for(const hc_session *s, int n) {
+// Attention splits of every (token, kv head) of a chunk of n tokens whose longest context is
+// max_len positions: enough CTAs to fill the SMs twice, and at most 256 keys a split for the
+// longest (rounded up to a power of two, so that few step graphs differ by their splits).
+int splits_for(const hc_session *s, int n, int max_len) {
   const int kv = int(s->m->d.kv_heads);
   int sp = (2 * s->m->sms) / (kv * n);
-  return std::max(1, std::min(kMaxSplits, sp));
+  int by_len = 1;
+  while (by_len < kMaxSplits && by_len * 256 < max_len) by_len *= 2;
+  return std::max(1, std::min(kMaxSplits, std::max(sp, by_len)));
+}
+
+// The longest context (positions read, its own included) of the chunk's tokens in toks_host.
+int chunk_max_len(const hc_session *s, int n) {
+  int m = 0;
+  for (int i = 0; i < n; ++i) m = std::max(m, s->toks_host[i].pos + 1);
+  return m;
 }
 
 template <typename T>
@@ -110,13 +122,12 @@ void release_pages(hc_session *s, int seq, int len) {
 
 // Enqueues one chunk of n tokens (already in toks_dev) on the session's stream; returns the
 // number of kernels launched.
-int enqueue_chunk(hc_session *s, int n, bool accept) {
+int enqueue_chunk(hc_session *s, int n, bool accept, int splits) {
   hc_model *m = s->m;
   const auto &d = m->d;
   const int D = int(d.hidden), F = int(d.inter), H = int(d.heads), KV = int(d.kv_heads);
   const int hd = int(d.head_dim), V = int(d.vocab);
   const int W = (H + 2 * KV) * hd;
-  const int splits = splits_for(s, n);
   cudaStream_t st = s->st;
   int k = 0;
   hc::embed(s->toks_dev, n, m->embed, m->embed ? nullptr : &m->head->m, D, s->x, s->amax, st);
@@ -237,10 +248,11 @@ char *run_chunk(hc_session *s, int n, bool accept) {
   cudaStream_t st = s->st;
   const bool use_graph = !(s->o.flags & HC_SESSION_NO_GRAPH);
   const bool mk = !accept && mk_chunk(s, n);
-  const int key = n * 4 + (accept ? 1 : 0) + (mk ? 2 : 0);
+  const int splits = splits_for(s, n, chunk_max_len(s, n));
+  const int key = ((mk ? 0 : splits) * 128 + n) * 4 + (accept ? 1 : 0) + (mk ? 2 : 0);
   auto enqueue_all = [&]() -> int {
     cudaMemcpyAsync(s->toks_dev, s->toks_host, sizeof(hc::StepTok) * n, cudaMemcpyHostToDevice, st);
-    int k = mk ? enqueue_mk(s, n, false) : enqueue_chunk(s, n, accept);
+    int k = mk ? enqueue_mk(s, n, false) : enqueue_chunk(s, n, accept, splits);
     if (mk) cudaMemcpyAsync(s->mk_status_host, s->mk_status, sizeof(int), cudaMemcpyDeviceToHost, st);
     cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
     if (accept) cudaMemcpyAsync(s->res_host, s->res_dev, sizeof(int32_t) * 2, cudaMemcpyDeviceToHost, st);
@@ -319,7 +331,7 @@ char *mk_setup(hc_session *s) {
   cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->ordinal);
   if (!coop) return nullptr;
   s->mk_ctas = hc::mk_max_ctas(m->ordinal);
-  hc::MkParams probe = mk_params(s, kMaxChunk, false);
+  hc::MkParams probe = mk_params(s, hc::kMkMaxTok, false);
   const size_t smem = hc::mk_smem(probe, s->mk_ctas);
   if (smem == 0) return nullptr;
   HC_TRY_CUDA(hc::mk_prepare(225 * 1024));  // every layout mk_layout makes fits in it
@@ -474,6 +486,7 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
   HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
   size_t wi = 0;
   int row = 0;
+  double step_us = 0;  // the call's device time: the sum over its chunks
   for (size_t c0 = 0; c0 < all.size(); c0 += kMaxChunk) {
     const int n = int(std::min<size_t>(kMaxChunk, all.size() - c0));
     std::memcpy(s->toks_host, &all[c0], sizeof(hc::StepTok) * n);
@@ -490,6 +503,7 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
       if (state) *state = e ? HC_STATE_ERROR : st_;
       return e;
     }
+    step_us += s->stats.last_step_us;
     for (; wi < want.size() && size_t(want[wi]) < c0 + n; ++wi, ++row) {
       const int local = int(want[wi] - c0);
       if (argmax) argmax[row] = s->am_host[local];
@@ -500,6 +514,7 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
   const auto &md = s->m->d;
   for (auto &t : all) kv += uint64_t(t.pos + 1) * md.kv_heads * md.head_dim * 4 * md.layers;
   s->stats.kv_bytes = kv;
+  s->stats.last_step_us = step_us;
   for (int i = 0; i < nseq; ++i) s->pos[seq_ids[i]] += n_tokens[i];
   s->stats.steps++;
   s->stats.tokens += all.size();
@@ -569,7 +584,7 @@ HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, i
       hc::mk_launch(mk_params(s, 1, true), s->mk_ctas, st);
       s->launches_per_chunk[0] = 1;
     } else {
-      s->launches_per_chunk[0] = uint64_t(enqueue_chunk(s, 1, false)) + 1;
+      s->launches_per_chunk[0] = uint64_t(enqueue_chunk(s, 1, false, splits_for(s, 1, 0))) + 1;
       hc::advance(s->toks_dev, s->am_dev, s->gen_out, s->gen_count, st);
     }
     cudaError_t e = cudaStreamEndCapture(st, &graph);

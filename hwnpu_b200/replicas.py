@@ -1,8 +1,8 @@
 """Multi-GPU by replicas (no collective on the decode path).
 
 Sequences are independent, so a job of several GPUs runs one engine replica a GPU with the
-weights replicated, and splits the sequences between them round robin (the partition SURVEY
-section 8(e) of this build names for the ragged-batch config). The only cross-rank traffic is the
+weights replicated, and splits the sequences between them round robin (the partition of the
+64-sequence ragged-batch workload). The only cross-rank traffic is the
 timing: the job's time is the slowest replica's, and its throughput is the tokens of all replicas
 over that time. Works over any torch.distributed backend (gloo on CPU for the tests, NCCL on the
 GPUs).

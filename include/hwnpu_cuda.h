@@ -226,8 +226,8 @@ enum {
 typedef struct hc_session_opts {
   uint32_t max_context;  /* positions a sequence may hold (Session.Cache) */
   uint32_t max_seqs;     /* sequence slots */
-  uint32_t max_step;     /* most tokens hc_speculate verifies in one call (1..8); hc_step reads
-                          * any number, in passes of up to 8 tokens over the weights */
+  uint32_t max_step;     /* most tokens hc_speculate verifies in one call (1..64); hc_step reads
+                          * any number, in passes of up to 64 tokens over the weights */
   uint32_t kv_format;    /* HC_KV_* */
   uint32_t page_size;    /* positions a page (HC_KV_INT8_PAGED), 16 */
   uint32_t flags;        /* HC_SESSION_* */
@@ -295,7 +295,7 @@ typedef struct hc_stats {
   uint64_t launches;       /* kernels launched (graph nodes included) */
   uint64_t weight_bytes;   /* weight bytes read by the last step */
   uint64_t kv_bytes;       /* KV bytes read by the last step */
-  double last_step_us;     /* device time of the last step (CUDA events) */
+  double last_step_us;     /* device time of the last call (CUDA events; the sum over its chunks) */
 } hc_stats;
 
 HC_API char *hc_stats_get(hc_session *s, hc_stats *out);

@@ -79,7 +79,7 @@ def test_int4_known_answer_through_tiles(device):
 
 @pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
-@pytest.mark.parametrize("ntok", [1, 3, 8, 11])
+@pytest.mark.parametrize("ntok", [1, 3, 8, 11, 37, 64, 70])
 def test_gemv(device, fmt, shape, ntok):
     rows, cols = shape
     w = synth.normal(5, f"g{rows}x{cols}", rows * cols, 0.02).reshape(rows, cols)

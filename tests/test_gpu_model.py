@@ -125,12 +125,13 @@ def test_megakernel_batch_of_four(device, models):
 
 
 def test_all_rows_and_chunking(device, models):
-    # 11 tokens in one call cross the 8-token chunks; every row against the oracle's
+    # 75 tokens in one call cross the 64-token chunks (a batched chunk, then 11 tokens); every row
+    # against the oracle's
     model = get(models, TINY)
     lm = device.load_model(model)
-    sess = lm.session(max_context=32, max_step=16)
-    ref = O.OracleSession(model, 32)
-    toks = list(synth.tokens(3, TINY.vocab, 11))
+    sess = lm.session(max_context=96, max_step=16)
+    ref = O.OracleSession(model, 96)
+    toks = list(synth.tokens(3, TINY.vocab, 75))
     got = sess.step_tokens(toks, all_rows=True)
     want = synth.f16_values(ref.step(toks, all_rows=True))
     for r in range(len(toks)):
@@ -197,6 +198,36 @@ def test_ragged_batch_equals_single_sequences(device, models):
         la, aa = alone[i].step_batch([0], [prompts[i]])
         assert ab[i] == aa[0]
         assert np.abs(synth.f16_values(lb[i]) - synth.f16_values(la[0])).max() <= 5e-3
+    for s in alone:
+        s.close()
+    batch.close()
+    lm.close()
+
+
+@pytest.mark.parametrize("kv_format", [A.HC_KV_F16, A.HC_KV_INT8_PAGED], ids=["f16", "int8paged"])
+def test_wide_batch_equals_single_sequences(device, models, kv_format):
+    # 20 sequences of ragged contexts decode one token each in one call (the batched GEMV, tokens
+    # on the MMA's n) and read the logits and choices each reads alone (a token a call)
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    n = 20
+    batch = lm.session(max_context=48, max_seqs=n, kv_format=kv_format)
+    alone = [lm.session(max_context=48, kv_format=kv_format) for _ in range(n)]
+    prompts = [list(synth.tokens(60 + i, TINY.vocab, 1 + (7 * i) % 23)) for i in range(n)]
+    nxt = []
+    for i in range(n):
+        _, am = batch.step_batch([i], [prompts[i]])
+        alone[i].step_batch([0], [prompts[i]])
+        nxt.append(int(am[0]))
+    for _ in range(2):
+        lb, ab = batch.step_batch(list(range(n)), [[t] for t in nxt])
+        for i in range(n):
+            la, aa = alone[i].step_batch([0], [[nxt[i]]])
+            assert np.abs(synth.f16_values(lb[i]) - synth.f16_values(la[0])).max() <= 5e-3
+            v = synth.f16_values(la[0])
+            if top2_margin(v) > 1e-2:
+                assert ab[i] == aa[0]
+        nxt = [int(x) for x in ab]
     for s in alone:
         s.close()
     batch.close()
