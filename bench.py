@@ -301,6 +301,18 @@ def run_c5(args, rank, world, local, dist):
 
     W = max(3, args.warmup)
     run(W, False)
+    if args.profile:  # a few steps between cudaProfilerStart/Stop (for ncu --profile-from-start off)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        dec, prm, dev_ms, _ = run(args.profile, True)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profiled_steps": args.profile, "decoded": dec, "prompt_tokens": prm,
+                          "device_ms": dev_ms}), flush=True)
+        sess.close()
+        lm.close()
+        dev.close()
+        return
     launches0 = sess.stats()["launches"]
     clocks = Clocks(local)
     if dist:
@@ -360,6 +372,58 @@ def run_c5(args, rank, world, local, dist):
     print(json.dumps(line), flush=True)
 
 
+def run_linear(args, local):
+    """One C2-shaped matrix (hc_linear_load) run over --ntok tokens (hc_linear_run), timed with CUDA
+    events on torch's stream: the GEMV kernels alone, for tuning and for ncu on a small case."""
+    import ctypes as C
+
+    import torch
+
+    import hwnpu_b200 as hb
+    from hwnpu_b200 import _abi as A
+    from hwnpu_b200 import synth
+
+    torch.cuda.set_device(local)
+    dev = hb.Device(local)
+    rows, cols, n = args.rows, args.cols, args.ntok
+    w = synth.normal(5, f"lin{rows}x{cols}", rows * cols, 0.02).reshape(rows, cols)
+    lin = synth.Linear.quantize(w, A.HC_FMT_INT4_ASYM_G32)
+    h = C.c_void_p()
+    A.check(A.lib().hc_linear_load(dev.h, C.byref(lin.desc()), C.byref(h)))
+    x = torch.randn(n, cols, device="cuda")
+    y = torch.empty(n, rows, device="cuda")
+    cs = torch.cuda.current_stream()
+
+    def once():
+        A.check(A.lib().hc_linear_run(h, C.c_void_p(x.data_ptr()), n, C.c_void_p(y.data_ptr()), C.c_void_p(cs.cuda_stream)))
+
+    for _ in range(max(3, args.warmup)):
+        once()
+    if args.profile:
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        for _ in range(args.profile):
+            once()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+    reps = max(1, args.steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cs)
+    for _ in range(reps):
+        once()
+    e1.record(cs)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    wbytes = lin.data.nbytes + lin.scales.nbytes + (lin.zeros.nbytes if lin.zeros is not None else 0)
+    peak, kind = peaks()
+    print(json.dumps({"workload": "linear", "rows": rows, "cols": cols, "ntok": n, "us_per_call": ms * 1e3,
+                      "weight_gbs": wbytes / (ms / 1e3) / 1e9, "frac_hbm": wbytes / (ms / 1e3) / 1e9 / peak,
+                      "int_tops_useful": 2.0 * rows * cols * n / (ms / 1e3) / 1e12,
+                      "note": "includes the activation quantiser launch(es)"}), flush=True)
+    A.lib().hc_linear_free(h)
+    dev.close()
+
+
 def workload_config(args):
     return {"workload": f"{args.workload.upper()} bs1 greedy decode: 1024-id random prompt, passes of 256 steps "
                         f"(context 1024-1280)",
@@ -375,7 +439,10 @@ def main():
     ap.add_argument("--steps", type=int, default=2560)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c1", "c4", "c5"], default="c2",
+    ap.add_argument("--rows", type=int, default=12288, help="--workload linear: matrix rows")
+    ap.add_argument("--cols", type=int, default=2048, help="--workload linear: matrix columns")
+    ap.add_argument("--ntok", type=int, default=64, help="--workload linear: tokens a call")
+    ap.add_argument("--workload", choices=["c2", "c1", "c4", "c5", "linear"], default="c2",
                     help="c2: the headline bs1 decode; c1: the small int8 model; c4: speculative decoding "
                          "(C1-shaped int8 draft with V151936 -> C2 target, k=4, 512 tokens from a 512-id prompt); "
                          "c5: 64 ragged sequences over a paged int8 KV cache, sharded over the ranks")
@@ -396,6 +463,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "linear":
+        run_linear(args, local)
         return
 
     import numpy as np

@@ -13,6 +13,14 @@
 namespace hc {
 namespace {
 
+// The batched activation layout (9..64 tokens in nb blocks of 8): per (k-tile kt, group G, block
+// b) 576 bytes at act_tn_offset: lane (g, c) of the MMA reads its B registers as the 16 bytes at
+// 16 (4g + c) -- token 8b + g's hi bytes 4c..4c+3 and 16+4c..19+4c of the group, then its lo bytes
+// likewise -- and the (S, X) of tokens 8b + 2c, 8b + 2c + 1 as the 16 bytes at 512 + 16c.
+__device__ __forceinline__ size_t act_tn_offset(int kt, int G, int b, int nb) {
+  return (size_t(kt * kGroupsPerTile + G) * nb + b) * kActTile;
+}
+
 // The end of both GEMV kernels: part[w][t][r] holds warp w's sum for token t and row r of its row
 // tile; the wpr warps of a row tile are added, scaled and written as out.mode says, for tokens
 // t < nt. Ends with the argmax atomics of kLogits (bmax is the CTA's per-token key, zeroed before).
@@ -158,8 +166,6 @@ __global__ void __launch_bounds__(256) gemm_tn_kernel(const uint8_t *__restrict_
       const uint8_t *tile = tiles + (size_t(rt) * ktiles + kt) * TB;
       if (kt + wpr < ktiles && lane < kLines)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(tile + size_t(wpr) * TB + lane * 128));
-      const uint8_t *at = act + size_t(kt) * kActTile;  // token t's tile at + t * ktiles * kActTile
-      const size_t tstride = size_t(ktiles) * kActTile;
 #pragma unroll 1
       for (int G = 0; G < kGroupsPerTile; ++G) {
         const int h = G >> 2, Ls = 4 * g + (G & 3);
@@ -193,21 +199,13 @@ __global__ void __launch_bounds__(256) gemm_tn_kernel(const uint8_t *__restrict_
         }
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-          const int tb = 8 * b + g;        // the token of this lane's B column
-          const int t0 = 8 * b + 2 * c;    // the tokens of this lane's D columns: t0, t0 + 1
-          uint32_t bh0 = 0, bh1 = 0, bl0 = 0, bl1 = 0;
-          if (tb < ntok) {
-            const uint8_t *ab = at + tb * tstride + G * 64 + 4 * c;
-            bh0 = ldg32(ab);
-            bh1 = ldg32(ab + 16);
-            if (KIND != kKindMx) {
-              bl0 = ldg32(ab + 32);
-              bl1 = ldg32(ab + 48);
-            }
-          }
-          float2 x0 = make_float2(0.f, 0.f), x1 = x0;
-          if (t0 < ntok) x0 = __ldg(reinterpret_cast<const float2 *>(at + t0 * tstride + kGroupsPerTile * 64 + G * 8));
-          if (t0 + 1 < ntok) x1 = __ldg(reinterpret_cast<const float2 *>(at + (t0 + 1) * tstride + kGroupsPerTile * 64 + G * 8));
+          // B registers of token 8b + g and the (S, X) of tokens 8b + 2c, 8b + 2c + 1 (the lane's D
+          // columns); the padding tokens of the last block are zero groups
+          const uint8_t *blk = act + act_tn_offset(kt, G, b, NB);
+          const uint4 bq = __ldg(reinterpret_cast<const uint4 *>(blk) + lane);
+          const float4 sx = __ldg(reinterpret_cast<const float4 *>(blk + 512) + c);
+          const uint32_t bh0 = bq.x, bh1 = bq.y, bl0 = bq.z, bl1 = bq.w;
+          const float2 x0 = make_float2(sx.x, sx.y), x1 = make_float2(sx.z, sx.w);
           int dh[4] = {0, 0, 0, 0};
           if (KIND == kKindInt4) mma_u8s8(dh, a[0], a[1], a[2], a[3], bh0, bh1);
           else mma_s8s8(dh, a[0], a[1], a[2], a[3], bh0, bh1);
@@ -297,41 +295,65 @@ __device__ double block_sum_d(double v, double *sh) {
 }
 
 // One warp quantises one group of 32 values (v is this lane's): hi = round_even(v * 127 / max),
-// the residual in lo at 1/256 of the scale (see common.h's kActTile).
-__device__ __forceinline__ void quant_group(float v, uint8_t *act_tile, int gi, int lane) {
+// the residual in lo at 1/256 of the scale (see common.h's kActTile); X is the group's sum of
+// (hi + lo / 256), the same on every lane.
+struct QGroup {
+  int8_t hq, lq;
+  float S, X;
+};
+__device__ __forceinline__ QGroup quant_vals(float v) {
   const float m = warp_max(fabsf(v));
-  int8_t hq = 0, lq = 0;
-  float S = 0.f;
-  int s256 = 0;
+  QGroup q{0, 0, 0.f, 0.f};
   if (m > 0.f) {
     const float inv = 127.0f / m;  // mxfp4.Vec.Quantize's inv (mxfp4.go:44)
-    S = m / 127.0f;
+    q.S = m / 127.0f;
     const float h = rintf(v * inv);
-    const float r = fmaf(-h, S, v);
+    const float r = fmaf(-h, q.S, v);
     const float l = fminf(fmaxf(rintf(r * (256.0f * inv)), -127.f), 127.f);
-    hq = int8_t(h);
-    lq = int8_t(l);
-    s256 = warp_sum_i(int(hq) * 256 + int(lq));
+    q.hq = int8_t(h);
+    q.lq = int8_t(l);
+    q.X = float(warp_sum_i(int(q.hq) * 256 + int(q.lq))) * (1.0f / 256.0f);
   }
-  act_tile[gi * 64 + lane] = uint8_t(hq);
-  act_tile[gi * 64 + 32 + lane] = uint8_t(lq);
-  if (lane == 0) {
-    float2 *sx = reinterpret_cast<float2 *>(act_tile + kGroupsPerTile * 64 + gi * 8);
-    *sx = make_float2(S, float(s256) * (1.0f / 256.0f));
-  }
+  return q;
+}
+
+// Token-major tiles (up to 8 tokens): group gi of the tile at act_tile.
+__device__ __forceinline__ void quant_group(float v, uint8_t *act_tile, int gi, int lane) {
+  const QGroup q = quant_vals(v);
+  act_tile[gi * 64 + lane] = uint8_t(q.hq);
+  act_tile[gi * 64 + 32 + lane] = uint8_t(q.lq);
+  if (lane == 0) *reinterpret_cast<float2 *>(act_tile + kGroupsPerTile * 64 + gi * 8) = make_float2(q.S, q.X);
+}
+
+// The batched layout: group G of k-tile kt for token t.
+__device__ __forceinline__ void quant_group_tn(float v, uint8_t *act, int kt, int G, int t, int nb, int lane) {
+  const QGroup q = quant_vals(v);
+  uint8_t *blk = act + act_tn_offset(kt, G, t / 8, nb);
+  const int g = t % 8, c = (lane % 16) / 4, at = (4 * g + c) * 16 + (lane / 16) * 4 + lane % 4;
+  blk[at] = uint8_t(q.hq);
+  blk[at + 8] = uint8_t(q.lq);
+  if (lane == 0) *reinterpret_cast<float2 *>(blk + 512 + g * 8) = make_float2(q.S, q.X);
 }
 
 // One CTA per (token, column tile): the RMS norm's sum of squares is taken over the whole row by
 // every CTA (the row is a few KB in L2), then the CTA quantises its tile's 8 groups, one warp each.
+// With nb > 0 the tiles take the batched layout, and the rows past ntok of the last block of 8
+// are written as zero groups.
 __global__ void __launch_bounds__(256) act_quant_kernel(const float *__restrict__ x, int ldx,
                                                         int n, const float *__restrict__ norm_w,
                                                         float scale, float eps16,
-                                                        uint8_t *__restrict__ act, int ktiles) {
+                                                        uint8_t *__restrict__ act, int ktiles,
+                                                        int ntok, int nb, const StepTok *__restrict__ rows) {
   __shared__ double red[32];
   pdl_trigger();
   pdl_wait();
   const int t = blockIdx.y, kt = blockIdx.x;
-  const float *xt = x + size_t(t) * ldx;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (t >= ntok) {  // padding of the batched layout (uniform over the CTA)
+    quant_group_tn(0.f, act, kt, warp, t, nb, lane);
+    return;
+  }
+  const float *xt = x + size_t(rows ? rows[t].head_src : t) * ldx;
   const float inv = scale == 1.f ? 1.f : 1.f / scale;
   float r = 1.f;
   if (norm_w) {
@@ -345,7 +367,6 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const float *__restrict_
     const float ms = float(s / double(n));
     r = float(1.0 / sqrt(double(ms) + double(eps16)));
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col = (kt * kGroupsPerTile + warp) * kGroup + lane;
   float v = 0.f;
   if (col < n) {
@@ -356,7 +377,8 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const float *__restrict_
       v = y * norm_w[col];
     }
   }
-  quant_group(v, act + (size_t(t) * ktiles + kt) * kActTile, warp, lane);
+  if (nb) quant_group_tn(v, act, kt, warp, t, nb, lane);
+  else quant_group(v, act + (size_t(t) * ktiles + kt) * kActTile, warp, lane);
 }
 
 // Merges the attention partials of one (token, head) (Flash-Decoding; with a sink logit when
@@ -367,7 +389,7 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict
                                                          const float *__restrict__ sinks,
                                                          int heads, int hd, int splits,
                                                          uint8_t *__restrict__ act, int ktiles,
-                                                         float *__restrict__ o_out) {
+                                                         int nb, float *__restrict__ o_out) {
   __shared__ float wsh[64];
   __shared__ float stat[2];
   pdl_trigger();
@@ -415,7 +437,8 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict
     // one warp a group of 32: warp w of this head holds columns h*hd + 32w .. + 31
     const int gcol = h * hd + d;
     const int grp = gcol / kGroup;
-    quant_group(o, act + (size_t(t) * ktiles + grp / kGroupsPerTile) * kActTile, grp % kGroupsPerTile, lane);
+    if (nb) quant_group_tn(o, act, grp / kGroupsPerTile, grp % kGroupsPerTile, t, nb, lane);
+    else quant_group(o, act + (size_t(t) * ktiles + grp / kGroupsPerTile) * kActTile, grp % kGroupsPerTile, lane);
   }
 }
 
@@ -444,21 +467,26 @@ void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cud
 }
 
 void act_quant(const float *x, int ldx, int n, int ntok, const float *norm_w, float scale,
-               float eps16, uint8_t *act, int ktiles, cudaStream_t st) {
-  launch_pdl(act_quant_kernel, dim3(ktiles, ntok), dim3(256), 0, st, x, ldx, n, norm_w, scale, eps16, act, ktiles);
+               float eps16, uint8_t *act, int ktiles, cudaStream_t st, const StepTok *rows) {
+  const int nb = act_tn_blocks(ntok);
+  launch_pdl(act_quant_kernel, dim3(ktiles, nb ? 8 * nb : ntok), dim3(256), 0, st, x, ldx, n, norm_w, scale, eps16,
+             act, ktiles, ntok, nb, rows);
 }
 
 void attn_merge_quant(const float *part_ml, const float *part_o, const float *sinks, int ntok,
                       int heads, int hd, int splits, uint8_t *act, int ktiles, float *o_out,
-                      cudaStream_t st) {
-  // columns past heads*hd in the last tile are zero groups
+                      cudaStream_t st, bool batched_layout) {
+  const int nb = batched_layout ? act_tn_blocks(ntok) : 0;
+  // columns past heads*hd in the last tile are zero groups; so are the padding tokens of a batch
   const int n = heads * hd;
-  if (n % kTileCols) {
+  if (nb) {
+    cudaMemsetAsync(act, 0, size_t(ktiles) * kGroupsPerTile * nb * kActTile, st);
+  } else if (n % kTileCols) {
     for (int t = 0; t < ntok; ++t)
       cudaMemsetAsync(act + (size_t(t) * ktiles + ktiles - 1) * kActTile, 0, kActTile, st);
   }
   launch_pdl(attn_merge_kernel, dim3(heads, ntok), dim3(hd), 0, st, part_ml, part_o, sinks, heads, hd, splits, act,
-             ktiles, o_out);
+             ktiles, nb, o_out);
 }
 
 void dequant(const DevMat &W, int row0, int nrows, float *out, cudaStream_t st) {

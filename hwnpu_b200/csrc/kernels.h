@@ -56,26 +56,33 @@ struct GemvOut {
 // token per MMA column group (gemv_kernel), 9..64 tokens on the MMA's n (gemm_tn_kernel).
 void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cudaStream_t st);
 
-// Quantises ntok rows of x (float32, stride ldx, n columns) into the GEMV's activation tiles
-// (ktiles of kActTile bytes a token), after an optional RMS norm: when norm_w is set,
-// x is normed as qwen3's normScaled with scale (1 or 64) and epsilon eps16 (the fp16 constant
-// f16(eps / scale^2)) and multiplied by norm_w (float32 values of fp16 weights).
-void act_quant(const float *x, int ldx, int n, int ntok, const float *norm_w, float scale,
-               float eps16, uint8_t *act, int ktiles, cudaStream_t st);
-
-// Attention partials -> merged o (float32 [ntok][heads*hd]) -> activation tiles of the output
-// projection (Flash-Decoding's merge with gpt-oss's sinks, paged.go:252-310).
-void attn_merge_quant(const float *part_ml, const float *part_o, const float *sinks, int ntok,
-                      int heads, int hd, int splits, uint8_t *act, int ktiles, float *o_out,
-                      cudaStream_t st);
-
 // Per-token position data of a step, in device memory so that a captured graph replays it.
 struct StepTok {
   int32_t token;  // id
   int32_t slot;   // sequence slot
   int32_t pos;    // position of this token
-  int32_t pad_;
+  int32_t head_src;  // entry j < the chunk's head rows: the chunk token whose logits are row j
 };
+
+// Blocks of 8 tokens of the batched activation layout that 9..64 tokens take (0: token-major).
+inline int act_tn_blocks(int ntok) { return ntok > 8 ? (ntok + 7) / 8 : 0; }
+
+// Quantises ntok rows of x (float32, stride ldx, n columns) into the GEMV's activation tiles
+// (ktiles of kActTile bytes a token; for 9..64 tokens the batched layout of 8 act_tn_blocks(ntok)
+// token rows, padding included), after an optional RMS norm: when norm_w is set,
+// x is normed as qwen3's normScaled with scale (1 or 64) and epsilon eps16 (the fp16 constant
+// f16(eps / scale^2)) and multiplied by norm_w (float32 values of fp16 weights).
+// With rows set, token t's input is row rows[t].head_src of x (the head's rows of a chunk).
+void act_quant(const float *x, int ldx, int n, int ntok, const float *norm_w, float scale,
+               float eps16, uint8_t *act, int ktiles, cudaStream_t st, const StepTok *rows = nullptr);
+
+// Attention partials -> merged o (float32 [ntok][heads*hd]) -> activation tiles of the output
+// projection (Flash-Decoding's merge with gpt-oss's sinks, paged.go:252-310); batched_layout: the
+// tiles as act_quant lays out ntok tokens for the GEMV (else token-major, ntok tiles a k-tile).
+void attn_merge_quant(const float *part_ml, const float *part_o, const float *sinks, int ntok,
+                      int heads, int hd, int splits, uint8_t *act, int ktiles, float *o_out,
+                      cudaStream_t st, bool batched_layout = false);
+
 
 struct AttnGeom {
   int heads, kv_heads, hd, cap, window;  // cap: positions a slot's cache holds

@@ -121,8 +121,9 @@ void release_pages(hc_session *s, int seq, int len) {
 }
 
 // Enqueues one chunk of n tokens (already in toks_dev) on the session's stream; returns the
-// number of kernels launched.
-int enqueue_chunk(hc_session *s, int n, bool accept, int splits) {
+// number of kernels launched. Only `heads` rows go through the final norm and the head: row j is
+// chunk token toks[j].head_src (the rows a caller reads; none for the inside of a long prompt).
+int enqueue_chunk(hc_session *s, int n, bool accept, int splits, int heads) {
   hc_model *m = s->m;
   const auto &d = m->d;
   const int D = int(d.hidden), F = int(d.inter), H = int(d.heads), KV = int(d.kv_heads);
@@ -150,7 +151,7 @@ int enqueue_chunk(hc_session *s, int n, bool accept, int splits) {
       ++k;
     }
     hc::attn_split(s->q, s->toks_dev, n, g, kcl, vcl, splits, s->part_ml, s->part_o, st, s->paged ? &pk : nullptr);
-    hc::attn_merge_quant(s->part_ml, s->part_o, w.sinks, n, H, hd, splits, s->act, w.o->m.ktiles, nullptr, st);
+    hc::attn_merge_quant(s->part_ml, s->part_o, w.sinks, n, H, hd, splits, s->act, w.o->m.ktiles, nullptr, st, true);
     hc::GemvOut o2;
     o2.mode = hc::kAdd; o2.y = s->x; o2.ldy = D;
     hc::gemv(w.o->m, s->act, n, o2, st);
@@ -162,12 +163,15 @@ int enqueue_chunk(hc_session *s, int n, bool accept, int splits) {
     hc::gemv(w.down->m, s->act, n, o2, st);
     k += 10;
   }
-  hc::act_quant(s->x, D, D, n, m->final_norm, m->norm_head.scale, m->norm_head.eps16, s->act, m->head->m.ktiles, st);
-  hc::GemvOut oh;
-  oh.mode = hc::kLogits; oh.ldy = V; oh.logits = s->logits_dev; oh.amax = s->amax;
-  hc::gemv(m->head->m, s->act, n, oh, st);
-  hc::amax_to_index(s->amax, n, s->am_dev, st);
-  k += 3;
+  if (heads > 0) {
+    hc::act_quant(s->x, D, D, heads, m->final_norm, m->norm_head.scale, m->norm_head.eps16, s->act,
+                  m->head->m.ktiles, st, heads == n ? nullptr : s->toks_dev);
+    hc::GemvOut oh;
+    oh.mode = hc::kLogits; oh.ldy = V; oh.logits = s->logits_dev; oh.amax = s->amax;
+    hc::gemv(m->head->m, s->act, heads, oh, st);
+    hc::amax_to_index(s->amax, heads, s->am_dev, st);
+    k += 3;
+  }
   if (accept) { hc::spec_accept(s->am_dev, s->toks_dev, n, s->res_dev, st); ++k; }
   return k;
 }
@@ -241,20 +245,21 @@ bool mk_chunk(const hc_session *s, int n) {
   return true;
 }
 
-// The whole chunk: tokens in, greedy choices (and the accept result) out, as one graph.
-char *run_chunk(hc_session *s, int n, bool accept) {
+// The whole chunk: tokens in, greedy choices (and the accept result) out, as one graph. heads:
+// the rows read out (toks_host[j].head_src for j < heads; all n rows for accept).
+char *run_chunk(hc_session *s, int n, bool accept, int heads) {
   for (int i = 0; i < n; ++i)
     if (char *e = ensure_pages(s, s->toks_host[i].slot, s->toks_host[i].pos, s->toks_host[i].pos + 1)) return e;
   cudaStream_t st = s->st;
   const bool use_graph = !(s->o.flags & HC_SESSION_NO_GRAPH);
-  const bool mk = !accept && mk_chunk(s, n);
+  const bool mk = !accept && heads == n && mk_chunk(s, n);
   const int splits = splits_for(s, n, chunk_max_len(s, n));
-  const int key = ((mk ? 0 : splits) * 128 + n) * 4 + (accept ? 1 : 0) + (mk ? 2 : 0);
+  const int key = (((mk ? 0 : splits) * 128 + n) * 128 + heads) * 4 + (accept ? 1 : 0) + (mk ? 2 : 0);
   auto enqueue_all = [&]() -> int {
     cudaMemcpyAsync(s->toks_dev, s->toks_host, sizeof(hc::StepTok) * n, cudaMemcpyHostToDevice, st);
-    int k = mk ? enqueue_mk(s, n, false) : enqueue_chunk(s, n, accept, splits);
+    int k = mk ? enqueue_mk(s, n, false) : enqueue_chunk(s, n, accept, splits, heads);
     if (mk) cudaMemcpyAsync(s->mk_status_host, s->mk_status, sizeof(int), cudaMemcpyDeviceToHost, st);
-    cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
+    if (heads > 0) cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * heads, cudaMemcpyDeviceToHost, st);
     if (accept) cudaMemcpyAsync(s->res_host, s->res_dev, sizeof(int32_t) * 2, cudaMemcpyDeviceToHost, st);
     return k;
   };
@@ -490,8 +495,10 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
   for (size_t c0 = 0; c0 < all.size(); c0 += kMaxChunk) {
     const int n = int(std::min<size_t>(kMaxChunk, all.size() - c0));
     std::memcpy(s->toks_host, &all[c0], sizeof(hc::StepTok) * n);
+    int heads = 0;  // the chunk's rows that are read out, in order
+    for (size_t w = wi; w < want.size() && size_t(want[w]) < c0 + n; ++w) s->toks_host[heads++].head_src = int(want[w] - c0);
     if (s->mk_status_host) *s->mk_status_host = 0;
-    if (char *e = run_chunk(s, n, false)) {
+    if (char *e = run_chunk(s, n, false, heads)) {
       for (int i = 0; i < nseq; ++i) s->poisoned[seq_ids[i]] = true;
       return e;
     }
@@ -504,10 +511,9 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
       return e;
     }
     step_us += s->stats.last_step_us;
-    for (; wi < want.size() && size_t(want[wi]) < c0 + n; ++wi, ++row) {
-      const int local = int(want[wi] - c0);
-      if (argmax) argmax[row] = s->am_host[local];
-      if (logits) HC_TRY_CUDA(cudaMemcpy(logits + size_t(row) * V, s->logits_dev + size_t(local) * V, size_t(V) * 2, cudaMemcpyDeviceToHost));
+    for (int j = 0; wi < want.size() && size_t(want[wi]) < c0 + n; ++wi, ++row, ++j) {
+      if (argmax) argmax[row] = s->am_host[j];
+      if (logits) HC_TRY_CUDA(cudaMemcpy(logits + size_t(row) * V, s->logits_dev + size_t(j) * V, size_t(V) * 2, cudaMemcpyDeviceToHost));
     }
   }
   uint64_t kv = 0;
@@ -535,11 +541,11 @@ HC_API char *hc_speculate(hc_session *s, int32_t seq, const int32_t *toks, int32
   const int V = int(s->m->d.vocab);
   for (int j = 0; j < n; ++j) {
     if (toks[j] < 0 || toks[j] >= V) return hc::make_error("hc_speculate: token out of the vocabulary");
-    s->toks_host[j] = hc::StepTok{toks[j], seq, s->pos[seq] + j, 0};
+    s->toks_host[j] = hc::StepTok{toks[j], seq, s->pos[seq] + j, j};
   }
   if (hc::fault_fires(hc::kFaultStep)) return hc::make_error("injected fault: step");
   HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
-  if (char *e = run_chunk(s, n, true)) { s->poisoned[seq] = true; return e; }
+  if (char *e = run_chunk(s, n, true, n)) { s->poisoned[seq] = true; return e; }
   int32_t st_ = HC_STATE_ERROR;
   char *e = wait_done(s, timeout_ms, &st_);
   if (e || st_ != HC_STATE_COMPLETED) {
@@ -584,7 +590,7 @@ HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, i
       hc::mk_launch(mk_params(s, 1, true), s->mk_ctas, st);
       s->launches_per_chunk[0] = 1;
     } else {
-      s->launches_per_chunk[0] = uint64_t(enqueue_chunk(s, 1, false, splits_for(s, 1, 0))) + 1;
+      s->launches_per_chunk[0] = uint64_t(enqueue_chunk(s, 1, false, splits_for(s, 1, 0), 1)) + 1;
       hc::advance(s->toks_dev, s->am_dev, s->gen_out, s->gen_count, st);
     }
     cudaError_t e = cudaStreamEndCapture(st, &graph);
