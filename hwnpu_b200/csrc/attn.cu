@@ -354,14 +354,25 @@ __global__ void __launch_bounds__(128) kv_append_int8_kernel(const float *__rest
       s_new = __half2float(__float2half_ru(m / 127.0f));
       if (off > 0 && s_old > 0.f) {
         // requantise the page's earlier rows to the larger scale
+        // (rows 0..off-1 are contiguous: 16 bytes a lane a pass, at most 4 passes)
         const float f = s_old / s_new;
-        for (int r = 0; r < off; ++r) {
-          int8_t *row = pool + (ph * kPage + r) * HD;
+        uint4 *rows = reinterpret_cast<uint4 *>(pool + ph * kPage * HD);
+        const int n16 = off * HD / 16;
+#pragma unroll 4
+        for (int i = lane; i < n16; i += 32) {
+          uint4 w = rows[i];
+          uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-          for (int k = 0; k < E; ++k) {
-            const int e = lane + 32 * k;
-            row[e] = int8_t(fminf(fmaxf(rintf(float(row[e]) * f), -127.f), 127.f));
+          for (int k = 0; k < 4; ++k) {
+            uint32_t o = 0;
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) {
+              const float q = float(int8_t((u[k] >> (8 * bb)) & 0xff));
+              o |= uint32_t(uint8_t(int8_t(fminf(fmaxf(rintf(q * f), -127.f), 127.f)))) << (8 * bb);
+            }
+            u[k] = o;
           }
+          rows[i] = make_uint4(u[0], u[1], u[2], u[3]);
         }
       }
       if (lane == 0) scales[ph] = __half_as_ushort(__float2half_rn(s_new));

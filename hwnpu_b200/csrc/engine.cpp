@@ -210,6 +210,7 @@ HC_API char *hc_linear_load(hc_device *d, const hc_linear_desc *desc, hc_linear 
   *out = nullptr;
   if (!int_format(desc->format)) return hc::make_error("hc_linear_load: not an integer format");
   HC_TRY_CUDA(cudaSetDevice(hc::device_ordinal(d)));
+  if (char *e = hc::gemv_prepare()) return e;
   auto l = std::make_unique<hc_linear>();
   l->ordinal = hc::device_ordinal(d);
   if (char *e = hc::load_linear(hc::rows_of(*desc), &l->w, nullptr)) return e;

@@ -7,6 +7,8 @@
 // rows, the exact integer dot products of 8 columns of 4 groups at once (common.h). Lane (g, c)
 // then scales its rows g, g+8 by the weight scale (and zero point) and the activation's scale of
 // its groups c and 4 + c in float32; 2 shuffles add the 4 lanes of a row.
+#include <mutex>
+
 #include "device.cuh"
 #include "kernels.h"
 
@@ -131,6 +133,18 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint8_t *__restrict__ t
 // 16 rows x 8 tokens, which lane (g, c) scales for rows g, g + 8 and tokens 2c, 2c + 1 with the
 // same float32 arithmetic as the token-a-column GEMV (wa_mma): s S (hi + lo/256 - z Xq) for int4,
 // S (hi + lo/256) for int8, 2^(e-127) S hi for mxfp4.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Dynamic shared memory of gemm_tn_kernel<KIND, nb>: 8 warps x 2 stages of nb x 576 bytes (the
+// larger of that and the 8 x 8nb x 16 float partials).
+constexpr int gemm_tn_smem(int nb) { return 8 * 2 * nb * kActTile; }
+
 __device__ __forceinline__ uint32_t ldg32(const uint8_t *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
 __device__ __forceinline__ uint2 ldg64(const uint8_t *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
 
@@ -143,13 +157,17 @@ __global__ void __launch_bounds__(256) gemm_tn_kernel(const uint8_t *__restrict_
                                                       GemvOut out) {
   constexpr int TB = KIND == kKindInt8 ? kTileInt8 : (KIND == kKindInt4 ? kTileInt4 : kTileMx);
   constexpr int NT = 8 * NB;
-  __shared__ float part[8][NT][kTileRows];
+  constexpr int SB = NB * kActTile;  // one (k-tile, group)'s B operands of all the tokens
+  // dynamic shared memory (gemm_tn_smem): each warp's two stages of B, later the CTA's partials
+  extern __shared__ __align__(16) uint8_t tn_smem[];
+  float (*part)[NT][kTileRows] = reinterpret_cast<float (*)[NT][kTileRows]>(tn_smem);
   __shared__ unsigned long long bmax[NT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int rpc = 8 / wpr;
   const int lrt = warp / wpr, ks = warp % wpr;
   const int rt = blockIdx.x * rpc + lrt;
+  uint8_t *stage = tn_smem + warp * 2 * SB;
   pdl_trigger();
   if (threadIdx.x < NT) bmax[threadIdx.x] = 0ull;
   float acc[NB][4];
@@ -161,13 +179,34 @@ __global__ void __launch_bounds__(256) gemm_tn_kernel(const uint8_t *__restrict_
   if (mine && lane < kLines)
     asm volatile("prefetch.global.L2 [%0];" ::"l"(tiles + (size_t(rt) * ktiles + ks) * TB + lane * 128));
   pdl_wait();
+  // The warp walks its (k-tile, group) steps in order; the B operands of step i + 1 are copied
+  // into the other stage (cp.async, 16 bytes a lane a copy) while step i computes.
+  auto issue = [&](int kt, int G, int buf) {
+    const uint8_t *src = act + act_tn_offset(kt, G, 0, NB);
+    uint8_t *dst = stage + buf * SB;
+    for (int i = lane; i < SB / 16; i += 32) cp_async16(dst + 16 * i, src + 16 * i);
+  };
   if (mine) {
-    for (int kt = ks; kt < ktiles; kt += wpr) {
-      const uint8_t *tile = tiles + (size_t(rt) * ktiles + kt) * TB;
-      if (kt + wpr < ktiles && lane < kLines)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(tile + size_t(wpr) * TB + lane * 128));
+    const int steps = ((ktiles - ks + wpr - 1) / wpr) * kGroupsPerTile;
+    issue(ks, 0, 0);
+    cp_async_commit();
+    const uint8_t *tile = nullptr;
+    int kt = ks - wpr;
 #pragma unroll 1
-      for (int G = 0; G < kGroupsPerTile; ++G) {
+    for (int it = 0; it < steps; ++it) {
+      const int G = it % kGroupsPerTile, buf = it & 1;
+      if (G == 0) {
+        kt += wpr;
+        tile = tiles + (size_t(rt) * ktiles + kt) * TB;
+        if (kt + wpr < ktiles && lane < kLines)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(tile + size_t(wpr) * TB + lane * 128));
+      }
+      if (it + 1 < steps) issue(ks + ((it + 1) / kGroupsPerTile) * wpr, (it + 1) % kGroupsPerTile, buf ^ 1);
+      cp_async_commit();
+      cp_async_wait_1();  // this step's copies (all groups but the newest) are in
+      __syncwarp();
+      const uint8_t *sb = stage + buf * SB;
+      {
         const int h = G >> 2, Ls = 4 * g + (G & 3);
         const int piece0 = (KIND == kKindInt8 ? 4 * h : 0) + (c >> 1);
         const uint2 w01 = ldg64(tile + (piece0 * 32 + Ls) * 16 + 8 * (c & 1));
@@ -201,9 +240,9 @@ __global__ void __launch_bounds__(256) gemm_tn_kernel(const uint8_t *__restrict_
         for (int b = 0; b < NB; ++b) {
           // B registers of token 8b + g and the (S, X) of tokens 8b + 2c, 8b + 2c + 1 (the lane's D
           // columns); the padding tokens of the last block are zero groups
-          const uint8_t *blk = act + act_tn_offset(kt, G, b, NB);
-          const uint4 bq = __ldg(reinterpret_cast<const uint4 *>(blk) + lane);
-          const float4 sx = __ldg(reinterpret_cast<const float4 *>(blk + 512) + c);
+          const uint8_t *blk = sb + b * kActTile;
+          const uint4 bq = reinterpret_cast<const uint4 *>(blk)[lane];
+          const float4 sx = reinterpret_cast<const float4 *>(blk + 512)[c];
           const uint32_t bh0 = bq.x, bh1 = bq.y, bl0 = bq.z, bl1 = bq.w;
           const float2 x0 = make_float2(sx.x, sx.y), x1 = make_float2(sx.z, sx.w);
           int dh[4] = {0, 0, 0, 0};
@@ -237,8 +276,11 @@ __global__ void __launch_bounds__(256) gemm_tn_kernel(const uint8_t *__restrict_
           }
         }
       }
+      __syncwarp();  // every lane is done with this stage before step it + 2 copies into it
     }
+    cp_async_wait_0();
   }
+  __syncthreads();  // the partials overwrite the stages of every warp
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
     const int t0 = 8 * b + 2 * c;
@@ -265,8 +307,8 @@ void launch_kind(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &o
       switch ((ntok + 7) / 8) {
 #define HC_NB(b)                                                                                      \
   case b:                                                                                             \
-    launch_pdl(gemm_tn_kernel<KIND, b>, dim3(grid), dim3(256), 0, st, W.tiles, W.row_scale, W.bias, act, \
-               ntok, W.rtiles, W.ktiles, W.rows, wpr, out);                                          \
+    launch_pdl(gemm_tn_kernel<KIND, b>, dim3(grid), dim3(256), gemm_tn_smem(b), st, W.tiles, W.row_scale, \
+               W.bias, act, ntok, W.rtiles, W.ktiles, W.rows, wpr, out);                             \
     break;
         HC_NB(2) HC_NB(3) HC_NB(4) HC_NB(5) HC_NB(6) HC_NB(7) HC_NB(8)
 #undef HC_NB
@@ -454,6 +496,24 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ tiles, const float *_
 }
 
 }  // namespace
+
+char *gemv_prepare() {
+  static std::mutex mu;
+  static bool done[64] = {};
+  int dev = 0;
+  HC_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return make_error("gemv_prepare: device ordinal beyond 64");
+  std::lock_guard<std::mutex> lk(mu);
+  if (done[dev]) return nullptr;
+#define HC_SET(K, b) \
+  HC_TRY_CUDA(cudaFuncSetAttribute(gemm_tn_kernel<K, b>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_tn_smem(b)));
+#define HC_SET_K(K) HC_SET(K, 2) HC_SET(K, 3) HC_SET(K, 4) HC_SET(K, 5) HC_SET(K, 6) HC_SET(K, 7) HC_SET(K, 8)
+  HC_SET_K(kKindInt8) HC_SET_K(kKindInt4) HC_SET_K(kKindMx)
+#undef HC_SET_K
+#undef HC_SET
+  done[dev] = true;
+  return nullptr;
+}
 
 void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cudaStream_t st) {
   const int wpr = W.ktiles >= 8 ? 8 : (W.ktiles >= 4 ? 4 : (W.ktiles >= 2 ? 2 : 1));

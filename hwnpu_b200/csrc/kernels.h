@@ -52,6 +52,10 @@ struct GemvOut {
   unsigned long long *amax = nullptr;   // kLogits: [t], see argmax_key in misc.cu
 };
 
+// Sets, once a device (call it with the device current, outside stream capture), the shared
+// memory the batched GEMV asks for; hc_session_new and hc_linear_load call it.
+char *gemv_prepare();
+
 // y = x W^T for ntok (1..64) tokens whose activations act_quant wrote into act: up to 8 tokens a
 // token per MMA column group (gemv_kernel), 9..64 tokens on the MMA's n (gemm_tn_kernel).
 void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cudaStream_t st);

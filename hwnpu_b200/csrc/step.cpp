@@ -381,6 +381,7 @@ HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session
   if (o.kv_format == HC_KV_INT8_PAGED && o.page_size != uint32_t(hc::kPage))
     return hc::make_error("hc_session_new: the paged int8 cache has pages of " + std::to_string(hc::kPage) + " positions");
   HC_TRY_CUDA(cudaSetDevice(m->ordinal));
+  if (char *e = hc::gemv_prepare()) return e;
   auto s = std::make_unique<hc_session>();
   s->m = m;
   s->o = o;
