@@ -29,8 +29,8 @@ __device__ __forceinline__ size_t act_tn_offset(int kt, int G, int b, int nb) {
 template <int KIND, int NT>
 __device__ __forceinline__ void gemv_finish(float (*part)[NT][kTileRows], unsigned long long *bmax, int nt,
                                             const float *__restrict__ row_scale, const float *__restrict__ bias,
-                                            int rtiles, int rows, int wpr, const GemvOut &out) {
-  const int rpc = 8 / wpr;
+                                            int rtiles, int rows, int wpr, const GemvOut &out, int warps = 8) {
+  const int rpc = warps / wpr;
   __syncthreads();
   for (int idx = threadIdx.x; idx < rpc * NT * kTileRows; idx += blockDim.x) {
     const int l2 = idx / (NT * kTileRows), t = (idx / kTileRows) % NT, r16 = idx % kTileRows;
@@ -141,15 +141,19 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// Dynamic shared memory of gemm_tn_kernel<KIND, nb>: 8 warps x 2 stages of nb x 576 bytes (the
-// larger of that and the 8 x 8nb x 16 float partials).
-constexpr int gemm_tn_smem(int nb) { return 8 * 2 * nb * kActTile; }
+// Dynamic shared memory of gemm_tn_kernel<KIND, nb, warps, ..>: warps x 2 stages of nb x 576 bytes
+// (the larger of that and the warps x 8nb x 16 float partials).
+constexpr int gemm_tn_smem(int nb, int warps = 8) { return warps * 2 * nb * kActTile; }
+constexpr int kTnNarrowRows = 512;  // row tiles below which the batched GEMV takes 16-warp CTAs
 
 __device__ __forceinline__ uint32_t ldg32(const uint8_t *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
 __device__ __forceinline__ uint2 ldg64(const uint8_t *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
 
-template <int KIND, int NB>
-__global__ void __launch_bounds__(256) gemm_tn_kernel(const uint8_t *__restrict__ tiles,
+// WARPS warps a CTA; GS: the warps that share one k-tile's 8 groups (1, or 2 for the narrow
+// matrices, so that each warp walks fewer steps). A warp's units are u = ks, ks + wpr, ... of the
+// row tile's ktiles x GS units, unit u being groups (u % GS) * 8 / GS .. of k-tile u / GS.
+template <int KIND, int NB, int WARPS, int GS>
+__global__ void __launch_bounds__(WARPS * 32) gemm_tn_kernel(const uint8_t *__restrict__ tiles,
                                                       const float *__restrict__ row_scale,
                                                       const float *__restrict__ bias,
                                                       const uint8_t *__restrict__ act, int ntok,
@@ -164,20 +168,22 @@ __global__ void __launch_bounds__(256) gemm_tn_kernel(const uint8_t *__restrict_
   __shared__ unsigned long long bmax[NT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int rpc = 8 / wpr;
+  constexpr int SPU = kGroupsPerTile / GS;  // steps (groups) a unit
+  const int rpc = WARPS / wpr;
   const int lrt = warp / wpr, ks = warp % wpr;
   const int rt = blockIdx.x * rpc + lrt;
+  const int units = ktiles * GS;
   uint8_t *stage = tn_smem + warp * 2 * SB;
   pdl_trigger();
   if (threadIdx.x < NT) bmax[threadIdx.x] = 0ull;
   float acc[NB][4];
 #pragma unroll
   for (int b = 0; b < NB; ++b) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.f;
-  const bool mine = rt < rtiles && ks < ktiles;
+  const bool mine = rt < rtiles && ks < units;
   // the first weight tile does not depend on the kernels before: bring it towards L2 meanwhile
   constexpr int kLines = (TB + 127) / 128;
   if (mine && lane < kLines)
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(tiles + (size_t(rt) * ktiles + ks) * TB + lane * 128));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(tiles + (size_t(rt) * ktiles + ks / GS) * TB + lane * 128));
   pdl_wait();
   // The warp walks its (k-tile, group) steps in order; the B operands of step i + 1 are copied
   // into the other stage (cp.async, 16 bytes a lane a copy) while step i computes.
@@ -186,22 +192,30 @@ __global__ void __launch_bounds__(256) gemm_tn_kernel(const uint8_t *__restrict_
     uint8_t *dst = stage + buf * SB;
     for (int i = lane; i < SB / 16; i += 32) cp_async16(dst + 16 * i, src + 16 * i);
   };
+  auto unit_kt = [&](int u) { return u / GS; };
+  auto unit_g0 = [&](int u) { return (u % GS) * SPU; };
   if (mine) {
-    const int steps = ((ktiles - ks + wpr - 1) / wpr) * kGroupsPerTile;
-    issue(ks, 0, 0);
+    const int steps = ((units - ks + wpr - 1) / wpr) * SPU;
+    issue(unit_kt(ks), unit_g0(ks), 0);
     cp_async_commit();
     const uint8_t *tile = nullptr;
-    int kt = ks - wpr;
+    int u = ks - wpr, G = 0;
 #pragma unroll 1
     for (int it = 0; it < steps; ++it) {
-      const int G = it % kGroupsPerTile, buf = it & 1;
-      if (G == 0) {
-        kt += wpr;
-        tile = tiles + (size_t(rt) * ktiles + kt) * TB;
-        if (kt + wpr < ktiles && lane < kLines)
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(tile + size_t(wpr) * TB + lane * 128));
+      const int buf = it & 1;
+      if (it % SPU == 0) {
+        u += wpr;
+        G = unit_g0(u);
+        tile = tiles + (size_t(rt) * ktiles + unit_kt(u)) * TB;
+        if (u + wpr < units && lane < kLines)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(tiles + (size_t(rt) * ktiles + unit_kt(u + wpr)) * TB + lane * 128));
+      } else {
+        ++G;
       }
-      if (it + 1 < steps) issue(ks + ((it + 1) / kGroupsPerTile) * wpr, (it + 1) % kGroupsPerTile, buf ^ 1);
+      if (it + 1 < steps) {
+        const int u1 = ks + ((it + 1) / SPU) * wpr;
+        issue(unit_kt(u1), unit_g0(u1) + (it + 1) % SPU, buf ^ 1);
+      }
       cp_async_commit();
       cp_async_wait_1();  // this step's copies (all groups but the newest) are in
       __syncwarp();
@@ -289,7 +303,7 @@ __global__ void __launch_bounds__(256) gemm_tn_kernel(const uint8_t *__restrict_
     part[warp][t0][g + 8] = acc[b][2];
     part[warp][t0 + 1][g + 8] = acc[b][3];
   }
-  gemv_finish<KIND, NT>(part, bmax, ntok, row_scale, bias, rtiles, rows, wpr, out);
+  gemv_finish<KIND, NT>(part, bmax, ntok, row_scale, bias, rtiles, rows, wpr, out, WARPS);
 }
 
 template <int KIND>
@@ -304,11 +318,23 @@ void launch_kind(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &o
     HC_NT(1) HC_NT(2) HC_NT(3) HC_NT(4) HC_NT(5) HC_NT(6) HC_NT(7) HC_NT(8)
 #undef HC_NT
     default: {
+      // narrow matrices (few row tiles): 16 warps a row tile, two to a k-tile's groups
+      const bool narrow = W.rtiles < kTnNarrowRows;
+      int twpr = wpr, tgrid = grid;
+      if (narrow) {
+        const int units = 2 * W.ktiles;
+        twpr = units >= 16 ? 16 : (units >= 8 ? 8 : (units >= 4 ? 4 : 2));
+        tgrid = (W.rtiles + 16 / twpr - 1) / (16 / twpr);
+      }
       switch ((ntok + 7) / 8) {
-#define HC_NB(b)                                                                                      \
-  case b:                                                                                             \
-    launch_pdl(gemm_tn_kernel<KIND, b>, dim3(grid), dim3(256), gemm_tn_smem(b), st, W.tiles, W.row_scale, \
-               W.bias, act, ntok, W.rtiles, W.ktiles, W.rows, wpr, out);                             \
+#define HC_NB(b)                                                                                           \
+  case b:                                                                                                  \
+    if (narrow)                                                                                            \
+      launch_pdl(gemm_tn_kernel<KIND, b, 16, 2>, dim3(tgrid), dim3(512), gemm_tn_smem(b, 16), st, W.tiles, \
+                 W.row_scale, W.bias, act, ntok, W.rtiles, W.ktiles, W.rows, twpr, out);                   \
+    else                                                                                                   \
+      launch_pdl(gemm_tn_kernel<KIND, b, 8, 1>, dim3(tgrid), dim3(256), gemm_tn_smem(b), st, W.tiles,     \
+                 W.row_scale, W.bias, act, ntok, W.rtiles, W.ktiles, W.rows, twpr, out);                   \
     break;
         HC_NB(2) HC_NB(3) HC_NB(4) HC_NB(5) HC_NB(6) HC_NB(7) HC_NB(8)
 #undef HC_NB
@@ -505,8 +531,11 @@ char *gemv_prepare() {
   if (dev < 0 || dev >= 64) return make_error("gemv_prepare: device ordinal beyond 64");
   std::lock_guard<std::mutex> lk(mu);
   if (done[dev]) return nullptr;
-#define HC_SET(K, b) \
-  HC_TRY_CUDA(cudaFuncSetAttribute(gemm_tn_kernel<K, b>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_tn_smem(b)));
+#define HC_SET(K, b)                                                                                  \
+  HC_TRY_CUDA(cudaFuncSetAttribute(gemm_tn_kernel<K, b, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                   gemm_tn_smem(b)));                                                   \
+  HC_TRY_CUDA(cudaFuncSetAttribute(gemm_tn_kernel<K, b, 16, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                   gemm_tn_smem(b, 16)));
 #define HC_SET_K(K) HC_SET(K, 2) HC_SET(K, 3) HC_SET(K, 4) HC_SET(K, 5) HC_SET(K, 6) HC_SET(K, 7) HC_SET(K, 8)
   HC_SET_K(kKindInt8) HC_SET_K(kKindInt4) HC_SET_K(kKindMx)
 #undef HC_SET_K
