@@ -44,11 +44,14 @@ constexpr int kMaxSplits = 64;
 constexpr int kSplitKeys = 1024;  // keys a split reads, at most, for the chunk's longest context
 
 // Attention splits of every (token, kv head) of a chunk of n tokens whose longest context is
-// max_len positions: enough CTAs to fill the SMs twice, and at most kSplitKeys keys a split for
-// the longest (rounded up to a power of two, so that few step graphs differ by their splits).
+// max_len positions: enough CTAs to fill the SMs twice (as for one token when n <= 8), and at
+// most kSplitKeys keys a split for the longest (rounded up to a power of two, so that few step
+// graphs differ by their splits).
 int splits_for(const hc_session *s, int n, int max_len) {
   const int kv = int(s->m->d.kv_heads);
-  int sp = (2 * s->m->sms) / (kv * n);
+  // up to 8 tokens take the one-token count, so that a speculative verify row, or any row of a
+  // small batch, is computed exactly as a one-token step (hc_generate) computes it
+  int sp = (2 * s->m->sms) / (kv * (n <= 8 ? 1 : n));
   int by_len = 1;
   while (by_len < kMaxSplits && by_len * kSplitKeys < max_len) by_len *= 2;
   return std::max(1, std::min(kMaxSplits, std::max(sp, by_len)));

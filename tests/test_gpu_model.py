@@ -186,6 +186,29 @@ def test_speculate_equals_plain_greedy(device, models):
     lm.close()
 
 
+def test_verify_row_equals_one_token_step_bit_for_bit(device, models):
+    # the first row of a 5-row speculative verify is computed exactly as a one-token step computes
+    # it (C2's layer shapes, 8 kv heads), so speculative decoding reproduces greedy decoding even
+    # where two logits tie in fp16
+    model = get(models, C2_2L)
+    lm = device.load_model(model)
+    a = lm.session(max_context=80, max_step=5)
+    b = lm.session(max_context=80)
+    prompt = list(synth.tokens(41, C2_2L.vocab, 40))
+    t = a.greedy(prompt)
+    assert b.greedy(prompt) == t
+    rng = np.random.default_rng(5)
+    for _ in range(4):
+        drafts = [int(x) for x in rng.integers(C2_2L.vocab, size=4)]
+        kept, nxt, row = a.speculate_tokens([t] + drafts, want_logits=True)
+        want = b.step_tokens([t])
+        assert kept == 1 and np.array_equal(row, want) and nxt == int(np.argmax(want))
+        t = nxt
+    a.close()
+    b.close()
+    lm.close()
+
+
 def test_ragged_batch_equals_single_sequences(device, models):
     # sequences of different lengths in one call read the same logits as alone
     model = get(models, TINY)
