@@ -104,7 +104,7 @@ SIGNATURES = {
     "hc_stats_get": (_err, [C.c_void_p, C.POINTER(Stats)]),
     "hc_profile_get": (_err, [C.c_void_p, C.POINTER(C.c_double), C.c_uint32, C.POINTER(C.c_uint32)]),
     "hc_set_fault": (_err, [C.c_char_p]),
-    "hc_synth_normal": (_err, [C.c_uint64, C.c_char_p, C.c_float, _f32p, C.c_uint64]),
+    "hc_synth_normal": (_err, [C.c_uint64, C.c_char_p, _f32p, _f32p, C.c_uint64]),
     "hc_synth_tokens": (_err, [C.c_uint64, C.c_int32, _i32p, C.c_uint64]),
     "hc_quantize_linear": (_err, [_f32p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int32, C.c_int32,
                                   _u8p, _u16p]),

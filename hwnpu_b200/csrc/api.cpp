@@ -24,6 +24,12 @@ int g_fault_point = -1;  // FaultPoint armed, or -1
 long g_fault_left = 0;   // calls of that point before the one that fails
 }  // namespace
 
+namespace {
+std::atomic<long> g_stall_ms{0};  // "stall:MS": the next step first waits MS ms on the device
+}  // namespace
+
+long take_stall_ms() { return g_stall_ms.exchange(0); }
+
 bool fault_fires(FaultPoint p) {
   std::lock_guard<std::mutex> g(g_fault_mu);
   if (g_fault_point != int(p)) return false;
@@ -114,6 +120,11 @@ HC_API char *hc_set_fault(const char *spec) {
   std::string point = s.substr(0, colon);
   long n = std::strtol(s.c_str() + colon + 1, nullptr, 10);
   if (n < 1) return hc::make_error("hc_set_fault: N must be at least 1");
+  if (point == "stall") {
+    if (n > 2000) return hc::make_error("hc_set_fault: a stall is at most 2000 ms");
+    hc::g_stall_ms = n;
+    return nullptr;
+  }
   if (point == "alloc") hc::g_fault_point = hc::kFaultAlloc;
   else if (point == "h2d") hc::g_fault_point = hc::kFaultH2D;
   else if (point == "step") hc::g_fault_point = hc::kFaultStep;

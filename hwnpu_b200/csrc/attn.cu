@@ -143,6 +143,9 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
     for (int k = 0; k < E; ++k) o[r][k] = 0.f;
   }
   const size_t base = (size_t(tk.slot) * g.kv_heads + kvh) * size_t(g.cap) * HD;
+  // key j sits at slot j mod cap: the slot itself in a linear cache (every key below cap), a ring
+  // otherwise; the split's keys span less than cap, so one wrap at most
+  const int slot0 = k0 % g.cap;
   // the trip count is the same for every lane (the shuffles below take the whole warp); a group
   // whose key is past the chunk's end loads nothing and leaves its softmax as it is. The loads of
   // a group's next key are issued before the current key's arithmetic (one key in flight ahead).
@@ -166,8 +169,10 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
       kp = reinterpret_cast<const uint32_t *>(pk.k + (ph * kPage + j % kPage) * HD + l8 * E);
       vp = reinterpret_cast<const uint32_t *>(pk.v + (ph * kPage + j % kPage) * HD + l8 * E);
     } else {
-      kp = reinterpret_cast<const uint32_t *>(kcache + base + size_t(j) * HD + l8 * E);
-      vp = reinterpret_cast<const uint32_t *>(vcache + base + size_t(j) * HD + l8 * E);
+      int sl = slot0 + (j - k0);
+      if (sl >= g.cap) sl -= g.cap;
+      kp = reinterpret_cast<const uint32_t *>(kcache + base + size_t(sl) * HD + l8 * E);
+      vp = reinterpret_cast<const uint32_t *>(vcache + base + size_t(sl) * HD + l8 * E);
     }
     if (KW % 4 == 0) {
 #pragma unroll

@@ -107,6 +107,8 @@ char *make_error(const std::string &msg);
 enum FaultPoint { kFaultAlloc = 0, kFaultH2D = 1, kFaultStep = 2 };
 // True when the armed fault of this point fires on this call.
 bool fault_fires(FaultPoint p);
+// The armed device stall in milliseconds (hc_set_fault "stall:MS"), cleared by the call; 0: none.
+long take_stall_ms();
 
 // cudaMalloc that honours the alloc fault and returns an error string.
 char *dev_alloc(void **p, size_t n, const char *what);

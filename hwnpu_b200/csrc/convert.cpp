@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "common.h"
+#include "../../include/hwnpu_cuda_synth.h"
 
 namespace {
 
@@ -116,8 +117,9 @@ HC_API void hc_f16_to_f32(const uint16_t *src, float *dst, uint64_t n) {
   });
 }
 
-HC_API char *hc_synth_normal(uint64_t seed, const char *name, float std_, float *out, uint64_t n) {
-  if (!name || (!out && n)) return hc::make_error("hc_synth_normal: NULL argument");
+HC_API char *hc_synth_normal(uint64_t seed, const char *name, const float *std_p, float *out, uint64_t n) {
+  if (!name || !std_p || (!out && n)) return hc::make_error("hc_synth_normal: NULL argument");
+  const float std_ = *std_p;
   const uint64_t h = fnv1a(name);
   const uint64_t chunks = (n + kChunk - 1) / kChunk;
   host_parallel(chunks, 1, [&](uint64_t c0, uint64_t c1) {

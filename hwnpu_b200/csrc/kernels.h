@@ -143,6 +143,10 @@ void route(const float *logits, int rows, int n, int k, int32_t *idx, float *w, 
 void spec_accept(const int32_t *amax_idx, const StepTok *toks, int n, int32_t *res,
                  cudaStream_t st);
 
+// A bounded device-side wait of ms milliseconds (at most 2 s) on st: the injected stall that makes
+// a step outlast its timeout in the failure tests, with nothing hung or faulted.
+void device_stall(long ms, cudaStream_t st);
+
 // The device-side token feedback of hc_generate: out[*count] = am[0], the next step reads that
 // token at the next position.
 void advance(StepTok *toks, const int32_t *am, int32_t *out, int32_t *count, cudaStream_t st);

@@ -117,7 +117,22 @@ __global__ void advance_kernel(StepTok *__restrict__ toks, const int32_t *__rest
   *count = i + 1;
 }
 
+// One thread waits until ns nanoseconds of the global timer have passed (capped at 2 s).
+__global__ void stall_kernel(unsigned long long ns) {
+  unsigned long long t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  if (ns > 2000000000ull) ns = 2000000000ull;
+  do {
+    __nanosleep(100000);
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  } while (t - t0 < ns);
+}
+
 }  // namespace
+
+void device_stall(long ms, cudaStream_t st) {
+  if (ms > 0) stall_kernel<<<1, 1, 0, st>>>((unsigned long long)ms * 1000000ull);
+}
 
 void advance(StepTok *toks, const int32_t *am, int32_t *out, int32_t *count, cudaStream_t st) {
   launch_pdl(advance_kernel, dim3(1), dim3(1), 0, st, toks, am, out, count);

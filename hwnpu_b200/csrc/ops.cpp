@@ -26,7 +26,9 @@ HC_API char *hc_attention_run(const float *q, const uint16_t *kcache, const uint
   const int rep = heads / kv_heads;
   if (head_dim != 64 && head_dim != 128) return hc::make_error("hc_attention_run: head_dim must be 64 or 128");
   if (rep != 1 && rep != 2 && rep != 4 && rep != 8) return hc::make_error("hc_attention_run: heads per kv head must be 1, 2, 4 or 8");
-  if (pos < 0 || pos + ntok > cap) return hc::make_error("hc_attention_run: positions beyond the cache");
+  if (pos < 0 || cap < 1) return hc::make_error("hc_attention_run: bad positions");
+  if (pos + ntok > cap && !(window > 0 && cap >= window + ntok - 1))
+    return hc::make_error("hc_attention_run: positions beyond the cache (a ring needs window > 0 and cap >= window + ntok - 1)");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int splits = 16;
   std::vector<hc::StepTok> toks(ntok);

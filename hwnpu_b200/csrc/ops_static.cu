@@ -47,7 +47,9 @@ HC_API char *hc_attention_run_static(const float *q, const uint16_t *kcache, con
   if (head_dim != 64 && head_dim != 128) return hc::make_error("hc_attention_run_static: head_dim must be 64 or 128");
   if (rep != 1 && rep != 2 && rep != 4 && rep != 8)
     return hc::make_error("hc_attention_run_static: heads per kv head must be 1, 2, 4 or 8");
-  if (pos < 0 || pos + ntok > cap) return hc::make_error("hc_attention_run_static: positions beyond the cache");
+  if (pos < 0 || cap < 1) return hc::make_error("hc_attention_run_static: bad positions");
+  if (pos + ntok > cap && !(window > 0 && cap >= window + ntok - 1))
+    return hc::make_error("hc_attention_run_static: positions beyond the cache (a ring needs window > 0 and cap >= window + ntok - 1)");
   // the scratch this call needs, each part on a 256-byte boundary
   const int splits = hc::kStaticSplits;
   const int ktiles = (heads * head_dim + hc::kTileCols - 1) / hc::kTileCols;
@@ -66,15 +68,22 @@ HC_API char *hc_attention_run_static(const float *q, const uint16_t *kcache, con
   if (dev < 0 || dev >= hc::kStaticMaxDevices)
     return hc::make_error("hc_attention_run_static: device ordinal " + std::to_string(dev) + " beyond " +
                           std::to_string(hc::kStaticMaxDevices));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Outside a stream capture the address is looked up on every call (a device reset or a new
+  // primary context moves the array); inside one, the address of the last call outside it is used.
+  cudaStreamCaptureStatus cap_status = cudaStreamCaptureStatusNone;
+  HC_TRY_CUDA(cudaStreamIsCapturing(st, &cap_status));
   uint8_t *base = nullptr;
   {
     std::lock_guard<std::mutex> lk(hc::g_mu);
-    if (!hc::g_addr[dev]) {
+    if (cap_status == cudaStreamCaptureStatusNone) {
       void *a = nullptr;
       const cudaError_t e = cudaGetSymbolAddress(&a, hc::g_attn_scratch);
       if (e != cudaSuccess)
         return hc::make_error(std::string("hc_attention_run_static: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
       hc::g_addr[dev] = a;
+    } else if (!hc::g_addr[dev]) {
+      return hc::make_error("hc_attention_run_static: the first call on a device must come before any stream capture");
     }
     base = static_cast<uint8_t *>(hc::g_addr[dev]);
   }
@@ -82,7 +91,6 @@ HC_API char *hc_attention_run_static(const float *q, const uint16_t *kcache, con
   auto *ml = reinterpret_cast<float *>(base + b_toks);
   auto *po = reinterpret_cast<float *>(base + b_toks + b_ml);
   uint8_t *act = base + b_toks + b_ml + b_po;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   hc::fill_toks_kernel<<<1, 32, 0, st>>>(dt, ntok, pos);
   hc::AttnGeom g{heads, kv_heads, head_dim, cap, window, *scale};
   hc::attn_split(q, dt, ntok, g, kcache, vcache, splits, ml, po, st);

@@ -280,6 +280,7 @@ char *run_chunk(hc_session *s, int n, bool accept, int heads) {
     s->graphs[key] = exec;
   }
   HC_TRY_CUDA(cudaEventRecord(s->ev0, st));
+  hc::device_stall(hc::take_stall_ms(), st);
   if (use_graph) {
     HC_TRY_CUDA(cudaGraphLaunch(s->graphs[key], st));
   } else {
@@ -608,6 +609,7 @@ HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, i
   HC_TRY_CUDA(cudaMemsetAsync(s->gen_count, 0, sizeof(int32_t), st));
   if (mk) HC_TRY_CUDA(cudaMemsetAsync(s->mk_status, 0, sizeof(int), st));
   HC_TRY_CUDA(cudaEventRecord(s->ev0, st));
+  hc::device_stall(hc::take_stall_ms(), st);
   for (int i = 0; i < n; ++i) HC_TRY_CUDA(cudaGraphLaunch(s->gen_graph, st));
   HC_TRY_CUDA(cudaEventRecord(s->ev1, st));
   if (mk) HC_TRY_CUDA(cudaMemcpyAsync(s->mk_status_host, s->mk_status, sizeof(int), cudaMemcpyDeviceToHost, st));

@@ -4,6 +4,10 @@ The weights are drawn N(0, std^2) per tensor name (hc_synth_normal) and quantise
 library's converter routines into the reference's byte layouts (palette.QuantizeLinear's int8,
 the asymmetric int4 of group 32, MXFP4's Encode), the form hc_model_load takes. A Model keeps
 the numpy arrays alive and builds the ctypes descriptor over them.
+
+The generator and the quantisers come from a `gen` object (normal, tokens, quantize, f16_bits);
+the default is this package's library (LibGen). A CPU-only caller passes another with the same
+results (the oracle's, tests/oracle_lib.OracleGen) so that it never maps libhwnpu_cuda.so.
 """
 
 import ctypes as C
@@ -52,7 +56,8 @@ def _f32(a):
 
 def normal(seed, name, n, std):
     out = np.empty(n, dtype=np.float32)
-    A.check(A.lib().hc_synth_normal(seed, name.encode(), std, _f32(out), n))
+    sd = np.array([std], np.float32)
+    A.check(A.lib().hc_synth_normal(seed, name.encode(), _f32(sd), _f32(out), n))
     return out
 
 
@@ -120,22 +125,34 @@ class Linear:
         raise ValueError(f"format {fmt}")
 
 
+class LibGen:
+    """The synthetic-weight generator and quantisers of libhwnpu_cuda.so."""
+
+    normal = staticmethod(normal)
+    tokens = staticmethod(tokens)
+    f16_bits = staticmethod(f16_bits)
+
+    @staticmethod
+    def quantize(w, fmt, search=False):
+        return Linear.quantize(w, fmt, search)
+
+
 class Model:
     """A synthetic model of a Config: quantised weights plus norms, and its hc_model_desc."""
 
-    def __init__(self, cfg: Config, seed: int = 0, norm_std: float = 0.0):
+    def __init__(self, cfg: Config, seed: int = 0, norm_std: float = 0.0, gen=LibGen):
         self.cfg = cfg
         c = cfg
         hd = c.head_dim
 
         def mat(name, rows, cols):
-            w = normal(seed, name, rows * cols, c.std).reshape(rows, cols)
-            return Linear.quantize(w, c.fmt, c.quant_search)
+            w = gen.normal(seed, name, rows * cols, c.std).reshape(rows, cols)
+            return gen.quantize(w, c.fmt, c.quant_search)
 
         def norm(name, n):
             if norm_std == 0.0:
-                return f16_bits(np.ones(n, np.float32))
-            return f16_bits(1.0 + normal(seed, name, n, norm_std))
+                return gen.f16_bits(np.ones(n, np.float32))
+            return gen.f16_bits(1.0 + gen.normal(seed, name, n, norm_std))
 
         self.layers = []
         for i in range(c.layers):
@@ -161,7 +178,7 @@ class Model:
             self.embed = None
         else:
             self.head = mat("lm_head.weight", c.vocab, c.hidden)
-            self.embed = f16_bits(normal(seed, "model.embed_tokens.weight", c.vocab * c.hidden, c.std))
+            self.embed = gen.f16_bits(gen.normal(seed, "model.embed_tokens.weight", c.vocab * c.hidden, c.std))
         self._desc = None
 
     def desc(self):

@@ -310,21 +310,19 @@ HC_API char *hc_stats_get(hc_session *s, hc_stats *out);
  * consumers waited for full stages, ran in all. */
 HC_API char *hc_profile_get(hc_session *s, double *us, uint32_t cap, uint32_t *n);
 
-/* Host-side fault injection for tests (the reference fakes its drivers instead, testdata/zemock):
+/* Fault injection for tests (the reference fakes its drivers instead, testdata/zemock):
  * "alloc:N" fails the N-th device allocation from now, "h2d:N" the N-th host-to-device copy,
- * "step:N" the N-th hc_step, each with an error string; "" clears. Nothing faults on the GPU. */
+ * "step:N" the N-th hc_step, each with an error string; "stall:MS" (MS <= 2000) makes the next
+ * hc_step, hc_speculate or hc_generate first wait MS milliseconds on the device, so that a shorter
+ * timeout_ms runs out (HC_STATE_TIMEOUT, the sequences poisoned until hc_seq_reset); "" clears.
+ * Nothing faults or hangs on the GPU: the stall is a bounded wait on the global timer. */
 HC_API char *hc_set_fault(const char *spec);
 
 /* ---------------------------------------------------------------------------------------- */
-/* Converter side: synthetic weights and the reference's quantisers, on the host's cores      */
+/* Converter side: the reference's quantisers, on the host's cores                            */
+/* (the seeded synthetic-weight helpers of tests and benchmarks are in hwnpu_cuda_synth.h)    */
 /* ---------------------------------------------------------------------------------------- */
 
-/* n values drawn N(0, std^2), seeded by (seed, name): PCG32 streams of 2^20 values each, so
- * the values do not depend on the thread count (replaces llm.NewSynthetic's role,
- * internal/llm/synth.go:10-36, with the normal draws BASELINE's configs ask for). */
-HC_API char *hc_synth_normal(uint64_t seed, const char *name, float std, float *out, uint64_t n);
-/* n token ids uniform on [0, vocab) from seed. */
-HC_API char *hc_synth_tokens(uint64_t seed, int32_t vocab, int32_t *out, uint64_t n);
 /* palette.QuantizeLinear (internal/palette/linear.go:36-114): bits 4 or 8, one fp16 scale per
  * col_block columns (0: whole rows), with the MSE clip search when search != 0. data gets
  * rows*cols bytes (8 bits) or rows*cols/2 (4 bits), scales rows*(cols/col_block). */
@@ -368,9 +366,10 @@ HC_API char *hc_linear_run(hc_linear *l, const float *x, int32_t ntok, float *y,
 /* Decode attention of one sequence over an fp16 cache (blocks.SDPAGrouped blocks.go:516-539,
  * gpt-oss's sdpaSink gptoss/build.go:256-285, Flash-Decoding's merge paged.go:227-310):
  * q float32 [ntok][heads][head_dim] (already normed and rotated), kcache/vcache fp16
- * [kv_heads][cap][head_dim] holding positions [0, pos + ntok) (ring slots pos mod cap when
- * window > 0 and cap == window), token t at position pos + t sees keys p <= pos + t with
- * pos + t - p < window (window 0: all). sinks float32 [heads] or NULL. o float32
+ * [kv_heads][cap][head_dim] with the key and value of position p at slot p mod cap: a linear cache
+ * (pos + ntok <= cap), or a ring of the sliding window (gptoss StepInputs' ring, build.go:291-326)
+ * that holds the step's own rows too, which needs window > 0 and cap >= window + ntok - 1;
+ * token t at position pos + t sees keys p <= pos + t with pos + t - p < window (window 0: all). sinks float32 [heads] or NULL. o float32
  * [ntok][heads][head_dim]. scale is multiplied into the scores. */
 HC_API char *hc_attention_run(const float *q, const uint16_t *kcache, const uint16_t *vcache,
                               const float *sinks, float *o, int32_t ntok, int32_t heads,
@@ -389,8 +388,9 @@ HC_API char *hc_attention_run(const float *q, const uint16_t *kcache, const uint
  * tiles) exceeds 8 MiB is rejected with an error. The work is enqueued on stream and not waited
  * for: errors of the launches are returned, errors of the execution show on the stream. Calls
  * that overlap in time on one device (other streams or threads) share the scratch and race: run
- * them on one stream. The first call on a device looks the array's address up
- * (cudaGetSymbolAddress, with that device current); make it before any stream capture. */
+ * them on one stream. A call outside a stream capture looks the array's address up on its device
+ * (cudaGetSymbolAddress, with that device current); a call inside a capture uses the address of the
+ * last call outside one, so make a first call on each device before any stream capture. */
 HC_API char *hc_attention_run_static(const float *q, const uint16_t *kcache, const uint16_t *vcache,
                                      const float *sinks, float *o, int32_t ntok, int32_t heads,
                                      int32_t kv_heads, int32_t head_dim, int32_t pos, int32_t cap,

@@ -29,6 +29,13 @@ OR_API float or_exp(float x);
  * the name (internal/llm/synth.go:17-36). */
 OR_API void or_synth_uniform(const char *name, float *out, uint64_t n);
 
+/* The benchmark configurations' seeded inputs (synth.cpp): n values N(0, std^2) for a tensor name,
+ * and n token ids uniform on [0, vocab); equal bit for bit to the product's generator. */
+OR_API void or_synth_normal(uint64_t seed, const char *name, const float *std_, float *out, uint64_t n);
+OR_API void or_synth_tokens(uint64_t seed, int32_t vocab, int32_t *out, uint64_t n);
+/* or_f16_bits over n values. */
+OR_API void or_f32_to_f16_n(const float *src, uint16_t *dst, uint64_t n);
+
 /* palette.QuantizeLinear / Linear.Dequantize (internal/palette/linear.go:36-169) */
 OR_API void or_quantize_linear(const float *w, uint32_t rows, uint32_t cols, uint32_t col_block,
                                int32_t bits, int32_t search, uint8_t *data, uint16_t *scales);

@@ -21,6 +21,9 @@ SIG = {
     "or_f16_value": (C.c_float, [C.c_uint16]),
     "or_exp": (C.c_float, [C.c_float]),
     "or_synth_uniform": (None, [C.c_char_p, _f32p, C.c_uint64]),
+    "or_synth_normal": (None, [C.c_uint64, C.c_char_p, _f32p, _f32p, C.c_uint64]),
+    "or_synth_tokens": (None, [C.c_uint64, C.c_int32, _i32p, C.c_uint64]),
+    "or_f32_to_f16_n": (None, [_f32p, _u16p, C.c_uint64]),
     "or_quantize_linear": (None, [_f32p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int32, C.c_int32, _u8p, _u16p]),
     "or_dequant_linear": (None, [_u8p, _u16p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int32, _f32p]),
     "or_dequant_int4_asym": (None, [_u8p, _u16p, _u16p, C.c_uint32, C.c_uint32, _f32p]),
@@ -63,6 +66,80 @@ def lib():
 
 def p(a, t):
     return a.ctypes.data_as(t)
+
+
+def _row_blocks(rows, fn, block=256):
+    """Runs fn(r0, r1) over row blocks on the host's threads (ctypes releases the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    spans = [(r, min(rows, r + block)) for r in range(0, rows, block)]
+    with ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
+        list(ex.map(lambda s: fn(*s), spans))
+
+
+class OracleGen:
+    """synth.Model's generator on the oracle's side (or_synth_*, or_quantize_*, or_mxfp4_encode):
+    the same values and bytes as the product library's, with no call into libhwnpu_cuda.so."""
+
+    @staticmethod
+    def normal(seed, name, n, std):
+        out = np.empty(n, np.float32)
+        sd = np.array([std], np.float32)
+        lib().or_synth_normal(seed, name.encode(), p(sd, _f32p), p(out, _f32p), n)
+        return out
+
+    @staticmethod
+    def tokens(seed, vocab, n):
+        out = np.empty(n, np.int32)
+        lib().or_synth_tokens(seed, vocab, p(out, _i32p), n)
+        return out
+
+    @staticmethod
+    def f16_bits(x):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty(x.shape, np.uint16)
+        lib().or_f32_to_f16_n(p(x, _f32p), p(out, _u16p), x.size)
+        return out
+
+    @staticmethod
+    def quantize(w, fmt, search=False):
+        from hwnpu_b200.synth import Linear
+
+        w = np.ascontiguousarray(w, np.float32)
+        rows, cols = w.shape
+        L = lib()
+        if fmt in (A.HC_FMT_INT8_ROW, A.HC_FMT_INT4_SYM_G32):
+            bits, blk = (8, cols) if fmt == A.HC_FMT_INT8_ROW else (4, 32)
+            per = cols // blk
+            data = np.empty(rows * cols * bits // 8, np.uint8)
+            sc = np.empty(rows * per, np.uint16)
+            rb = cols * bits // 8
+
+            def run(r0, r1):
+                L.or_quantize_linear(p(w[r0:r1], _f32p), r1 - r0, cols, 0 if bits == 8 else 32, bits, int(search),
+                                     p(data[r0 * rb:], _u8p), p(sc[r0 * per:], _u16p))
+            _row_blocks(rows, run)
+            return Linear(fmt, rows, cols, data, scales=sc)
+        if fmt == A.HC_FMT_INT4_ASYM_G32:
+            data = np.empty(rows * cols // 2, np.uint8)
+            sc = np.empty(rows * cols // 32, np.uint16)
+            z = np.empty(rows * cols // 32, np.uint16)
+
+            def run(r0, r1):
+                L.or_quantize_int4_asym(p(w[r0:r1], _f32p), r1 - r0, cols, p(data[r0 * cols // 2:], _u8p),
+                                        p(sc[r0 * cols // 32:], _u16p), p(z[r0 * cols // 32:], _u16p))
+            _row_blocks(rows, run)
+            return Linear(fmt, rows, cols, data, scales=sc, zeros=z)
+        if fmt == A.HC_FMT_MXFP4:
+            data = np.empty(rows * cols // 2, np.uint8)
+            e = np.empty(rows * cols // 32, np.uint8)
+
+            def run(r0, r1):
+                for r in range(r0, r1):
+                    L.or_mxfp4_encode(p(w[r], _f32p), cols, p(data[r * cols // 2:], _u8p), p(e[r * cols // 32:], _u8p))
+            _row_blocks(rows, run, block=64)
+            return Linear(fmt, rows, cols, data, exps=e)
+        raise ValueError(f"format {fmt}")
 
 
 class OracleSession:

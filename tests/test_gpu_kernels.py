@@ -149,6 +149,45 @@ def test_attention(H, KV, hd, window, sink, ntok, pos):
     assert np.abs(got - want).max() < 2e-5 * max(1.0, np.abs(want).max())
 
 
+@pytest.mark.parametrize("ntok,pos,cap", [(1, 127, 128), (1, 300, 128), (1, 1000, 128), (3, 500, 130), (5, 77, 132)])
+def test_attention_ring_window(ntok, pos, cap):
+    # gpt-oss's sliding layers keep a ring of the window (gptoss StepInputs, build.go:291-326): the
+    # key of position p at slot p mod cap; positions past the window have wrapped around
+    H, KV, hd, window = 64, 8, 64, 128
+    rng = np.random.default_rng(pos * 3 + ntok)
+    q = rng.standard_normal((ntok, H, hd)).astype(np.float32)
+    ring_k = rng.standard_normal((KV, cap, hd)).astype(np.float16)
+    ring_v = rng.standard_normal((KV, cap, hd)).astype(np.float16)
+    sinks = (rng.standard_normal(H) * 2).astype(np.float32)
+    scale = np.float32(synth.f16_values(synth.f16_bits(np.array([1 / np.sqrt(hd)], np.float32)))[0])
+    # the linear view the reference attends over: position p reads ring slot p mod cap
+    P = pos + ntok
+    lin_k = ring_k[:, np.arange(P) % cap]
+    lin_v = ring_v[:, np.arange(P) % cap]
+    tq = torch.from_numpy(q).cuda()
+    tk = torch.from_numpy(ring_k.view(np.uint16).astype(np.int16)).cuda()
+    tv = torch.from_numpy(ring_v.view(np.uint16).astype(np.int16)).cuda()
+    ts = torch.from_numpy(sinks).cuda()
+    to = torch.empty_like(tq)
+    sc = np.array([scale], np.float32)
+    A.check(A.lib().hc_attention_run(C.c_void_p(tq.data_ptr()), C.c_void_p(tk.data_ptr()), C.c_void_p(tv.data_ptr()),
+                                     C.c_void_p(ts.data_ptr()), C.c_void_p(to.data_ptr()), ntok, H, KV, hd, pos, cap,
+                                     window, sc.ctypes.data_as(C.POINTER(C.c_float)), None))
+    want = attention_ref(q, lin_k, lin_v, pos, window, sinks, float(scale))
+    got = to.cpu().numpy()
+    assert np.abs(got - want).max() < 2e-5 * max(1.0, np.abs(want).max())
+
+
+def test_attention_ring_too_small_is_an_error():
+    # a ring of exactly the window cannot hold a 3-token step's own rows
+    z = torch.zeros(1 << 16, device="cuda")
+    p = C.c_void_p(z.data_ptr())
+    sc = np.array([0.125], np.float32)
+    with pytest.raises(hb.HcError, match="ring"):
+        A.check(A.lib().hc_attention_run(p, p, p, None, p, 3, 8, 8, 64, 500, 128, 128,
+                                         sc.ctypes.data_as(C.POINTER(C.c_float)), None))
+
+
 def test_argmax_first_of_equal():
     v = np.full((3, 151936), -5.0, np.float32)
     v[0, [7, 99, 151935]] = 3.0       # a tie: the first wins

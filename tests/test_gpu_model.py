@@ -319,3 +319,82 @@ def test_injected_faults_leave_the_session_usable(device, models):
         s.step_tokens([TINY.vocab])
     s.close()
     lm.close()
+
+
+def test_step_timeout_poisons_until_reset(device, models):
+    # xs_run_wait's timeout (native/xrtshim/xrtshim.h:106-108) and the engine's rule that a failed
+    # step leaves the cache half written (chat/engine.go:1521-1525): a device stall of 400 ms
+    # (hc_set_fault "stall:400", a bounded wait on the global timer) outlasts a 20 ms timeout; the
+    # call reports HC_STATE_TIMEOUT, the sequence refuses further steps until hc_seq_reset, and after
+    # the reset the session decodes as a fresh one does
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    s = lm.session(max_context=48)
+    fresh = lm.session(max_context=48)
+    toks = list(synth.tokens(77, TINY.vocab, 6))
+    A.check(A.lib().hc_set_fault(b"stall:400"))
+    with pytest.raises(TimeoutError):
+        s.step_batch([0], [toks], timeout_ms=20)
+    with pytest.raises(hb.HcError, match="reset"):
+        s.step_tokens(toks)
+    s.reset()
+    want = fresh.step_tokens(toks)
+    assert np.array_equal(s.step_tokens(toks), want)
+    # hc_generate's wait likewise
+    first = int(np.argmax(want))
+    A.check(A.lib().hc_set_fault(b"stall:400"))
+    with pytest.raises(TimeoutError):
+        s.generate(first, 4, timeout_ms=20)
+    with pytest.raises(hb.HcError, match="reset"):
+        s.generate(first, 4)
+    s.reset()
+    assert s.pos() == 0
+    s.close()
+    fresh.close()
+    lm.close()
+
+
+def _stream_check(got_stream, ref_margins, ref_stream):
+    """Greedy streams must be identical wherever the oracle's top-2 margin exceeds the tolerance;
+    past the first step where it does not, the two may part (both choices are within tolerance)."""
+    for i, (g, w, m) in enumerate(zip(got_stream, ref_stream, ref_margins)):
+        if m <= 2 * TOL:
+            return i
+        assert g == w, (i, g, w, m)
+    return len(ref_stream)
+
+
+@pytest.mark.parametrize("cfg,prompt,steps,logit_steps", [(synth.C1, 256, 128, 16), (synth.C2, 1024, 16, 16)],
+                         ids=["c1-256-128", "c2-28L-1024-16"])
+def test_baseline_config_matches_oracle(device, cfg, prompt, steps, logit_steps):
+    # BASELINE configs[0] and configs[1] at their own sizes: all layers, the stated prompt length
+    # (ids from the benchmark's seed), then greedy steps. Logits after the prompt and after each of
+    # the first logit_steps tokens are compared with the oracle's (max-abs 2e-2, cosine 0.9999); the
+    # device-resident greedy loop (hc_generate) must reproduce the oracle's greedy stream.
+    model = synth.Model(cfg, seed=0)
+    lm = device.load_model(model)
+    ctx = prompt + steps + 2
+    sess = lm.session(max_context=ctx)
+    gen = lm.session(max_context=ctx)
+    ref = O.OracleSession(model, ctx)
+    toks = list(synth.tokens(1, cfg.vocab, prompt))
+    got = sess.step_tokens(toks)
+    want = synth.f16_values(ref.step(toks)[0])
+    compare(got, want)
+    first = int(np.argmax(want))
+    ref_stream, margins = [], []
+    w_tok = first
+    for i in range(steps):
+        want_row = synth.f16_values(ref.step([w_tok])[0])
+        if i < logit_steps:
+            compare(sess.step_tokens([w_tok]), want_row)
+        margins.append(top2_margin(want_row))
+        w_tok = int(np.argmax(want_row))
+        ref_stream.append(w_tok)
+    assert gen.greedy(toks) == first or top2_margin(want) <= 2 * TOL
+    out = gen.generate(first, steps).tolist()
+    _stream_check(out, margins, ref_stream)
+    sess.close()
+    gen.close()
+    lm.close()
+    ref.close()

@@ -42,12 +42,18 @@ def _run(fn, c, out):
 
 
 def test_static_matches_allocating_entry_twice():
+    # Both entry points run the same kernels with the same splits, so their outputs agree bit for
+    # bit. The large gpt-oss-like case (about 1.3 MB of partials) runs first and leaves stale
+    # partials in every part of the scratch the small C2 case (about 130 KB) then reads; the large
+    # case runs again after it. Equality on every call shows that nothing in the scratch needs to
+    # start at zero.
     rng = np.random.default_rng(2024)
-    cases = [_case(rng, 1, 16, 8, 128, 1100, 0, False),   # the C2 decode shape
-             _case(rng, 5, 64, 8, 64, 300, 128, True)]    # gpt-oss-like: sinks, sliding window
-    for c in cases:  # two calls in a row: the second reuses the scratch the first left behind
+    big = _case(rng, 5, 64, 8, 64, 300, 128, True)     # gpt-oss-like: sinks, sliding window
+    small = _case(rng, 1, 16, 8, 128, 1100, 0, False)  # the C2 decode shape
+    for c in (big, small, big):
         ref = _run(A.lib().hc_attention_run, c, torch.empty_like(c["dev"]["q"]))
         got = _run(A.lib().hc_attention_run_static, c, torch.empty_like(c["dev"]["q"]))
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
         assert np.abs(got - ref).max() <= TOL * max(1.0, np.abs(ref).max())
 
 
