@@ -1,32 +1,45 @@
 #!/usr/bin/env python
-"""Decode benchmark of the B200 engine on BASELINE configs[1] (C2): a 28-layer 1.7B Qwen3
-decoder with int4 asymmetric group-32 weights, batch 1, a 1024-id random prompt, greedy steps.
+"""Decode benchmark of the B200 engine on BASELINE.json's headline metric: decode tokens/s of the
+64-sequence ragged batch (configs[4], C5) at 1/2/4/8 GPUs, with the batch-1 figures of the 1.7B
+model (configs[1], C2) nested under "bs1"; % of the HBM roofline for both.
 
-A step is one decoded token. The timed region runs K tokens as passes of 256 greedy steps from
-the same 1024-token prompt (the KV cache is truncated back to the prompt after each pass, so the
-context stays in 1024..1280, the configuration's). value: tokens/s of the device-resident loop
-(hc_generate: tokens fed back on the device), timed with CUDA events on the session's stream.
-e2e: the same through the per-token public call hc_step (token H2D, greedy choice D2H each step).
+Default line (no --workload): C5 continuous-batched ragged decode of the C2 model over the paged
+int8 KV cache. 64 sequences with contexts drawn uniform on 128..8192 (seed 2) are sharded round
+robin over the ranks (weights replicated, no collective on the path); a step is one hc_step call
+over every slot of the rank (each slot's next token, or the 512-id prompt of a new sequence that
+took a finished one's slot). W untimed steps, then exactly K timed steps. value: the decoded tokens
+of all ranks / the slowest rank's device time (the sum of the call's chunk graphs, CUDA events);
+"scaling": "strong" (the 64 sequences are the job whatever N). e2e: the same tokens over CUDA
+events around the whole host loop (token lists in from host memory, greedy choices out).
+bs1: C2 greedy decode after a 1024-id prompt on every rank (its own sequence), K tokens of the
+device-resident loop (hc_generate) and of the per-token public call (hc_step) in passes of 256
+from the prompt (context 1024-1280).
 
-Under torchrun (N > 1) every rank runs its own replica (sequences are independent; weights are
-replicated; no collective on the path): value = all ranks' tokens / the slowest rank's time.
+--impl reference times the reference path's CPU restatement (oracle/: the Go path cannot run
+here) on the host's cores for the same metric: weights built by the oracle's own generator (no
+call into libhwnpu_cuda.so), per-token decode costs sampled at two contexts and the prefill rate,
+extrapolated to the same C5 schedule; rank 0 only.
 
---impl reference times the reference path's CPU restatement (oracle/, the Go path cannot run
-here) on the host's cores for the same metric, rank 0 only.
+Workloads c2 / c1 (bs1 lines), c4 (speculative), linear (one GEMV) remain as --workload.
 """
 
 import argparse
+import hashlib
 import json
 import os
-import subprocess
 import sys
+import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+METRIC = "decode tokens/s (bs1, 64 ragged) at 1/2/4/8 B200; % HBM roofline"
 PROMPT = 1024
 PASS = 256
+C5_SEQS, C5_OWED, C5_NEW_PROMPT = 64, 128, 512
+# C2's paged int8 KV: int8 K and V rows + fp16 page scales, per position and layer, all layers
+C5_KV_POS = 28 * (8 * 128 * 2 + 2 * 8 * 2 / 16)
 
 
 def peaks():
@@ -38,92 +51,501 @@ def peaks():
         return 6650.0, "fallback"
 
 
-class Clocks:
-    """nvidia-smi samples during the timed region (clock and throttle reasons)."""
+def cpu_info():
+    model = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return os.cpu_count() or 1, model
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+class Clocks:
+    """SM clock and clock-event (throttle) reasons sampled through NVML every 10 ms while running."""
 
     def __init__(self, gpu):
-        self.gpu, self.p, self.path = gpu, None, None
+        self.gpu, self.samples, self.run, self.th = gpu, [], False, None
+        self.mx = None
 
     def start(self):
         try:
-            os.makedirs(os.path.join(ROOT, "gpurun_out"), exist_ok=True)
-            self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{self.gpu}_{os.getpid()}.csv")
-            self.f = open(self.path, "w")
-            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                       "-i", str(self.gpu), "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+            import pynvml as N
+
+            N.nvmlInit()
+            h = N.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.mx = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            names = {N.nvmlClocksThrottleReasonHwSlowdown: "hw_slowdown",
+                     N.nvmlClocksThrottleReasonHwThermalSlowdown: "hw_thermal_slowdown",
+                     N.nvmlClocksThrottleReasonSwThermalSlowdown: "sw_thermal_slowdown",
+                     N.nvmlClocksThrottleReasonSwPowerCap: "sw_power_cap"}
+
+            def loop():
+                while self.run:
+                    try:
+                        sm = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+                        r = N.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                        self.samples.append((sm, [v for k, v in names.items() if r & k]))
+                    except Exception:
+                        pass
+                    time.sleep(0.01)
+
+            self.run = True
+            self.th = threading.Thread(target=loop, daemon=True)
+            self.th.start()
         except Exception:
-            self.p = None
+            self.run = False
 
     def stop(self):
-        if not self.p:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.p.terminate()
-        self.p.wait()
-        self.f.close()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.run:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"], "samples": 0}
+        self.run = False
+        self.th.join()
+        sm = sorted(s for s, _ in self.samples)
+        reasons = sorted({r for _, rs in self.samples for r in rs})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": self.mx, "reasons": reasons,
+                "samples": len(sm), "source": "NVML every 10 ms during the timed region"}
 
 
-def build_model(workload):
-    import hwnpu_b200 as hb
-
-    cfg = {"c2": hb.C2, "c1": hb.C1}[workload]
-    return hb.Model(cfg, seed=0)
-
-
-def cpu_generate(model, prompt_len, steps, threads):
-    """The oracle (the reference path restated on the CPU): tokens/s of greedy decode steps after
-    a prefilled prompt; returns (tokens/s, seconds)."""
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
+def c5_contexts():
     import numpy as np
-    import oracle_lib as O
-    from hwnpu_b200 import synth
 
-    s = O.OracleSession(model, prompt_len + steps + 1, threads=threads)
-    toks = synth.tokens(1, model.cfg.vocab, prompt_len)
-    logits = s.step(toks)[0]
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        t = O.lib().or_argmax_f16(O.p(logits, O._u16p), model.cfg.vocab)
-        logits = s.step([t])[0]
-    dt = time.perf_counter() - t0
-    s.close()
-    return steps / dt, dt
+    return np.random.default_rng(2).integers(128, 8192, size=C5_SEQS, endpoint=True)
 
 
-def run_reference(args, rank):
+class C5Schedule:
+    """The C5 batch of one rank: each slot's owed decode steps (sequence i starts with 128 - 2 i,
+    so they finish at different steps) and, once done, a new sequence with a 512-id prompt in its
+    slot. Both arms walk the same schedule."""
+
+    def __init__(self, mine):
+        self.mine = list(mine)
+        self.owed = [C5_OWED - 2 * g for g in self.mine]
+        self.seed = [1000 + g * 64 for g in self.mine]
+        ctx = c5_contexts()
+        self.ctx = [int(ctx[g]) for g in self.mine]  # positions each slot holds
+
+    def step(self):
+        """Advances one step: returns per slot ("decode", None) or ("prompt", seed of the new ids)."""
+        out = []
+        for i in range(len(self.mine)):
+            if self.owed[i] <= 0:
+                self.seed[i] += 1
+                self.owed[i] = C5_OWED
+                self.ctx[i] = 0
+                out.append(("prompt", self.seed[i]))
+                self.ctx[i] += C5_NEW_PROMPT
+            else:
+                out.append(("decode", None))
+                self.ctx[i] += 1
+            self.owed[i] -= 1
+        return out
+
+
+# ---- the CPU side: the oracle (the reference path restated) on the host's cores ----------------
+class CpuSample:
+    """The oracle's C2 costs on this host, a bounded sample: the weights built by the oracle's own
+    generator (the GPU arm's bytes, tests/test_abi.py checks it; libhwnpu_cuda.so is never
+    mapped), a prefill of a 1024-id prompt timed (tokens/s of prompt reading), and greedy decode
+    steps timed at two contexts (after a 64-id prompt and after the 1024-id one), so that a decode
+    token's cost is modelled as t0 + t1 * context for the paged int8 cache (C5) or the fp16 cache
+    (bs1)."""
+
+    def __init__(self, threads, kv_format, decode_steps=3):
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        import numpy as np
+
+        import oracle_lib as O
+        from hwnpu_b200 import _abi as A
+        from hwnpu_b200 import synth
+
+        self.threads = threads
+        t0 = time.perf_counter()
+        model = synth.Model(synth.C2, seed=0, gen=O.OracleGen)
+        self.build_s = time.perf_counter() - t0
+        ctx_cap = PROMPT + decode_steps + 8
+        short = O.OracleSession(model, 64 + decode_steps + 8, threads=threads, kv_format=kv_format)
+        long_ = O.OracleSession(model, ctx_cap, threads=threads, kv_format=kv_format, share=short)
+
+        def decode(sess, prompt_len, seed):
+            toks = O.OracleGen.tokens(seed, synth.C2.vocab, prompt_len)
+            a = time.perf_counter()
+            logits = sess.step(toks)[0]
+            pre = time.perf_counter() - a
+            a = time.perf_counter()
+            for _ in range(decode_steps):
+                t = O.lib().or_argmax_f16(O.p(logits, O._u16p), synth.C2.vocab)
+                logits = sess.step([t])[0]
+            return pre, (time.perf_counter() - a) / decode_steps
+
+        _, d_short = decode(short, 64, 1)
+        pre, d_long = decode(long_, PROMPT, 1)
+        long_.close()
+        short.close()
+        self.prefill_tok_s = PROMPT / pre
+        self.c_short, self.c_long = 64 + decode_steps / 2.0, PROMPT + decode_steps / 2.0
+        self.t1 = max(0.0, (d_long - d_short) / (self.c_long - self.c_short))
+        self.t0 = d_short - self.t1 * self.c_short
+        self.d_short, self.d_long = d_short, d_long
+        self.wall_s = time.perf_counter() - t0
+        self.kv = "paged int8" if kv_format == A.HC_KV_INT8_PAGED else "fp16"
+
+    def token_s(self, ctx):
+        return self.t0 + self.t1 * ctx
+
+    def describe(self):
+        return (f"oracle C2 ({self.kv} KV) on {self.threads} threads: prefill of a {PROMPT}-id prompt "
+                f"{self.prefill_tok_s:.1f} tok/s; greedy decode {1e3 * self.d_short:.0f} ms/token at context "
+                f"{self.c_short:.0f} and {1e3 * self.d_long:.0f} ms/token at {self.c_long:.0f} "
+                f"(cost modelled as linear in the context); {self.wall_s:.0f} s of CPU work")
+
+
+def cpu_c5(sample, world, steps):
+    """tokens/s of the C5 schedule on the CPU (every rank's slots one after another on one host):
+    each decoded token at its context by the linear model, each new sequence's prompt at the
+    prefill rate; extrapolated from the sample."""
+    from hwnpu_b200 import replicas
+
+    total_s, dec = 0.0, 0
+    for r in range(world):
+        sch = C5Schedule(replicas.shard(C5_SEQS, r, world))
+        for _ in range(steps):
+            for i, (kind, _) in enumerate(sch.step()):
+                if kind == "prompt":
+                    total_s += C5_NEW_PROMPT / sample.prefill_tok_s
+                else:
+                    total_s += sample.token_s(sch.ctx[i])
+                dec += 1
+    return dec / total_s
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the oracle's C5 rate (and bs1 rate) on the host's cores, rank 0 only."""
     if rank != 0:
         return
-    model = build_model(args.workload)
-    threads = os.cpu_count()
-    steps = max(1, min(args.steps, 16))
-    tps, dt = cpu_generate(model, 64, steps, threads)
-    sample = (f"{steps} greedy decode tokens of the {args.workload.upper()} model after a 64-id prompt "
-              f"(per-token cost is the fp32 weight stream: the KV of 1024-1280 positions is ~2% of it)")
-    line = {"impl": "reference", "metric": "decode tokens/s", "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": steps, "warmup": 0, "higher_is_better": True, "data": "synthetic",
-            "config": workload_config(args),
-            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
-            "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    from hwnpu_b200 import _abi as A
+
+    cores, model_name = cpu_info()
+    if args.workload in ("default", "c5"):
+        s = CpuSample(cores, A.HC_KV_INT8_PAGED)
+        value = cpu_c5(s, world, args.steps)
+        sample = s.describe() + f"; extrapolated to {args.steps} steps of the C5 schedule ({C5_SEQS} sequences)"
+        config = c5_config(args, world)
+    else:
+        s = CpuSample(cores, A.HC_KV_F16)
+        value = 1.0 / s.token_s(PROMPT + (PASS + 1) / 2.0)
+        sample = s.describe() + f"; at the bs1 context {PROMPT}-{PROMPT + PASS}"
+        config = bs1_config(args, world)
+    base = {"value": value, "unit": "tokens/s", "cores": cores, "cpu": model_name, "kind": "port", "sample": sample}
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "data": "synthetic",
+            "config": config, "cpu_baseline": base,
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- the GPU side ---------------------------------------------------------------------------------
+def c5_config(args, world):
+    return {"workload": "C5 continuous-batched ragged decode: 64 sequences, contexts U[128,8192] (seed 2), "
+                        "128 steps owed each (staggered), finished ones replaced by 512-id prompts; "
+                        "paged int8 KV (16-position pages)",
+            "model": "C2 28L d2048 16q/8kv hd128 FFN6144 V151936 tied, int4 asym g32",
+            "global_batch": C5_SEQS, "parallelism": f"sequence shards x{world} (replicated weights)",
+            "l2": "inputs larger than L2 (1.1 GB of weights and ~15 GB of KV a step)"}
+
+
+def bs1_config(args, world):
+    return {"workload": f"C2 bs1 greedy decode: {PROMPT}-id random prompt, passes of {PASS} steps "
+                        f"(context {PROMPT}-{PROMPT + PASS})",
+            "model": "C2 28L d2048 16q/8kv hd128 FFN6144 V151936 tied, int4 asym g32",
+            "global_batch": world, "seq_len": PROMPT + PASS, "prompt": PROMPT, "steps_per_pass": PASS,
+            "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (the weights, ~1.1 GB, stream every token)"}
+
+
+def source_sha(rel):
+    try:
+        return hashlib.sha1(open(os.path.join(ROOT, rel), "rb").read()).hexdigest()[:16]
+    except OSError:
+        return None
+
+
+def profiled_traffic(name):
+    """DRAM bytes a launch of the named kernel moved in an ncu capture (profiles/<name>.json), when
+    the kernel's source file is still the one captured; else None."""
+    try:
+        rec = json.load(open(os.path.join(ROOT, "profiles", name + ".json")))
+    except Exception:
+        return None, None
+    if rec.get("source_sha1") != source_sha(rec.get("source", "")):
+        return None, f"profiles/{name}.json is from another build of {rec.get('source')}"
+    return rec.get("dram_bytes_per_launch"), f"profiles/{name}.json ({rec.get('workload')})"
+
+
+def kernel_roofline(dev, lin, ntok, label, profile_name, reps=50):
+    """The GEMV class of a step on one of its matrices, timed alone with CUDA events on torch's stream
+    (hc_linear_run: its activation quantiser launch included): algorithmic bytes = the matrix's
+    weight bytes per launch."""
+    import ctypes as C
+
+    import torch
+
+    from hwnpu_b200 import _abi as A
+
+    h = C.c_void_p()
+    A.check(A.lib().hc_linear_load(dev.h, C.byref(lin.desc()), C.byref(h)))
+    x = torch.randn(ntok, lin.cols, device="cuda")
+    y = torch.empty(ntok, lin.rows, device="cuda")
+    cs = torch.cuda.current_stream()
+
+    def once():
+        A.check(A.lib().hc_linear_run(h, C.c_void_p(x.data_ptr()), ntok, C.c_void_p(y.data_ptr()),
+                                      C.c_void_p(cs.cuda_stream)))
+
+    for _ in range(5):
+        once()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cs)
+    for _ in range(reps):
+        once()
+    e1.record(cs)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    A.lib().hc_linear_free(h)
+    wbytes = sum(a.nbytes for a in (lin.data, lin.scales, lin.zeros, lin.exps) if a is not None)
+    peak, kind = peaks()
+    ach = wbytes / (ms / 1e3) / 1e9
+    traffic, source = profiled_traffic(profile_name)
+    return {"bound": "hbm", "kernel": label, "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+            "peak_kind": kind, "traffic": traffic, "traffic_source": source, "bytes_per_launch": wbytes,
+            "ms_per_launch": ms, "tokens": ntok}
+
+
+def run_bs1(args, lm, model, dev, world, dist, K, W, persistent):
+    """C2 bs1 on this rank: the device-resident loop (value) and the public per-token call (e2e)."""
+    import torch
+
+    from hwnpu_b200 import replicas, synth
+
+    sess = lm.session(max_context=PROMPT + PASS + W + 8, max_step=8, persistent=persistent)
+    prompt = synth.tokens(1, model.cfg.vocab, PROMPT)
+    first = sess.greedy(prompt)
+    base = sess.pos()
+    sess.generate(first, W)
+    sess.truncate(base)
+    stream = torch.cuda.ExternalStream(sess.stream())
+    launches0 = sess.stats()["launches"]
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    done = 0
+    while done < K:
+        n = min(PASS, K - done)
+        sess.generate(first, n)
+        sess.truncate(base)
+        done += n
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    launches = sess.stats()["launches"] - launches0
+    barrier()
+    E = min(K, PASS)
+    tok = first
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(E):
+        tok = sess.greedy([tok])
+    f1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = f0.elapsed_time(f1)
+    sess.truncate(base)
+    sess.close()
+    barrier()
+    t_max = replicas.job_time(ms, dist, "cuda")
+    t_e2e = replicas.job_time(ms_e2e, dist, "cuda")
+    cfg = model.cfg
+    kv_per_pos = cfg.layers * cfg.kv_heads * cfg.head_dim * 2 * 2
+    bytes_tok = lm.weight_bytes + kv_per_pos * (PROMPT + (PASS + 1) / 2.0)
+    peak, peak_kind = peaks()
+    per_gpu = K / (t_max / 1e3)
+    return {"value": world * K / (t_max / 1e3), "unit": "tokens/s", "ms_per_step": t_max / K, "steps": K,
+            "e2e": {"value": world * E / (t_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * world,
+                    "d2h_bytes_per_step": 4 * world, "api": "hc_step per token (token in, greedy choice out)"},
+            "gpu_launches": int(launches), "path": "persistent step" if persistent else "kernel sequence",
+            "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": bytes_tok * per_gpu / 1e9,
+                              "frac": bytes_tok * per_gpu / 1e9 / peak, "peak": peak, "peak_kind": peak_kind,
+                              "ideal_tokens_per_s": peak * 1e9 / bytes_tok},
+            "config": bs1_config(args, world)}
+
+
+def run_c5(args, lm, world, rank, dist, K, W):
+    """The C5 batch of this rank (see the module docstring); returns the line's C5 figures."""
+    import torch
+
+    from hwnpu_b200 import _abi as A
+    from hwnpu_b200 import replicas, synth
+
+    mine = replicas.shard(C5_SEQS, rank, world)
+    n = len(mine)
+    ctx_all = c5_contexts()
+    max_ctx = int(ctx_all.max()) + C5_OWED + W + K + 16
+    warm = n  # an extra slot that runs the chunk shapes once before the timed steps
+    sess = lm.session(max_context=max_ctx, max_seqs=n + 1, kv_format=A.HC_KV_INT8_PAGED)
+    for k in range(1, 9):
+        sess.step_batch([warm], [synth.tokens(7, synth.C2.vocab, k)], want_logits=False)
+    sess.reset(warm)
+    sch = C5Schedule(mine)
+    t_fill = time.perf_counter()
+    last = []
+    for i, g in enumerate(mine):
+        _, am = sess.step_batch([i], [synth.tokens(100 + g, synth.C2.vocab, int(ctx_all[g]))], want_logits=False)
+        last.append(int(am[0]))
+    torch.cuda.synchronize()
+    fill_s = time.perf_counter() - t_fill
+    stream = torch.cuda.ExternalStream(sess.stream())
+
+    def run(steps, timed):
+        dec = prm = 0
+        dev_ms = kv = 0.0
+        for _ in range(steps):
+            plan = sch.step()
+            lists = []
+            for i, (kind, seed) in enumerate(plan):
+                if kind == "prompt":
+                    sess.reset(i)
+                    lists.append(synth.tokens(seed, synth.C2.vocab, C5_NEW_PROMPT))
+                else:
+                    lists.append([last[i]])
+            pos0 = [sess.pos(i) for i in range(n)] if timed else None
+            _, am = sess.step_batch(list(range(n)), lists, want_logits=False)
+            for i in range(n):
+                last[i] = int(am[i])
+            dec += n
+            prm += sum(len(l) - 1 for l in lists)
+            if timed:
+                dev_ms += sess.stats()["last_step_us"] / 1e3
+                for i in range(n):  # KV positions each token attends to (its own row included)
+                    m = len(lists[i])
+                    kv += C5_KV_POS * (m * pos0[i] + m * (m + 1) / 2)
+        return dec, prm, dev_ms, kv
+
+    run(W, False)
+    launches0 = sess.stats()["launches"]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    dec, prm, dev_ms, kv = run(K, True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    launches = sess.stats()["launches"] - launches0
+    sess.close()
+    t_dev = replicas.job_time(dev_ms, dist, "cuda")
+    t_e2e = replicas.job_time(e2e_ms, dist, "cuda")
+    dec_all = replicas.job_total(dec, dist, "cuda")
+    prm_all = replicas.job_total(prm, dist, "cuda")
+    kv_all = replicas.job_total(int(kv), dist, "cuda")
+    peak, peak_kind = peaks()
+    step_bytes = world * K * lm.weight_bytes + kv_all  # each rank reads its weights once a step
+    ach = step_bytes / (t_dev / 1e3) / 1e9 / world
+    return {"value": dec_all / (t_dev / 1e3), "ms_per_step": t_dev / K, "decoded_tokens": dec_all,
+            "prompt_tokens_read": prm_all, "prompt_tokens_per_s": prm_all / (t_dev / 1e3),
+            "e2e": {"value": dec_all / (t_e2e / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * (dec_all + prm_all) // K + 12 * C5_SEQS,
+                    "d2h_bytes_per_step": 4 * C5_SEQS,
+                    "api": "hc_step over every slot a step (host-built token lists in, greedy choices out)"},
+            "gpu_launches": int(launches),
+            "step_roofline": {"bytes_per_step": step_bytes / K, "achieved_gbs_per_gpu": ach, "peak": peak,
+                              "peak_kind": peak_kind, "frac": ach / peak,
+                              "weights_bytes_per_rank_step": lm.weight_bytes, "kv_bytes_per_step": kv_all / K},
+            "fill": {"slots_rank0": n, "seconds_rank0": fill_s}}
+
+
+def run_default(args, rank, world, local, dist):
+    import torch
+
+    import hwnpu_b200 as hb
+
+    K, W = args.steps, max(3, args.warmup)
+    dev = hb.Device(local)
+    model = hb.Model(hb.C2, seed=0)
+    lm = dev.load_model(model)
+    clocks = Clocks(local)
+    clocks.start()
+    c5 = run_c5(args, lm, world, rank, dist, K, W)
+    clk = clocks.stop()
+    bs1 = run_bs1(args, lm, model, dev, world, dist, K, W, args.persistent)
+    # the dominant kernel class of the C5 step: the batched GEMV (64 tokens on the MMA's n), on the
+    # largest matrix of a layer (gate/up, 12288 x 2048)
+    gu = hb.synth.Linear.quantize(hb.synth.normal(5, "bench.gate_up", 12288 * 2048, 0.02).reshape(12288, 2048),
+                                  hb._abi.HC_FMT_INT4_ASYM_G32)
+    roof = kernel_roofline(dev, gu, 64, "gemm_tn_kernel<int4, 64 tokens> on the C2 gate/up 12288x2048 "
+                           "(+ its activation quantiser)", "gemm_tn_c2_gateup64")
+    bs1["roofline"] = kernel_roofline(dev, gu, 1, "gemv_kernel<int4, 1 token> on the C2 gate/up 12288x2048 "
+                                      "(+ its activation quantiser)", "gemv_c2_gateup1")
+    lm.close()
+    dev.close()
+    if dist:
+        dist.barrier()
+    if rank != 0:
+        return
+    line = {"metric": METRIC, "value": c5["value"], "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": c5["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int4 weights x int8 (hi+lo) activations -> int32, f32 scaling; int8 KV x fp16 page scales",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform ids)", "config": c5_config(args, world),
+            "e2e": c5["e2e"], "gpu_launches": c5["gpu_launches"], "roofline": roof,
+            "step_roofline": c5["step_roofline"], "decoded_tokens": c5["decoded_tokens"],
+            "prompt_tokens_read": c5["prompt_tokens_read"], "prompt_tokens_per_s": c5["prompt_tokens_per_s"],
+            "fill": c5["fill"], "clocks": clk, "bs1": bs1}
+    if world == 1 and not args.no_cpu_baseline:
+        try:
+            from hwnpu_b200 import _abi as A
+
+            cores, cpu_model = cpu_info()
+            s = CpuSample(cores, A.HC_KV_INT8_PAGED)
+            v = cpu_c5(s, world, K)
+            line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "cpu": cpu_model, "kind": "port",
+                                    "sample": s.describe() + f"; extrapolated to the {K} timed steps of the C5 schedule"}
+            s16 = CpuSample(cores, A.HC_KV_F16)
+            bs1["cpu_baseline"] = {"value": 1.0 / s16.token_s(PROMPT + (PASS + 1) / 2.0), "unit": "tokens/s",
+                                   "cores": cores, "cpu": cpu_model, "kind": "port", "sample": s16.describe()}
+        except Exception as e:  # the baseline is reported, not required for the GPU number
+            line["cpu_baseline"] = {"value": None, "error": str(e)[:300]}
+    print(json.dumps(line), flush=True)
+
+
+def run_bs1_line(args, rank, world, local, dist, workload):
+    """--workload c2 / c1: the bs1 line alone (weak scaling: a sequence a rank)."""
+    import hwnpu_b200 as hb
+
+    K, W = args.steps, max(3, args.warmup)
+    dev = hb.Device(local)
+    model = hb.Model({"c2": hb.C2, "c1": hb.C1}[workload], seed=0)
+    lm = dev.load_model(model)
+    clocks = Clocks(local)
+    clocks.start()
+    r = run_bs1(args, lm, model, dev, world, dist, K, W, args.persistent)
+    clk = clocks.stop()
+    lm.close()
+    dev.close()
+    if rank != 0:
+        return
+    cfg = r.pop("config")
+    if workload == "c1":
+        cfg["workload"] = cfg["workload"].replace("C2", "C1")
+        cfg["model"] = "C1 4L d1024 16q/4kv hd64 FFN2816 V32000, int8 rows"
+    line = {"metric": "decode tokens/s", "unit": "tokens/s", "n_gpus": world, "warmup": W, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4/int8 weights x int8 (hi+lo) activations",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform ids)", "config": cfg, "clocks": clk, **r}
     print(json.dumps(line), flush=True)
 
 
@@ -220,157 +642,6 @@ def run_c4(args, rank, world, local, dist):
         raise SystemExit("speculative output differs from plain greedy decoding")
 
 
-C5_SEQS, C5_STEPS, C5_NEW_PROMPT = 64, 128, 512
-C5_KV_POS = 28 * (8 * 128 * 2 + 2 * 8 * 2 / 16)  # int8 K and V rows + fp16 page scales, per position
-
-
-def run_c5(args, rank, world, local, dist):
-    """C5: continuous-batched ragged decode of the C2 model over a paged
-    int8 KV cache (16-position pages, fp16 scale per page and KV head). 64 sequences with contexts
-    drawn uniform on 128..8192 (PCG64, seed 2), each owed 128 decode steps; the owed counts are
-    staggered (sequence i has 128 - 2i left) so that sequences finish at different steps, and a
-    finished one is replaced in its slot by a new sequence whose 512-id prompt is read in the same
-    batched step as the others' decode tokens. The 64 sequences are sharded round robin over the
-    ranks (replicas.shard), weights replicated, no collective on the path.
-
-    A timed step is one hc_step call over every slot of the rank (each slot's next token, or a new
-    prompt). value: the decoded tokens of all ranks / the slowest rank's device time (the sum of the
-    call's chunk graphs, CUDA events). e2e: the same tokens over CUDA events around the whole host
-    loop (token lists in, greedy choices out, slot replacement), max over ranks."""
-    import numpy as np
-    import torch
-
-    import hwnpu_b200 as hb
-    from hwnpu_b200 import _abi as A
-    from hwnpu_b200 import replicas, synth
-
-    ctx_all = np.random.default_rng(2).integers(128, 8192, size=C5_SEQS, endpoint=True)
-    mine = replicas.shard(C5_SEQS, rank, world)
-    n = len(mine)
-    dev = hb.Device(local)
-    model = hb.Model(hb.C2, seed=0)
-    lm = dev.load_model(model)
-    max_ctx = int(ctx_all.max()) + C5_STEPS + 16
-    warm = n  # an extra slot that runs the chunk shapes once before the timed steps
-    sess = lm.session(max_context=max_ctx, max_seqs=n + 1, kv_format=A.HC_KV_INT8_PAGED)
-    for k in range(1, 9):
-        sess.step_batch([warm], [synth.tokens(7, hb.C2.vocab, k)], want_logits=False)
-    sess.reset(warm)
-
-    # the starting state: every slot's context read as a prompt (untimed)
-    t_fill = time.perf_counter()
-    last, owed, ctx_tok = [], [], 0
-    for i, gi in enumerate(mine):
-        _, am = sess.step_batch([i], [synth.tokens(100 + gi, hb.C2.vocab, int(ctx_all[gi]))], want_logits=False)
-        last.append(int(am[0]))
-        owed.append(C5_STEPS - 2 * gi)
-        ctx_tok += int(ctx_all[gi])
-    torch.cuda.synchronize()
-    fill_s = time.perf_counter() - t_fill
-    stream = torch.cuda.ExternalStream(sess.stream())
-    new_seed = [1000 + gi * 64 for gi in mine]
-
-    def run(steps, timed):
-        """`steps` batched steps; returns (decoded tokens, prompt tokens, device ms, kv bytes)."""
-        dec = prm = 0
-        dev_ms = kv = 0.0
-        for _ in range(steps):
-            lists, fresh = [], []
-            for i in range(n):
-                if owed[i] <= 0:  # finished: a new sequence takes the slot
-                    sess.reset(i)
-                    new_seed[i] += 1
-                    lists.append(synth.tokens(new_seed[i], hb.C2.vocab, C5_NEW_PROMPT))
-                    owed[i] = C5_STEPS
-                    fresh.append(i)
-                else:
-                    lists.append([last[i]])
-            pos0 = [sess.pos(i) for i in range(n)] if timed else None
-            _, am = sess.step_batch(list(range(n)), lists, want_logits=False)
-            for i in range(n):
-                last[i] = int(am[i])
-                owed[i] -= 1
-            dec += n
-            prm += sum(len(l) - 1 for l in lists)
-            if timed:
-                dev_ms += sess.stats()["last_step_us"] / 1e3
-                for i in range(n):  # KV positions each token attends to (its own row included)
-                    m = len(lists[i])
-                    kv += C5_KV_POS * (m * pos0[i] + m * (m + 1) / 2)
-        return dec, prm, dev_ms, kv
-
-    W = max(3, args.warmup)
-    run(W, False)
-    if args.profile:  # a few steps between cudaProfilerStart/Stop (for ncu --profile-from-start off)
-        torch.cuda.synchronize()
-        torch.cuda.profiler.start()
-        dec, prm, dev_ms, _ = run(args.profile, True)
-        torch.cuda.synchronize()
-        torch.cuda.profiler.stop()
-        print(json.dumps({"profiled_steps": args.profile, "decoded": dec, "prompt_tokens": prm,
-                          "device_ms": dev_ms}), flush=True)
-        sess.close()
-        lm.close()
-        dev.close()
-        return
-    launches0 = sess.stats()["launches"]
-    clocks = Clocks(local)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clocks.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    dec, prm, dev_ms, kv = run(C5_STEPS, True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    e2e_ms = e0.elapsed_time(e1)
-    launches = sess.stats()["launches"] - launches0
-    t_dev = replicas.job_time(dev_ms, dist, "cuda")
-    t_e2e = replicas.job_time(e2e_ms, dist, "cuda")
-    dec_all = replicas.job_total(dec, dist, "cuda")
-    prm_all = replicas.job_total(prm, dist, "cuda")
-    kv_all = replicas.job_total(int(kv), dist, "cuda")
-    weight_bytes = lm.weight_bytes
-    sess.close()
-    lm.close()
-    dev.close()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
-    peak, peak_kind = peaks()
-    # algorithmic bytes: each rank reads its weights once per step, plus the KV every token touches
-    step_bytes = world * C5_STEPS * weight_bytes + kv_all
-    ach = step_bytes / (t_dev / 1e3) / 1e9 / world  # per GPU
-    line = {
-        "metric": "decode tokens/s", "value": dec_all / (t_dev / 1e3), "unit": "tokens/s", "n_gpus": world,
-        "steps": C5_STEPS, "warmup": W, "ms_per_step": t_dev / C5_STEPS, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None,
-        "dtype": "int4 x int8(hi+lo) MMA -> int32, f32 scaling; int8 KV x fp16 page scales",
-        "data": "synthetic (seeded N(0,0.02) weights, uniform ids)",
-        "config": {"workload": "C5 continuous-batched ragged decode: 64 sequences, contexts U[128,8192] (seed 2), "
-                               "128 steps owed each (staggered), finished ones replaced by 512-id prompts; "
-                               "paged int8 KV (16-position pages)",
-                   "model": "C2 28L d2048 16q/8kv hd128 FFN6144 V151936 tied, int4 asym g32",
-                   "global_batch": C5_SEQS, "parallelism": f"sequence shards x{world} (replicated weights)",
-                   "l2": "inputs larger than L2 (1.1 GB of weights and ~15 GB of KV a step)"},
-        "decoded_tokens": dec_all, "prompt_tokens_read": prm_all,
-        "prompt_tokens_per_s": prm_all / (t_dev / 1e3),
-        "e2e": {"value": dec_all / (t_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 16 * (dec_all + prm_all) // C5_STEPS,
-                "d2h_bytes_per_step": 4 * dec_all // C5_STEPS,
-                "api": "hc_step over every slot per step (host-built token lists, greedy choices out)"},
-        "gpu_launches": int(launches),
-        "step_roofline": {"bytes_per_step": step_bytes / C5_STEPS, "achieved_gbs_per_gpu": ach, "peak": peak,
-                          "peak_kind": peak_kind, "frac": ach / peak,
-                          "weights_bytes_per_rank_step": weight_bytes, "kv_bytes_per_step": kv_all / C5_STEPS},
-        "fill": {"context_tokens_rank0": ctx_tok, "seconds_rank0": fill_s},
-        "clocks": clk,
-    }
-    print(json.dumps(line), flush=True)
-
 
 def run_linear(args, local):
     """One C2-shaped matrix (hc_linear_load) run over --ntok tokens (hc_linear_run), timed with CUDA
@@ -424,55 +695,41 @@ def run_linear(args, local):
     dev.close()
 
 
-def workload_config(args):
-    return {"workload": f"{args.workload.upper()} bs1 greedy decode: 1024-id random prompt, passes of 256 steps "
-                        f"(context 1024-1280)",
-            "model": "C2 28L d2048 16q/8kv hd128 FFN6144 V151936 tied, int4 asym g32" if args.workload == "c2"
-            else "C1 4L d1024 16q/4kv hd64 FFN2816 V32000, int8 rows",
-            "global_batch": args.gpus, "seq_len": PROMPT + PASS, "prompt": PROMPT, "steps_per_pass": PASS,
-            "parallelism": f"replicas x{args.gpus}", "l2": "inputs larger than L2 (the weights, ~1.1 GB, stream every token)"}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2560)
+    ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["default", "c5", "c2", "c1", "c4", "linear"], default="default",
+                    help="default: the C5 64-sequence ragged decode line with the C2 bs1 figures nested; "
+                         "c2 / c1: a bs1 line alone; c4: speculative decoding (C1-shaped int8 draft with V151936 "
+                         "-> C2 target, k=4, 512 tokens from a 512-id prompt); linear: one GEMV")
     ap.add_argument("--rows", type=int, default=12288, help="--workload linear: matrix rows")
     ap.add_argument("--cols", type=int, default=2048, help="--workload linear: matrix columns")
     ap.add_argument("--ntok", type=int, default=64, help="--workload linear: tokens a call")
-    ap.add_argument("--workload", choices=["c2", "c1", "c4", "c5", "linear"], default="c2",
-                    help="c2: the headline bs1 decode; c1: the small int8 model; c4: speculative decoding "
-                         "(C1-shaped int8 draft with V151936 -> C2 target, k=4, 512 tokens from a 512-id prompt); "
-                         "c5: 64 ragged sequences over a paged int8 KV cache, sharded over the ranks")
-    ap.add_argument("--e2e-steps", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--chunk-trace", default=None,
-                    help="with --phases: save CTA 0's per-chunk ring events of the last step (.npy)")
-    ap.add_argument("--mk", action="store_true",
-                    help="run the step as the persistent one-launch kernel (experimental) instead of the kernel sequence")
+    ap.add_argument("--persistent", action="store_true",
+                    help="run bs1 decode steps as the persistent one-launch step instead of the kernel sequence")
     ap.add_argument("--phases", action="store_true",
-                    help="print the persistent step's per-phase timing (hc_profile_get) after a few steps and exit")
-    ap.add_argument("--profile", type=int, default=0,
-                    help="run this many decode steps between cudaProfilerStart/Stop after the warm-up and exit "
-                         "(for ncu --profile-from-start off)")
+                    help="print the persistent step's per-phase timing (hc_profile_get) of C2 bs1 and exit")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, world)
         return
     if args.workload == "linear":
         run_linear(args, local)
         return
+    if args.phases:
+        run_phases(args, local)
+        return
 
-    import numpy as np
     import torch
-
-    import hwnpu_b200 as hb
-    from hwnpu_b200 import synth
 
     torch.cuda.set_device(local)
     dist = None
@@ -482,167 +739,45 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
-    if args.workload == "c4":
+    if args.workload in ("default", "c5"):
+        run_default(args, rank, world, local, dist)
+    elif args.workload == "c4":
         run_c4(args, rank, world, local, dist)
-        if dist:
-            dist.destroy_process_group()
-        return
-    if args.workload == "c5":
-        run_c5(args, rank, world, local, dist)
-        return
-    W = max(3, args.warmup)
-    K = args.steps
-    model = build_model(args.workload)
-    dev = hb.Device(local)
-    lm = dev.load_model(model)
-    sess = lm.session(max_context=PROMPT + PASS + W + 8, max_step=8, profile=args.phases,
-                      megakernel=args.mk or args.phases)
-    prompt = synth.tokens(1, model.cfg.vocab, PROMPT)
-    first = sess.greedy(prompt)
-    base = sess.pos()
-    sess.generate(first, W)
-    sess.truncate(base)
-    stream = torch.cuda.ExternalStream(sess.stream())
-    if args.phases:
-        import numpy as np
-        acc = None
-        for _ in range(8):
-            sess.generate(first, 1)
-            ph = sess.profile()
-            acc = ph if acc is None else acc + ph
-        acc /= 8
-        cyc = sess.last_cycles
-        if args.chunk_trace:
-            np.save(args.chunk_trace, sess.last_chunks)
-            np.save(args.chunk_trace.replace(".npy", "_unit.npy"), sess.last_unit)
-        L = model.cfg.layers
-        names = ["qkv", "attention", "o", "gate/up", "down"]
-        per = {n: [round(float(x), 3) for x in acc[i:5 * L:5].mean(axis=0)] for i, n in enumerate(names)}
-        print(json.dumps({"phase_us_per_layer_inputs_weights_epilogue_barrier": per,
-                          "head": acc[5 * L].tolist(), "total_us": float(acc.sum()),
-                          "cycles_producer_waited_busy_consumer_waited_busy": [float(x) for x in cyc]}), flush=True)
-        return
-    if args.profile:
-        torch.cuda.synchronize()
-        torch.cuda.profiler.start()
-        sess.generate(first, args.profile)
-        torch.cuda.synchronize()
-        torch.cuda.profiler.stop()
-        print(json.dumps({"profiled_steps": args.profile, "launches_per_step": sess.stats()["launches"]}), flush=True)
-        return
-    launches0 = sess.stats()["launches"]
-
-    def barrier():
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    clocks = Clocks(local)
-    barrier()
-    clocks.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    done = 0
-    while done < K:
-        n = min(PASS, K - done)
-        sess.generate(first, n)
-        sess.truncate(base)
-        done += n
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    launches = sess.stats()["launches"] - launches0
-    clk = clocks.stop()
-    barrier()
-
-    # e2e: the public per-token call, token in from pinned host memory, choice out, every step
-    E = min(args.e2e_steps, PASS)
-    tok = first
-    barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for _ in range(E):
-        tok = sess.greedy([tok])
-    f1.record(stream)
-    torch.cuda.synchronize()
-    ms_e2e = f0.elapsed_time(f1)
-    sess.truncate(base)
-    barrier()
-
-    # the dominant kernel: the GEMV over the head (151936 x 2048 int4 g32, the largest launch),
-    # timed alone with CUDA events on torch's stream (act quantisation + GEMV of one token)
-    import ctypes as C
-
-    from hwnpu_b200 import _abi as A
-
-    h = C.c_void_p()
-    A.check(A.lib().hc_linear_load(dev.h, C.byref(model.head.desc()), C.byref(h)))
-    x = torch.randn(1, model.cfg.hidden, device="cuda")
-    y = torch.empty(1, model.cfg.vocab, device="cuda")
-    cs = torch.cuda.current_stream()
-    for _ in range(5):
-        A.check(A.lib().hc_linear_run(h, C.c_void_p(x.data_ptr()), 1, C.c_void_p(y.data_ptr()), C.c_void_p(cs.cuda_stream)))
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 50
-    g0.record(cs)
-    for _ in range(reps):
-        A.check(A.lib().hc_linear_run(h, C.c_void_p(x.data_ptr()), 1, C.c_void_p(y.data_ptr()), C.c_void_p(cs.cuda_stream)))
-    g1.record(cs)
-    torch.cuda.synchronize()
-    gemv_ms = g0.elapsed_time(g1) / reps
-    A.lib().hc_linear_free(h)
-    head_bytes = model.head.data.nbytes + model.head.scales.nbytes + (model.head.zeros.nbytes if model.head.zeros is not None else 0)
-
-    from hwnpu_b200 import replicas
-
-    # the job's time is the slowest replica's (every rank runs the same K steps of its own replica)
-    t_max = replicas.job_time(ms, dist, "cuda")
-    ms_e2e = replicas.job_time(ms_e2e, dist, "cuda")
-    cfg = model.cfg
-    kv_per_pos = cfg.layers * cfg.kv_heads * cfg.head_dim * 2 * 2
-    mean_ctx = PROMPT + (PASS + 1) / 2.0
-    bytes_tok = lm.weight_bytes + kv_per_pos * mean_ctx
-    peak, peak_kind = peaks()
-    value = world * K / (t_max / 1e3)
-    per_gpu = K / (ms / 1e3)
-    traffic = None
-    tf = os.path.join(ROOT, "profiles", "gemv_head_traffic.json")
-    if os.path.exists(tf):
-        try:
-            traffic = json.load(open(tf)).get("bytes_per_launch")
-        except Exception:
-            traffic = None
-    ach = head_bytes / (gemv_ms / 1e3) / 1e9
-    line = {
-        "metric": "decode tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": t_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int4 x int8(hi+lo) MMA -> int32, f32 scaling", "data": "synthetic (seeded N(0,0.02) weights, uniform ids)",
-        "config": workload_config(args),
-        "e2e": {"value": world * E / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 16,
-                "d2h_bytes_per_step": 4, "api": "hc_step per token (pinned token in, greedy choice out)"},
-        "gpu_launches": int(launches),
-        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<int4> on the 151936x2048 head (+ its act quantiser)",
-                     "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_kind": peak_kind,
-                     "traffic": traffic, "bytes_per_launch": head_bytes, "ms_per_launch": gemv_ms},
-        "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": bytes_tok * per_gpu / 1e9,
-                          "frac": bytes_tok * per_gpu / 1e9 / peak, "ideal_tokens_per_s": peak * 1e9 / bytes_tok},
-        "clocks": clk,
-    }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        try:
-            tps, dt = cpu_generate(model, 64, 8, os.cpu_count())
-            line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                                    "sample": f"8 greedy decode tokens after a 64-id prompt on the oracle ({dt:.1f} s)"}
-        except Exception as e:  # the baseline is reported, not required for the GPU number
-            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
-    sess.close()
-    lm.close()
-    dev.close()
+    else:
+        run_bs1_line(args, rank, world, local, dist, args.workload)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+
+
+def run_phases(args, local):
+    import torch
+
+    import hwnpu_b200 as hb
+    from hwnpu_b200 import synth
+
+    torch.cuda.set_device(local)
+    dev = hb.Device(local)
+    model = hb.Model(hb.C2, seed=0)
+    lm = dev.load_model(model)
+    sess = lm.session(max_context=PROMPT + 64, profile=True, persistent=True)
+    first = sess.greedy(synth.tokens(1, model.cfg.vocab, PROMPT))
+    sess.generate(first, 4)
+    acc = 0
+    units = 0
+    for _ in range(8):
+        sess.generate(first, 1)
+        acc = acc + sess.profile()
+        units = units + sess.last_units
+    acc /= 8
+    units /= 8
+    L = model.cfg.layers
+    names = ["qkv", "attention", "o", "gate/up", "down"]
+    per = {n: [round(float(x), 3) for x in acc[i:5 * L:5].mean(axis=0)] for i, n in enumerate(names)}
+    print(json.dumps({"phase_us_per_layer_inputs_work_barrier_stagewait": per, "head": acc[5 * L].tolist(),
+                      "total_us": float(acc[:, :3].sum()),
+                      "merging_unit_us_inputs_stages_partial_ticket_merge":
+                          [round(float(x), 3) for x in units[:, :5].mean(axis=0)]}), flush=True)
 
 
 if __name__ == "__main__":

@@ -7,7 +7,7 @@ mirror of the reference interfaces (engine.py) and the synthetic model builder (
 from . import _abi
 from ._abi import HcError, lib
 from .engine import Buffer, Device, LoadedModel, Provider, Session
-from .synth import C1, C2, C4_DRAFT, CONFIGS, Config, Linear, Model
+from .synth import C1, C2, C3, C4_DRAFT, CONFIGS, Config, Linear, Model
 
 __all__ = ["HcError", "lib", "Provider", "Device", "Buffer", "LoadedModel", "Session",
-           "Config", "Model", "Linear", "C1", "C2", "C4_DRAFT", "CONFIGS", "_abi"]
+           "Config", "Model", "Linear", "C1", "C2", "C3", "C4_DRAFT", "CONFIGS", "_abi"]

@@ -10,7 +10,7 @@ There is no fallback: without the library every call raises.
 import ctypes as C
 import os
 
-HC_ABI = 1
+HC_ABI = 2
 
 HC_STATE_COMPLETED, HC_STATE_ERROR, HC_STATE_TIMEOUT = 4, 5, 8
 HC_INFO_NAME, HC_INFO_PCI_BUS_ID, HC_INFO_ARCH, HC_INFO_MEMORY, HC_INFO_SMS, HC_INFO_DRIVER = range(6)
@@ -21,8 +21,7 @@ HC_FMT_INT8_ROW, HC_FMT_INT4_SYM_G32, HC_FMT_INT4_ASYM_G32, HC_FMT_MXFP4 = 2, 3,
 HC_ARCH_QWEN3, HC_ARCH_GPTOSS = 1, 2
 HC_MODEL_QK_NORM, HC_MODEL_TIED, HC_MODEL_NORM_SCALE, HC_MODEL_ATTN_BIAS = 1, 2, 4, 8
 HC_KV_F16, HC_KV_INT8_PAGED = 0, 1
-HC_SESSION_NO_GRAPH, HC_SESSION_MEGAKERNEL, HC_SESSION_PROFILE = 1, 2, 4
-MK_CHUNK_TRACE = 4096  # ring chunks of CTA 0 that hc_profile_get appends (kMkChunkTrace)
+HC_SESSION_NO_GRAPH, HC_SESSION_PERSISTENT, HC_SESSION_PROFILE = 1, 2, 4
 HC_STEP_ALL_ROWS = 1
 
 _p = C.c_void_p

@@ -30,6 +30,12 @@ std::atomic<long> g_stall_ms{0};  // "stall:MS": the next step first waits MS ms
 
 long take_stall_ms() { return g_stall_ms.exchange(0); }
 
+namespace {
+std::atomic<long long> g_spin_cycles{0};  // "spin:N": the next persistent step's waits give up after N cycles
+}  // namespace
+
+long long take_spin_cycles() { return g_spin_cycles.exchange(0); }
+
 bool fault_fires(FaultPoint p) {
   std::lock_guard<std::mutex> g(g_fault_mu);
   if (g_fault_point != int(p)) return false;
@@ -120,6 +126,10 @@ HC_API char *hc_set_fault(const char *spec) {
   std::string point = s.substr(0, colon);
   long n = std::strtol(s.c_str() + colon + 1, nullptr, 10);
   if (n < 1) return hc::make_error("hc_set_fault: N must be at least 1");
+  if (point == "spin") {
+    hc::g_spin_cycles = n;
+    return nullptr;
+  }
   if (point == "stall") {
     if (n > 2000) return hc::make_error("hc_set_fault: a stall is at most 2000 ms");
     hc::g_stall_ms = n;

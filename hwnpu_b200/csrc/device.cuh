@@ -231,6 +231,37 @@ __device__ __forceinline__ void wa_mma(const WTile<KIND> &wt, const BFrag<KIND> 
   }
 }
 
+// One warp quantises one group of 32 values (v is this lane's): hi = round_even(v * 127 / max),
+// the residual in lo at 1/256 of the scale (see common.h's kActTile); X is the group's sum of
+// (hi + lo / 256), the same on every lane.
+struct QGroup {
+  int8_t hq, lq;
+  float S, X;
+};
+__device__ __forceinline__ QGroup quant_vals(float v) {
+  const float m = warp_max(fabsf(v));
+  QGroup q{0, 0, 0.f, 0.f};
+  if (m > 0.f) {
+    const float inv = 127.0f / m;  // mxfp4.Vec.Quantize's inv (mxfp4.go:44)
+    q.S = m / 127.0f;
+    const float h = rintf(v * inv);
+    const float r = fmaf(-h, q.S, v);
+    const float l = fminf(fmaxf(rintf(r * (256.0f * inv)), -127.f), 127.f);
+    q.hq = int8_t(h);
+    q.lq = int8_t(l);
+    q.X = float(warp_sum_i(int(q.hq) * 256 + int(q.lq))) * (1.0f / 256.0f);
+  }
+  return q;
+}
+
+// Token-major tiles (up to 8 tokens): group gi of the tile at act_tile.
+__device__ __forceinline__ void quant_group(float v, uint8_t *act_tile, int gi, int lane) {
+  const QGroup q = quant_vals(v);
+  act_tile[gi * 64 + lane] = uint8_t(q.hq);
+  act_tile[gi * 64 + 32 + lane] = uint8_t(q.lq);
+  if (lane == 0) *reinterpret_cast<float2 *>(act_tile + kGroupsPerTile * 64 + gi * 8) = make_float2(q.S, q.X);
+}
+
 // Sums a lane value over the 4 lanes of one g (the groups c = 0..3): lane 4g ends with rows g, g+8.
 __device__ __forceinline__ float quad_sum(float v) {
   v += __shfl_xor_sync(0xffffffffu, v, 1);

@@ -7,7 +7,7 @@
 #include <vector>
 
 #include "kernels.h"
-#include "mk.h"
+#include "pstep.h"
 #include "repack.h"
 
 namespace hc {
@@ -90,13 +90,16 @@ struct hc_session {
   int32_t *am_dev = nullptr, *am_host = nullptr, *res_dev = nullptr, *res_host = nullptr;
   int32_t *gen_out = nullptr, *gen_count = nullptr;  // hc_generate's tokens [cap] and counter
   cudaGraphExec_t gen_graph = nullptr;
-  // the persistent one-launch step (mk.h), when the model has one
-  bool mk = false;
-  int mk_ctas = 0;
-  hc::MkLayer *mk_layers = nullptr;  // device [layers]
-  unsigned *mk_bar = nullptr;
-  int *mk_status = nullptr, *mk_status_host = nullptr;
-  unsigned long long *mk_trace = nullptr;  // HC_SESSION_PROFILE
+  // the persistent step (pstep.h), when the model and the device have one
+  bool ps = false;
+  int ps_ctas = 0, ps_kind = 0, ps_max_splits = 0, ps_max_tok = 0;
+  hc::PsLayer *ps_layers = nullptr;     // device [layers]
+  unsigned *ps_sync = nullptr;          // [0]: the grid barrier, from [4]: the merge and head tickets
+  size_t ps_sync_bytes = 0;
+  int *ps_status = nullptr, *ps_status_host = nullptr;
+  float *ps_attn = nullptr, *ps_part_ml = nullptr, *ps_part_o = nullptr, *ps_dx = nullptr;
+  unsigned long long *ps_trace = nullptr;  // HC_SESSION_PROFILE: CTA 0's barrier times
+  bool chunk_ps = false;                // the last chunk ran as the persistent step
   // captured step graphs by (tokens, accept kernel)
   std::map<int, cudaGraphExec_t> graphs;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;

@@ -19,10 +19,10 @@ hc_session::~hc_session() {
   for (auto &g : graphs) cudaGraphExecDestroy(g.second);
   if (gen_graph) cudaGraphExecDestroy(gen_graph);
   if (gen_out) cudaFree(gen_out);
-  for (void *p : {(void *)mk_layers,
-                  (void *)mk_bar, (void *)mk_status, (void *)mk_trace})
+  for (void *p : {(void *)ps_layers, (void *)ps_sync, (void *)ps_status, (void *)ps_trace, (void *)ps_attn,
+                  (void *)ps_part_ml, (void *)ps_part_o, (void *)ps_dx})
     if (p) cudaFree(p);
-  if (mk_status_host) cudaFreeHost(mk_status_host);
+  if (ps_status_host) cudaFreeHost(ps_status_host);
   if (gen_count) cudaFree(gen_count);
   for (void *p : {(void *)kp, (void *)vp, (void *)kps, (void *)vps, (void *)btab_dev, (void *)kv_stage})
     if (p) cudaFree(p);
@@ -180,11 +180,13 @@ int enqueue_chunk(hc_session *s, int n, bool accept, int splits, int heads) {
   return k;
 }
 
-// The persistent step's parameters for n tokens (one per sequence); gen: hc_generate's feedback.
-hc::MkParams mk_params(hc_session *s, int n, bool gen) {
+constexpr long long kSpinLimit = 4000000000ll;  // ~2 s of SM clocks: a wait of the persistent step
+
+// The persistent step's parameters for the n tokens in toks_dev; gen: hc_generate's feedback.
+hc::PsParams ps_params(hc_session *s, int n, bool gen, long long spin) {
   hc_model *m = s->m;
   const auto &d = m->d;
-  hc::MkParams p{};
+  hc::PsParams p{};
   p.layers = int(d.layers);
   p.D = int(d.hidden);
   p.F = int(d.inter);
@@ -194,13 +196,15 @@ hc::MkParams mk_params(hc_session *s, int n, bool gen) {
   p.V = int(d.vocab);
   p.cap = s->cap;
   p.ntok = n;
-  p.kind = m->head->m.kind;
-  p.kt_d = p.D / hc::kTileCols;
-  p.kt_f = p.F / hc::kTileCols;
-  p.kt_o = p.H * p.hd / hc::kTileCols;
+  p.kt_d = m->layers[0].qkv->m.ktiles;
+  p.kt_f = m->layers[0].down->m.ktiles;
+  p.kt_o = m->layers[0].o->m.ktiles;
   p.rt_qkv = m->layers[0].qkv->m.rtiles;
+  p.rt_o = m->layers[0].o->m.rtiles;
+  p.rt_gu = m->layers[0].gu->m.rtiles;
+  p.rt_down = m->layers[0].down->m.rtiles;
   p.rt_head = m->head->m.rtiles;
-  p.splits = std::max(1, std::min(hc::kMkMaxSplits, s->mk_ctas / (n * p.KV)));
+  p.max_splits = s->ps_max_splits;
   p.sc_in0 = m->norm_in0.scale;
   p.eps_in0 = m->norm_in0.eps16;
   p.sc = m->norm_mid.scale;
@@ -208,46 +212,42 @@ hc::MkParams mk_params(hc_session *s, int n, bool gen) {
   p.sc_head = m->norm_head.scale;
   p.eps_head = m->norm_head.eps16;
   p.score_scale = m->score_scale;
-  p.L = s->mk_layers;
+  p.L = s->ps_layers;
   p.head = m->head->m.tiles;
   p.head_scale = m->head->m.row_scale;
   p.embed = m->embed;
-  p.in_norm0 = m->layers[0].in_norm;
+  p.final_norm = m->final_norm;
   p.rope = s->rope;
   p.toks = s->toks_dev;
-  p.x = s->x;
-  p.h = s->h;
+  p.dx_o = s->x;
+  p.dx_down = s->ps_dx;
   p.qkv = s->qkv;
-  p.part_ml = s->part_ml;
-  p.part_o = s->part_o;
-  p.logits = s->logits_dev;
+  p.attn = s->ps_attn;
+  p.h = s->h;
+  p.part_ml = s->ps_part_ml;
+  p.part_o = s->ps_part_o;
+  p.tickets = reinterpret_cast<int *>(s->ps_sync + 4);
+  p.logits = gen ? nullptr : s->logits_dev;
   p.amax = s->amax;
   p.am = s->am_dev;
   p.gen_out = gen ? s->gen_out : nullptr;
   p.gen_count = gen ? s->gen_count : nullptr;
-  p.bar = s->mk_bar;
-  p.status = s->mk_status;
-  p.spin_limit = 4000000000ll;  // ~2 s of SM clocks
-  p.trace = s->mk_trace;
+  p.bar = s->ps_sync;
+  p.status = s->ps_status;
+  p.spin_limit = spin;
+  p.trace = s->ps_trace;
+  hc::ps_layout(p, s->ps_kind);
   return p;
 }
 
-// Enqueues the persistent step (barrier and status zeroed first); returns its launches.
-int enqueue_mk(hc_session *s, int n, bool gen) {
-  cudaMemsetAsync(s->mk_bar, 0, sizeof(unsigned), s->st);
-  cudaMemsetAsync(s->mk_status, 0, sizeof(int), s->st);
-  hc::mk_launch(mk_params(s, n, gen), s->mk_ctas, s->st);
+// Enqueues the persistent step (its barrier and tickets zeroed first); returns its launches.
+int enqueue_ps(hc_session *s, int n, bool gen, long long spin) {
+  cudaMemsetAsync(s->ps_sync, 0, s->ps_sync_bytes, s->st);
+  hc::ps_launch(ps_params(s, n, gen, spin), s->ps_kind, s->ps_ctas, s->st);
   return 1;
 }
 
-bool mk_chunk(const hc_session *s, int n) {
-  if (!s->mk || !hc::mk_supported(s->m->head->m.kind, n, int(s->m->d.head_dim), int(s->m->d.heads / s->m->d.kv_heads)))
-    return false;
-  for (int i = 0; i < n; ++i)
-    for (int j = 0; j < i; ++j)
-      if (s->toks_host[i].slot == s->toks_host[j].slot) return false;  // one token a sequence
-  return true;
-}
+bool ps_chunk(const hc_session *s, int n) { return s->ps && n <= s->ps_max_tok; }
 
 // The whole chunk: tokens in, greedy choices (and the accept result) out, as one graph. heads:
 // the rows read out (toks_host[j].head_src for j < heads; all n rows for accept).
@@ -255,18 +255,33 @@ char *run_chunk(hc_session *s, int n, bool accept, int heads) {
   for (int i = 0; i < n; ++i)
     if (char *e = ensure_pages(s, s->toks_host[i].slot, s->toks_host[i].pos, s->toks_host[i].pos + 1)) return e;
   cudaStream_t st = s->st;
-  const bool use_graph = !(s->o.flags & HC_SESSION_NO_GRAPH);
-  const bool mk = !accept && heads == n && mk_chunk(s, n);
-  const int splits = splits_for(s, n, chunk_max_len(s, n));
-  const int key = (((mk ? 0 : splits) * 128 + n) * 128 + heads) * 4 + (accept ? 1 : 0) + (mk ? 2 : 0);
+  // an armed "spin:N" fault runs this chunk once, outside the graphs, with waits of N cycles
+  const long long spin_fault = hc::take_spin_cycles();
+  const bool ps = ps_chunk(s, n);
+  const bool use_graph = !(s->o.flags & HC_SESSION_NO_GRAPH) && !(ps && spin_fault);
+  const int splits = ps ? 0 : splits_for(s, n, chunk_max_len(s, n));
+  const int key = ((splits * 128 + n) * 128 + heads) * 4 + (accept ? 1 : 0) + (ps ? 2 : 0);
+  s->chunk_ps = ps;
   auto enqueue_all = [&]() -> int {
     cudaMemcpyAsync(s->toks_dev, s->toks_host, sizeof(hc::StepTok) * n, cudaMemcpyHostToDevice, st);
-    int k = mk ? enqueue_mk(s, n, false) : enqueue_chunk(s, n, accept, splits, heads);
-    if (mk) cudaMemcpyAsync(s->mk_status_host, s->mk_status, sizeof(int), cudaMemcpyDeviceToHost, st);
-    if (heads > 0) cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * heads, cudaMemcpyDeviceToHost, st);
+    int k = 0;
+    if (ps) {
+      // every row's logits and greedy choice (row t: token t); the host picks the rows it reads
+      k = enqueue_ps(s, n, false, spin_fault ? spin_fault : kSpinLimit);
+      if (accept) { hc::spec_accept(s->am_dev, s->toks_dev, n, s->res_dev, st); ++k; }
+      cudaMemcpyAsync(s->ps_status_host, s->ps_status, sizeof(int), cudaMemcpyDeviceToHost, st);
+      cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
+    } else {
+      k = enqueue_chunk(s, n, accept, splits, heads);
+      if (heads > 0) cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * heads, cudaMemcpyDeviceToHost, st);
+    }
     if (accept) cudaMemcpyAsync(s->res_host, s->res_dev, sizeof(int32_t) * 2, cudaMemcpyDeviceToHost, st);
     return k;
   };
+  if (ps) {
+    *s->ps_status_host = 0;
+    cudaMemsetAsync(s->ps_status, 0, sizeof(int), st);
+  }
   if (use_graph && !s->graphs.count(key)) {
     cudaGraph_t graph = nullptr;
     HC_TRY_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
@@ -292,11 +307,13 @@ char *run_chunk(hc_session *s, int n, bool accept, int heads) {
   return nullptr;
 }
 
-// The persistent step's status after a wait: an error string when a barrier gave up.
-char *mk_status_error(hc_session *s) {
-  if (s->mk && *s->mk_status_host)
-    return hc::make_error("step: a device grid barrier timed out (phase " + std::to_string(*s->mk_status_host) + ")");
-  return nullptr;
+// The persistent step's status after a wait: an error string when one of its waits gave up.
+char *ps_status_error(hc_session *s) {
+  if (!s->ps || !*s->ps_status_host) return nullptr;
+  const int c = *s->ps_status_host;
+  std::string what = c < 100000 ? "grid barrier " + std::to_string(c) : c < 200000 ? "ring stage release (producer)"
+                     : c < 300000 ? "weight stage " + std::to_string(c - 200000) : "key stage " + std::to_string(c - 300000);
+  return hc::make_error("step: a device wait timed out (" + what + ")");
 }
 
 // Waits for the last chunk with a deadline (xrtshim.h's xs_run_wait with timeout_ms).
@@ -325,50 +342,60 @@ char *wait_done(hc_session *s, uint32_t timeout_ms, int32_t *state) {
   return nullptr;
 }
 
-// Sets up the persistent one-launch step when the model and the device allow it.
-char *mk_setup(hc_session *s) {
+// Sets up the persistent step when the model and the device allow it (a dense model of one integer
+// kind throughout, the fp16 cache, a cooperative launch of one CTA a SM).
+char *ps_setup(hc_session *s) {
   hc_model *m = s->m;
   const auto &d = m->d;
-  if (!(s->o.flags & HC_SESSION_MEGAKERNEL) || s->paged) return nullptr;
+  if (!(s->o.flags & HC_SESSION_PERSISTENT) || s->paged || d.arch != HC_ARCH_QWEN3) return nullptr;
   const int kind = m->head->m.kind, rep = int(d.heads / d.kv_heads);
-  if (!hc::mk_supported(kind, 1, int(d.head_dim), rep)) return nullptr;
-  if (d.hidden % hc::kTileCols || d.inter % hc::kTileCols || (d.heads * d.head_dim) % hc::kTileCols) return nullptr;
+  if (!hc::ps_supported(kind, int(d.head_dim), rep, s->cap)) return nullptr;
   for (auto &w : m->layers)
     if (w.qkv->m.kind != kind || w.o->m.kind != kind || w.gu->m.kind != kind || w.down->m.kind != kind ||
-        w.gu->m.bias || w.down->m.bias)
+        w.gu->m.bias || w.down->m.bias || w.sinks || w.qkv->m.ktiles != m->layers[0].qkv->m.ktiles)
       return nullptr;
-  int coop = 0;
-  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->ordinal);
-  if (!coop) return nullptr;
-  s->mk_ctas = hc::mk_max_ctas(m->ordinal);
-  hc::MkParams probe = mk_params(s, hc::kMkMaxTok, false);
-  const size_t smem = hc::mk_smem(probe, s->mk_ctas);
-  if (smem == 0) return nullptr;
-  HC_TRY_CUDA(hc::mk_prepare(225 * 1024));  // every layout mk_layout makes fits in it
-  std::vector<hc::MkLayer> L(d.layers);
+  if (m->head->m.ktiles != m->layers[0].qkv->m.ktiles) return nullptr;
+  HC_TRY_CUDA(hc::ps_prepare());
+  s->ps_ctas = hc::ps_ctas(m->ordinal);
+  if (!s->ps_ctas) return nullptr;
+  s->ps_kind = kind;
+  s->ps_max_splits = (s->cap + hc::kPsSplitKeys - 1) / hc::kPsSplitKeys;
+  // the most tokens a launch takes: its residual rows and activation tiles share the SM's shared
+  // memory with a ring of at least 4 stages
+  s->ps_max_tok = 0;
+  for (int n = 1; n <= hc::kPsMaxTok; ++n) {
+    hc::PsParams probe = ps_params(s, n, false, kSpinLimit);
+    if (hc::ps_layout(probe, kind)) s->ps_max_tok = n;
+  }
+  if (!s->ps_max_tok) return nullptr;
+  std::vector<hc::PsLayer> L(d.layers);
   for (size_t i = 0; i < L.size(); ++i) {
     const hc::LayerW &w = m->layers[i];
-    L[i] = hc::MkLayer{w.qkv->m.tiles, w.o->m.tiles, w.gu->m.tiles, w.down->m.tiles,
+    L[i] = hc::PsLayer{w.qkv->m.tiles, w.o->m.tiles, w.gu->m.tiles, w.down->m.tiles,
                        w.qkv->m.row_scale, w.o->m.row_scale, w.gu->m.row_scale, w.down->m.row_scale,
-                       w.qkv->m.bias, w.o->m.bias, w.post_norm,
-                       i + 1 < L.size() ? m->layers[i + 1].in_norm : m->final_norm,
-                       w.q_norm, w.k_norm, w.sinks,
+                       w.qkv->m.bias, w.o->m.bias, w.in_norm, w.post_norm, w.q_norm, w.k_norm, w.sinks,
                        s->kc + i * s->layer_kv, s->vc + i * s->layer_kv, w.window};
   }
-  if (char *e = alloc(&s->mk_layers, L.size(), "step layer table")) return e;
-  HC_TRY_CUDA(cudaMemcpy(s->mk_layers, L.data(), sizeof(hc::MkLayer) * L.size(), cudaMemcpyHostToDevice));
-  if (char *e = alloc(&s->mk_bar, 1, "grid barrier")) return e;
-  if (char *e = alloc(&s->mk_status, 1, "step status")) return e;
-  HC_TRY_CUDA(cudaMemset(s->mk_status, 0, sizeof(int)));
-  HC_TRY_CUDA(cudaHostAlloc(&s->mk_status_host, sizeof(int), cudaHostAllocDefault));
-  *s->mk_status_host = 0;
+  const int T = hc::kPsMaxTok, H = int(d.heads), hd = int(d.head_dim);
+  if (char *e = alloc(&s->ps_layers, L.size(), "step layer table")) return e;
+  HC_TRY_CUDA(cudaMemcpy(s->ps_layers, L.data(), sizeof(hc::PsLayer) * L.size(), cudaMemcpyHostToDevice));
+  s->ps_sync_bytes = sizeof(unsigned) * (4 + size_t(T) * d.kv_heads + 1);
+  if (char *e = alloc(&s->ps_sync, s->ps_sync_bytes / sizeof(unsigned), "grid barrier and tickets")) return e;
+  HC_TRY_CUDA(cudaMemset(s->ps_sync, 0, s->ps_sync_bytes));
+  if (char *e = alloc(&s->ps_status, 1, "step status")) return e;
+  HC_TRY_CUDA(cudaMemset(s->ps_status, 0, sizeof(int)));
+  HC_TRY_CUDA(cudaHostAlloc(&s->ps_status_host, sizeof(int), cudaHostAllocDefault));
+  *s->ps_status_host = 0;
+  if (char *e = alloc(&s->ps_attn, size_t(T) * H * hd, "attention output")) return e;
+  if (char *e = alloc(&s->ps_dx, size_t(T) * d.hidden, "down projection rows")) return e;
+  if (char *e = alloc(&s->ps_part_ml, size_t(T) * H * s->ps_max_splits * 2, "attention partials")) return e;
+  if (char *e = alloc(&s->ps_part_o, size_t(T) * H * s->ps_max_splits * hd, "attention partials")) return e;
   if (s->o.flags & HC_SESSION_PROFILE) {
-    const size_t n = (size_t(4) * hc::mk_phases(int(d.layers)) + 4) * s->mk_ctas + size_t(4) * hc::kMkChunkTrace +
-                     size_t(8) * d.layers;
-    if (char *e = alloc(&s->mk_trace, n, "phase trace")) return e;
-    HC_TRY_CUDA(cudaMemset(s->mk_trace, 0, n * sizeof(unsigned long long)));
+    const size_t n = size_t(4) * hc::ps_phases(int(d.layers)) + size_t(8) * d.layers;
+    if (char *e = alloc(&s->ps_trace, n, "phase trace")) return e;
+    HC_TRY_CUDA(cudaMemset(s->ps_trace, 0, n * sizeof(unsigned long long)));
   }
-  s->mk = true;
+  s->ps = true;
   return nullptr;
 }
 
@@ -459,7 +486,7 @@ HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session
   s->pos.assign(o.max_seqs, 0);
   s->poisoned.assign(o.max_seqs, false);
   HC_TRY_CUDA(cudaMemset(s->amax, 0, sizeof(unsigned long long) * T * hc::kAmaxSlots));
-  if (char *e = mk_setup(s.get())) return e;
+  if (char *e = ps_setup(s.get())) return e;
   *out = s.release();
   return nullptr;
 }
@@ -503,14 +530,13 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
     std::memcpy(s->toks_host, &all[c0], sizeof(hc::StepTok) * n);
     int heads = 0;  // the chunk's rows that are read out, in order
     for (size_t w = wi; w < want.size() && size_t(want[w]) < c0 + n; ++w) s->toks_host[heads++].head_src = int(want[w] - c0);
-    if (s->mk_status_host) *s->mk_status_host = 0;
     if (char *e = run_chunk(s, n, false, heads)) {
       for (int i = 0; i < nseq; ++i) s->poisoned[seq_ids[i]] = true;
       return e;
     }
     int32_t st_ = HC_STATE_ERROR;
     char *e = wait_done(s, timeout_ms, &st_);
-    if (!e && st_ == HC_STATE_COMPLETED) e = mk_status_error(s);
+    if (!e && st_ == HC_STATE_COMPLETED && s->chunk_ps) e = ps_status_error(s);
     if (e || st_ != HC_STATE_COMPLETED) {
       for (int i = 0; i < nseq; ++i) s->poisoned[seq_ids[i]] = true;
       if (state) *state = e ? HC_STATE_ERROR : st_;
@@ -518,8 +544,10 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
     }
     step_us += s->stats.last_step_us;
     for (int j = 0; wi < want.size() && size_t(want[wi]) < c0 + n; ++wi, ++row, ++j) {
-      if (argmax) argmax[row] = s->am_host[j];
-      if (logits) HC_TRY_CUDA(cudaMemcpy(logits + size_t(row) * V, s->logits_dev + size_t(j) * V, size_t(V) * 2, cudaMemcpyDeviceToHost));
+      // the kernel sequence writes the read rows in order; the persistent step every token's row
+      const int src = s->chunk_ps ? s->toks_host[j].head_src : j;
+      if (argmax) argmax[row] = s->am_host[src];
+      if (logits) HC_TRY_CUDA(cudaMemcpy(logits + size_t(row) * V, s->logits_dev + size_t(src) * V, size_t(V) * 2, cudaMemcpyDeviceToHost));
     }
   }
   uint64_t kv = 0;
@@ -554,9 +582,10 @@ HC_API char *hc_speculate(hc_session *s, int32_t seq, const int32_t *toks, int32
   if (char *e = run_chunk(s, n, true, n)) { s->poisoned[seq] = true; return e; }
   int32_t st_ = HC_STATE_ERROR;
   char *e = wait_done(s, timeout_ms, &st_);
+  if (!e && st_ == HC_STATE_COMPLETED && s->chunk_ps) e = ps_status_error(s);
   if (e || st_ != HC_STATE_COMPLETED) {
     s->poisoned[seq] = true;
-    if (state) *state = st_;
+    if (state) *state = e ? HC_STATE_ERROR : st_;
     return e;
   }
   *kept = s->res_host[0];
@@ -585,16 +614,14 @@ HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, i
   if (char *e = ensure_pages(s, seq, s->pos[seq], s->pos[seq] + n)) return e;
   cudaStream_t st = s->st;
   s->toks_host[0] = hc::StepTok{first, seq, s->pos[seq], 0};
-  const bool mk = s->mk && hc::mk_supported(s->m->head->m.kind, 1, int(s->m->d.head_dim),
-                                             int(s->m->d.heads / s->m->d.kv_heads));
+  const bool ps = ps_chunk(s, 1);
   if (!s->gen_graph) {
     cudaGraph_t graph = nullptr;
     HC_TRY_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    if (mk) {
-      // the status word is zeroed once before the loop: a failed launch makes the later ones return
-      cudaMemsetAsync(s->mk_bar, 0, sizeof(unsigned), st);
-      hc::mk_launch(mk_params(s, 1, true), s->mk_ctas, st);
-      s->launches_per_chunk[0] = 1;
+    if (ps) {
+      // the status word is zeroed once before the loop: after a failed launch the later ones
+      // return at once (they see it set)
+      s->launches_per_chunk[0] = uint64_t(enqueue_ps(s, 1, true, kSpinLimit));
     } else {
       s->launches_per_chunk[0] = uint64_t(enqueue_chunk(s, 1, false, splits_for(s, 1, 0), 1)) + 1;
       hc::advance(s->toks_dev, s->am_dev, s->gen_out, s->gen_count, st);
@@ -607,18 +634,21 @@ HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, i
   }
   HC_TRY_CUDA(cudaMemcpyAsync(s->toks_dev, s->toks_host, sizeof(hc::StepTok), cudaMemcpyHostToDevice, st));
   HC_TRY_CUDA(cudaMemsetAsync(s->gen_count, 0, sizeof(int32_t), st));
-  if (mk) HC_TRY_CUDA(cudaMemsetAsync(s->mk_status, 0, sizeof(int), st));
+  if (ps) {
+    *s->ps_status_host = 0;
+    HC_TRY_CUDA(cudaMemsetAsync(s->ps_status, 0, sizeof(int), st));
+  }
   HC_TRY_CUDA(cudaEventRecord(s->ev0, st));
   hc::device_stall(hc::take_stall_ms(), st);
   for (int i = 0; i < n; ++i) HC_TRY_CUDA(cudaGraphLaunch(s->gen_graph, st));
   HC_TRY_CUDA(cudaEventRecord(s->ev1, st));
-  if (mk) HC_TRY_CUDA(cudaMemcpyAsync(s->mk_status_host, s->mk_status, sizeof(int), cudaMemcpyDeviceToHost, st));
+  if (ps) HC_TRY_CUDA(cudaMemcpyAsync(s->ps_status_host, s->ps_status, sizeof(int), cudaMemcpyDeviceToHost, st));
   s->stats.launches += uint64_t(n) * s->launches_per_chunk[0];
   int32_t st_ = HC_STATE_ERROR;
   char *e = wait_done(s, timeout_ms, &st_);
-  if (!e && st_ == HC_STATE_COMPLETED && mk) {
+  if (!e && st_ == HC_STATE_COMPLETED && ps) {
     HC_TRY_CUDA(cudaStreamSynchronize(st));
-    e = mk_status_error(s);
+    e = ps_status_error(s);
   }
   if (e || st_ != HC_STATE_COMPLETED) {
     s->poisoned[seq] = true;
@@ -713,62 +743,36 @@ HC_API char *hc_seq_import_rows(hc_session *s, int32_t seq, int32_t start, int32
 
 HC_API char *hc_profile_get(hc_session *s, double *us, uint32_t cap, uint32_t *n) {
   if (!s || !n) return hc::make_error("hc_profile_get: NULL argument");
-  if (!s->mk_trace) return hc::make_error("hc_profile_get: the session was not opened with HC_SESSION_PROFILE and the persistent step");
-  const int P = hc::mk_phases(int(s->m->d.layers)), C = s->mk_ctas;
+  if (!s->ps_trace)
+    return hc::make_error("hc_profile_get: the session was not opened with HC_SESSION_PROFILE and the persistent step");
+  const int P = hc::ps_phases(int(s->m->d.layers));
   *n = uint32_t(P);
   if (!us) return nullptr;
-  std::vector<unsigned long long> t((size_t(4) * P + 4) * C);
+  std::vector<unsigned long long> t(size_t(4) * P);
   HC_TRY_CUDA(cudaStreamSynchronize(s->st));
-  HC_TRY_CUDA(cudaMemcpy(t.data(), s->mk_trace, t.size() * 8, cudaMemcpyDeviceToHost));
-  auto plane = [&](int k, int i, int c) { return t[(size_t(k) * P + i) * C + c]; };
-  unsigned long long prev = ~0ull;
-  for (int c = 0; c < C; ++c) prev = std::min(prev, plane(0, 0, c));
-  for (int i = 0; i < P && uint32_t(4 * i + 3) < cap; ++i) {
-    // the phase's marks (the slowest CTA of each): inputs ready, chunks consumed, arrival, release
-    unsigned long long m0 = 0, m1 = 0, arr = 0, rel = 0;
-    for (int c = 0; c < C; ++c) {
-      m0 = std::max(m0, plane(2, i, c));
-      m1 = std::max(m1, plane(3, i, c));
-      arr = std::max(arr, plane(0, i, c));
-      rel = std::max(rel, plane(1, i, c));
+  HC_TRY_CUDA(cudaMemcpy(t.data(), s->ps_trace, t.size() * 8, cudaMemcpyDeviceToHost));
+  auto d = [](unsigned long long a, unsigned long long b) { return b > a ? double(b - a) / 1e3 : 0.0; };
+  for (int i = 0; i < P; ++i) {
+    const unsigned long long start = i ? t[4 * (i - 1) + 2] : t[0];
+    const double v[4] = {d(start, t[4 * i]), d(t[4 * i], t[4 * i + 1]), i + 1 < P ? d(t[4 * i + 1], t[4 * i + 2]) : 0.0,
+                         double(t[4 * i + 3]) / 1e3};
+    for (int k = 0; k < 4; ++k)
+      if (uint32_t(4 * i + k) < cap) us[4 * i + k] = v[k];
+  }
+  // then, per layer, the attention unit that merged (token 0, kv head 0): microseconds from the
+  // unit's start to its inputs loaded, its stages in, its partial written, its ticket taken, the
+  // merge written; then the CTA and the unit's index in the CTA
+  const int L = int(s->m->d.layers);
+  if (cap >= uint32_t(4 * P + 8 * L)) {
+    std::vector<unsigned long long> u(size_t(8) * L);
+    HC_TRY_CUDA(cudaMemcpy(u.data(), s->ps_trace + size_t(4) * P, u.size() * 8, cudaMemcpyDeviceToHost));
+    for (int l = 0; l < L; ++l) {
+      const unsigned long long *m = &u[size_t(8) * l];
+      for (int k = 1; k < 6; ++k) us[4 * P + 8 * l + k - 1] = d(m[0], m[k]);
+      us[4 * P + 8 * l + 5] = double(m[6]);
+      us[4 * P + 8 * l + 6] = double(m[7]);
+      us[4 * P + 8 * l + 7] = 0;
     }
-    if (i == 0 || m0 < prev) m0 = prev;
-    if (m1 < m0) m1 = m0;
-    if (arr < m1) m1 = arr;
-    us[4 * i] = double(m0 - prev) / 1e3;      // activations into smem
-    us[4 * i + 1] = double(m1 - m0) / 1e3;    // chunks consumed
-    us[4 * i + 2] = double(arr - m1) / 1e3;   // epilogue to the last arrival
-    us[4 * i + 3] = double(rel - arr) / 1e3;  // the barrier
-    prev = rel;
-  }
-  // after the phases: the mean over CTAs of producer waited/busy and consumer (warp 0) waited/busy
-  // cycles of the step
-  if (cap >= uint32_t(4 * P + 4)) {
-    for (int k = 0; k < 4; ++k) {
-      double a = 0;
-      for (int c = 0; c < C; ++c) a += double(t[size_t(4) * P * C + size_t(c) * 4 + k]);
-      us[4 * P + k] = a / C;
-    }
-  }
-  // then CTA 0's ring chunks: [kMkChunkTrace][4] us since the step's first phase mark (0 = none)
-  if (cap >= uint32_t(4 * P + 4 + 4 * hc::kMkChunkTrace)) {
-    std::vector<unsigned long long> ct(size_t(4) * hc::kMkChunkTrace);
-    HC_TRY_CUDA(cudaMemcpy(ct.data(), s->mk_trace + t.size(), ct.size() * 8, cudaMemcpyDeviceToHost));
-    unsigned long long t0 = ~0ull;
-    for (int c = 0; c < C; ++c) t0 = std::min(t0, plane(0, 0, c));
-    for (size_t k = 0; k < ct.size(); ++k)
-      us[4 * P + 4 + k] = ct[k] ? (double(ct[k]) - double(t0)) / 1e3 : 0.0;
-  }
-  // then CTA 1's attention unit: [layers][8] clock cycles since the layer's event 0
-  const int Ly = int(s->m->d.layers);
-  if (cap >= uint32_t(4 * P + 4 + 4 * hc::kMkChunkTrace + 8 * Ly)) {
-    std::vector<unsigned long long> ut(size_t(8) * Ly);
-    HC_TRY_CUDA(cudaMemcpy(ut.data(), s->mk_trace + t.size() + size_t(4) * hc::kMkChunkTrace, ut.size() * 8,
-                           cudaMemcpyDeviceToHost));
-    for (int l = 0; l < Ly; ++l)
-      for (int k = 0; k < 8; ++k)
-        us[4 * P + 4 + 4 * hc::kMkChunkTrace + 8 * l + k] =
-            ut[8 * l + k] ? double(ut[8 * l + k]) - double(ut[8 * l]) : -1.0;
   }
   return nullptr;
 }

@@ -32,7 +32,7 @@ extern "C" {
 #endif
 
 /* The ABI version. A Go binding refuses a library of another (amdxrt/shim.go:124-128). */
-#define HC_ABI 1
+#define HC_ABI 2
 
 typedef struct hc_device hc_device;
 typedef struct hc_buf hc_buf;
@@ -218,8 +218,14 @@ enum {
 };
 enum {
   HC_SESSION_NO_GRAPH = 1 << 0,      /* launch the step's kernels one by one (no CUDA graph) */
-  HC_SESSION_MEGAKERNEL = 1 << 1,    /* run steps of one token a sequence as the persistent
-                                      * one-launch step instead of the kernel sequence (experimental) */
+  /* Run chunks of up to 8 tokens (decode steps, speculative verifies, small batches) of a dense
+   * model over the fp16 cache as the persistent step: one cooperative launch, one CTA a SM, a
+   * producer warp streaming each CTA's weight rows and cached keys through a shared-memory ring,
+   * attention splits fixed by position (a row computes the same in any chunk). Without it they run
+   * as the kernel sequence (one kernel an operation, chained by programmatic dependent launch),
+   * the faster of the two on B200 today. Longer chunks and the paged int8 cache always take the
+   * kernel sequence. */
+  HC_SESSION_PERSISTENT = 1 << 1,
   HC_SESSION_PROFILE = 1 << 2,       /* time the phases of the persistent step (hc_profile_get) */
 };
 
@@ -301,21 +307,26 @@ typedef struct hc_stats {
 HC_API char *hc_stats_get(hc_session *s, hc_stats *out);
 
 /* Per-phase timing of the last persistent step of a session opened with HC_SESSION_PROFILE (the
- * role of decode/profile.go:13-40, per-part times of a step), from the slowest CTA of each mark:
- * for phase i, us[4 i .. 4 i + 3] are the microseconds from the previous barrier's release to the
- * phase's inputs in shared memory, to its weights consumed, to the last CTA's arrival at the next
- * barrier, and to that barrier's release. Phases: embed, then 5 a layer (qkv, attention, o,
- * gate/up, down), head; *n gets their number. With cap >= 4 n + 4, us[4 n .. 4 n + 3] are the
- * step's mean SM cycles the stage producer waited for free stages, ran in all, and that the
- * consumers waited for full stages, ran in all. */
+ * role of decode/profile.go:13-40, per-part times of a step), as CTA 0 saw it: phases are 5 a layer
+ * (qkv GEMV, attention, o GEMV, gate/up, down) and the head; for phase i, us[4 i] is the time in
+ * microseconds from the previous grid barrier to the phase's inputs in shared memory, us[4 i + 1]
+ * to its work done, us[4 i + 2] to the next grid barrier passed, us[4 i + 3] the part of the work
+ * its first thread spent waiting for weight or key stages. *n gets the number of phases; us may be
+ * NULL to ask for it. With cap >= 4 n + 8 layers, us[4 n + 8 l ..] follow for each layer l: the
+ * attention unit that merged token 0's first kv head, microseconds from its start to its inputs
+ * loaded, its cached keys in, its partial written, its ticket taken and its merge written, then
+ * its CTA and its index among the CTA's units. */
 HC_API char *hc_profile_get(hc_session *s, double *us, uint32_t cap, uint32_t *n);
 
 /* Fault injection for tests (the reference fakes its drivers instead, testdata/zemock):
  * "alloc:N" fails the N-th device allocation from now, "h2d:N" the N-th host-to-device copy,
  * "step:N" the N-th hc_step, each with an error string; "stall:MS" (MS <= 2000) makes the next
  * hc_step, hc_speculate or hc_generate first wait MS milliseconds on the device, so that a shorter
- * timeout_ms runs out (HC_STATE_TIMEOUT, the sequences poisoned until hc_seq_reset); "" clears.
- * Nothing faults or hangs on the GPU: the stall is a bounded wait on the global timer. */
+ * timeout_ms runs out (HC_STATE_TIMEOUT, the sequences poisoned until hc_seq_reset); "spin:N" gives
+ * every wait of the next persistent step (grid barriers, ring stages) a limit of N clock cycles, so
+ * that a small N makes them give up and the call return the step's error; "" clears. Nothing faults
+ * or hangs on the GPU: the stall is a bounded wait on the global timer, and a persistent step whose
+ * wait gave up lets its copies land and returns. */
 HC_API char *hc_set_fault(const char *spec);
 
 /* ---------------------------------------------------------------------------------------- */

@@ -145,11 +145,50 @@ std::vector<float> f16_vec(const uint16_t *p, size_t n, float fill) {
   return v;
 }
 
+// One layer's MXFP4 experts as the checkpoint holds them (experts.MXFP4, host.go:62-66): gate_up
+// [experts * 2 inter][hidden] with gate rows even and up rows odd, down [experts * hidden][inter],
+// blocks of 16 bytes and one e8m0 exponent per 32 columns, float32 biases.
+struct Experts {
+  const uint8_t *gw = nullptr, *ge = nullptr, *dw = nullptr, *de = nullptr;
+  std::vector<float> gb, db;
+  bool present() const { return gw != nullptr; }
+};
+
 struct Layer {
   std::vector<float> in_norm, post_norm, q_norm, k_norm, sinks;
   Lin q, k, v, o, gate, up, down;
+  Lin router;  // gpt-oss: weights and bias as fp16 values (the program's F16s, gptoss/build.go:125-140)
+  Experts ex;
   int window = 0;
 };
+
+// gptoss.Config.RopeInvFreq (internal/llm/gptoss/config.go:136-166): YaRN's inverse frequencies
+// (transformers' _compute_yarn_parameters) and the factor the tables are scaled by.
+void yarn_inv_freq(const hc_model_desc &d, std::vector<double> &inv, float &factor) {
+  const int dim = int(d.head_dim), half = dim / 2;
+  inv.assign(half, 0);
+  if (d.yarn_factor <= 1) {
+    for (int i = 0; i < half; ++i) inv[i] = 1 / std::pow(d.rope_theta, double(2 * i) / double(dim));
+    factor = 1;
+    return;
+  }
+  auto corr = [&](double rot) {
+    return double(dim) * std::log(double(d.yarn_original) / (rot * 2 * M_PI)) / (2 * std::log(d.rope_theta));
+  };
+  double low = corr(d.yarn_beta_fast), high = corr(d.yarn_beta_slow);
+  if (d.yarn_truncate) { low = std::floor(low); high = std::ceil(high); }
+  low = std::max(low, 0.0);
+  high = std::min(high, double(dim - 1));
+  if (low == high) high += 0.001;
+  for (int i = 0; i < half; ++i) {
+    const double pos = std::pow(d.rope_theta, double(2 * i) / double(dim));
+    const double extra = 1 / pos, inter = 1 / (d.yarn_factor * pos);
+    const double ramp = std::min(std::max((double(i) - low) / (high - low), 0.0), 1.0);
+    const double ef = 1 - ramp;
+    inv[i] = inter * (1 - ef) + extra * ef;
+  }
+  factor = float(0.1 * std::log(d.yarn_factor) + 1);
+}
 
 }  // namespace
 
@@ -167,11 +206,58 @@ struct or_model {
 struct or_session {
   or_model *m;
   int cap, pos = 0;
+  int kv_format = HC_KV_F16;
   std::vector<std::vector<uint16_t>> kc, vc;  // per layer [kv_heads][cap][head_dim] fp16
+  // HC_KV_INT8_PAGED: per layer int8 rows [kv_heads][cap][head_dim] and fp16 scales
+  // [kv_heads][pages] for keys and for values
+  std::vector<std::vector<int8_t>> kq, vq;
+  std::vector<std::vector<uint16_t>> ks, vs;
 };
 
+namespace {
+
+constexpr int kOrPage = 16;  // positions a page of the int8 cache
+
+// The round-up of a float32 to fp16 (the page scale, the smallest fp16 not below v; v >= 0 and
+// finite here).
+float f16_round_up(float v) {
+  const uint16_t h = or_f16_bits(v);
+  float r = or_f16_value(h);
+  if (r < v) r = or_f16_value(uint16_t(h + 1));
+  return r;
+}
+
+// Writes row `off` of a page of the int8 cache (this library's paged format, which the reference
+// does not have: HC_KV_INT8_PAGED in include/hwnpu_cuda.h): the page's scale is the fp16 rounding
+// up of max|x| / 127 over its rows; a row that needs more requantises the page's earlier rows to the
+// new scale (q' = round_even(q * (s_old / s_new))), then the row is round_even(x * (1 / s)) clamped
+// to +-127.
+void page_write(int8_t *page_rows, uint16_t *scale, int off, const float *x, int hd) {
+  float m = 0;
+  for (int e = 0; e < hd; ++e) m = std::max(m, std::fabs(x[e]));
+  const float s_old = off == 0 ? 0.0f : or_f16_value(*scale);
+  float s_new = s_old;
+  if (m / 127.0f > s_old) {
+    s_new = f16_round_up(m / 127.0f);
+    if (off > 0 && s_old > 0) {
+      const float f = s_old / s_new;
+      for (int i = 0; i < off * hd; ++i) {
+        const float q = float(page_rows[i]);
+        page_rows[i] = int8_t(std::min(std::max(std::nearbyint(q * f), -127.0f), 127.0f));
+      }
+    }
+    *scale = or_f16_bits(s_new);
+  }
+  const float inv = s_new > 0 ? 1.0f / s_new : 0.0f;
+  for (int e = 0; e < hd; ++e)
+    page_rows[size_t(off) * hd + e] = int8_t(std::min(std::max(std::nearbyint(x[e] * inv), -127.0f), 127.0f));
+}
+
+}  // namespace
+
 OR_API or_model *or_model_new(const hc_model_desc *desc, int32_t threads) {
-  if (!desc || desc->arch != HC_ARCH_QWEN3) return nullptr;
+  if (!desc || (desc->arch != HC_ARCH_QWEN3 && desc->arch != HC_ARCH_GPTOSS)) return nullptr;
+  const bool gptoss = desc->arch == HC_ARCH_GPTOSS;
   auto *m = new or_model;
   m->d = *desc;
   m->pool = std::make_unique<Pool>(threads);
@@ -190,9 +276,24 @@ OR_API or_model *or_model_new(const hc_model_desc *desc, int32_t threads) {
     L.k = load_lin(*m->pool, ld.k);
     L.v = load_lin(*m->pool, ld.v);
     L.o = load_lin(*m->pool, ld.o);
-    L.gate = load_lin(*m->pool, ld.gate);
-    L.up = load_lin(*m->pool, ld.up);
-    L.down = load_lin(*m->pool, ld.down);
+    if (gptoss) {
+      L.router = load_lin(*m->pool, ld.router);
+      for (float &w : L.router.wt) w = f16r(w);
+      for (float &b : L.router.bias) b = f16r(b);
+      const hc_linear_desc &g = ld.experts_gate_up, &dn = ld.experts_down;
+      L.ex.gw = static_cast<const uint8_t *>(g.data);
+      L.ex.ge = g.exps;
+      L.ex.dw = static_cast<const uint8_t *>(dn.data);
+      L.ex.de = dn.exps;
+      L.ex.gb.assign(size_t(g.rows), 0.0f);
+      L.ex.db.assign(size_t(dn.rows), 0.0f);
+      if (g.bias) L.ex.gb.assign(g.bias, g.bias + g.rows);
+      if (dn.bias) L.ex.db.assign(dn.bias, dn.bias + dn.rows);
+    } else {
+      L.gate = load_lin(*m->pool, ld.gate);
+      L.up = load_lin(*m->pool, ld.up);
+      L.down = load_lin(*m->pool, ld.down);
+    }
     L.window = int(ld.sliding_window);
     if (ld.sinks) L.sinks.assign(ld.sinks, ld.sinks + d.heads);
     m->layers.push_back(std::move(L));
@@ -210,24 +311,49 @@ OR_API or_model *or_model_new(const hc_model_desc *desc, int32_t threads) {
       for (size_t i = 0; i < tmp.size(); ++i) m->embed[size_t(lo) * d.hidden + i] = or_f16_bits(tmp[i]);
     });
   }
-  // qwen3.Config.RopeInvFreq (internal/llm/qwen3/config.go:152-159)
-  m->inv_freq.resize(hd / 2);
-  for (int j = 0; j < hd / 2; ++j) m->inv_freq[j] = 1 / std::pow(d.rope_theta, double(2 * j) / double(hd));
+  if (gptoss) {
+    yarn_inv_freq(d, m->inv_freq, m->rope_factor);
+  } else {
+    // qwen3.Config.RopeInvFreq (internal/llm/qwen3/config.go:152-159)
+    m->inv_freq.resize(hd / 2);
+    for (int j = 0; j < hd / 2; ++j) m->inv_freq[j] = 1 / std::pow(d.rope_theta, double(2 * j) / double(hd));
+  }
   return m;
 }
 
 OR_API void or_model_free(or_model *m) { delete m; }
 
-OR_API or_session *or_session_new(or_model *m, int32_t max_context) {
+OR_API or_session *or_session_new_kv(or_model *m, int32_t max_context, int32_t kv_format) {
+  if (kv_format != HC_KV_F16 && kv_format != HC_KV_INT8_PAGED) return nullptr;
   auto *s = new or_session{m, max_context};
+  s->kv_format = kv_format;
   const auto &d = m->d;
-  s->kc.resize(d.layers);
-  s->vc.resize(d.layers);
-  for (uint32_t i = 0; i < d.layers; ++i) {
-    s->kc[i].assign(size_t(d.kv_heads) * max_context * d.head_dim, 0);
-    s->vc[i].assign(size_t(d.kv_heads) * max_context * d.head_dim, 0);
+  const size_t rows = size_t(d.kv_heads) * max_context * d.head_dim;
+  if (kv_format == HC_KV_F16) {
+    s->kc.resize(d.layers);
+    s->vc.resize(d.layers);
+    for (uint32_t i = 0; i < d.layers; ++i) {
+      s->kc[i].assign(rows, 0);
+      s->vc[i].assign(rows, 0);
+    }
+  } else {
+    const size_t pages = size_t(d.kv_heads) * ((max_context + kOrPage - 1) / kOrPage);
+    s->kq.resize(d.layers);
+    s->vq.resize(d.layers);
+    s->ks.resize(d.layers);
+    s->vs.resize(d.layers);
+    for (uint32_t i = 0; i < d.layers; ++i) {
+      s->kq[i].assign(rows, 0);
+      s->vq[i].assign(rows, 0);
+      s->ks[i].assign(pages, 0);
+      s->vs[i].assign(pages, 0);
+    }
   }
   return s;
+}
+
+OR_API or_session *or_session_new(or_model *m, int32_t max_context) {
+  return or_session_new_kv(m, max_context, HC_KV_F16);
 }
 
 OR_API void or_session_free(or_session *s) { delete s; }
@@ -265,6 +391,55 @@ void apply_rope(float *x, int hd, const float *cs, const float *sn) {
     float a = x[j] * cs[j];
     float b = r[j] * sn[j];
     x[j] = a + b;
+  }
+}
+
+// experts.Host.runRow (internal/llm/experts/host.go:478-591) of one row x (float32 of the fp16
+// moe_x): the row quantised per 32 (mxfp4.Vec.Quantize), each chosen expert's gate and up rows by
+// the MXFP4 dot product (mxfp4.Rows = Dot a row, matvec.go) plus their biases, gpt-oss's gated unit
+// (host.go:515-524: gate clamped above at limit, up to +-limit, g / (1 + exp(-alpha g)) * (up + 1),
+// the exp in float64), the activations quantised again, the down rows, and out += w_k (y + bias)
+// added in ascending expert number.
+void run_experts(Pool &pool, const hc_model_desc &d, const Experts &ex, const float *x, const int32_t *idx,
+                 const float *w, float *out) {
+  const int H = int(d.hidden), I = int(d.inter), K = int(d.top_k);
+  const float alpha = float(d.swiglu_alpha), limit = float(d.swiglu_limit);
+  std::vector<int8_t> xq(H);
+  std::vector<float> xs(H / 32);
+  or_mxfp4_quantize(x, uint32_t(H), xq.data(), xs.data());
+  std::vector<std::vector<float>> y(K, std::vector<float>(H));
+  for (int k = 0; k < K; ++k) {
+    const int e = idx[k];
+    std::vector<float> gu(size_t(2) * I);
+    pool.parallel_for(2 * I, 64, [&](long lo, long hi) {
+      for (long r = lo; r < hi; ++r) {
+        const size_t row = size_t(e) * 2 * I + r;
+        gu[r] = or_mxfp4_dot(ex.gw + row * (H / 2), ex.ge + row * (H / 32), uint32_t(H), xq.data(), xs.data()) +
+                ex.gb[row];
+      }
+    });
+    std::vector<float> act(I);
+    for (int j = 0; j < I; ++j) {
+      const float g = std::min(gu[2 * j], limit);
+      const float u = std::min(std::max(gu[2 * j + 1], -limit), limit);
+      act[j] = g / (1 + float(std::exp(double(-(alpha * g))))) * (u + 1);
+    }
+    std::vector<int8_t> hq(I);
+    std::vector<float> hs(I / 32);
+    or_mxfp4_quantize(act.data(), uint32_t(I), hq.data(), hs.data());
+    pool.parallel_for(H, 64, [&](long lo, long hi) {
+      for (long c = lo; c < hi; ++c) {
+        const size_t row = size_t(e) * H + c;
+        y[k][c] = or_mxfp4_dot(ex.dw + row * (I / 2), ex.de + row * (I / 32), uint32_t(I), hq.data(), hs.data());
+      }
+    });
+  }
+  std::vector<int> order(K);
+  for (int k = 0; k < K; ++k) order[k] = k;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return idx[a] < idx[b]; });
+  for (int k : order) {
+    const float *bias = ex.db.data() + size_t(idx[k]) * H;
+    for (int c = 0; c < H; ++c) out[c] += w[k] * (y[k][c] + bias[c]);
   }
 }
 
@@ -312,7 +487,19 @@ OR_API int32_t or_step(or_session *s, const int32_t *tokens, int32_t n, int32_t 
     // blocks.SDPAGrouped (blocks.go:516-539) over the cache (fp16 inputs) followed by the step's
     // own keys and values (float32 inside the program), with gpt-oss's sink column when present
     // (gptoss/build.go:256-285); masked keys weigh exactly 0 in the float64 softmax and are left out.
-    const auto &KC16 = s->kc[li], &VC16 = s->vc[li];
+    const bool paged = s->kv_format == HC_KV_INT8_PAGED;
+    const size_t npages = size_t((s->cap + kOrPage - 1) / kOrPage);
+    // cache row j of kv head kvh as float32: fp16 values, or int8 codes times the page's fp16 scale
+    auto cache_row = [&](bool val, int kvh, int j, float *out) {
+      if (!paged) {
+        const uint16_t *r = &(val ? s->vc : s->kc)[li][(size_t(kvh) * s->cap + j) * hd];
+        for (int e = 0; e < hd; ++e) out[e] = f16v(r[e]);
+      } else {
+        const int8_t *r = &(val ? s->vq : s->kq)[li][(size_t(kvh) * s->cap + j) * hd];
+        const float sc = f16v((val ? s->vs : s->ks)[li][size_t(kvh) * npages + j / kOrPage]);
+        for (int e = 0; e < hd; ++e) out[e] = float(r[e]) * sc;
+      }
+    };
     pool.parallel_for(long(n) * H, 1, [&](long lo, long hi) {
       std::vector<float> kv_k, kv_v, sc_(0), p;
       for (long job = lo; job < hi; ++job) {
@@ -324,10 +511,11 @@ OR_API int32_t or_step(or_session *s, const int32_t *tokens, int32_t n, int32_t 
         int nk = 0;
         std::vector<float> scores;
         std::vector<float> cache_v;
+        std::vector<float> crow(hd);
         for (int j = from; j < pos; ++j) {
-          const uint16_t *kr = &KC16[(size_t(kvh) * s->cap + j) * hd];
+          cache_row(false, kvh, j, crow.data());
           float acc = 0;
-          for (int e = 0; e < hd; ++e) acc = std::fma(qh[e], f16v(kr[e]), acc);
+          for (int e = 0; e < hd; ++e) acc = std::fma(qh[e], crow[e], acc);
           scores.push_back(acc * sscale);
           ++nk;
         }
@@ -359,8 +547,8 @@ OR_API int32_t or_step(or_session *s, const int32_t *tokens, int32_t n, int32_t 
           for (size_t j = j0; j < std::min(nkeys, j0 + KC); ++j) {
             if (scores[j] != scores[j]) continue;
             if (int(j) < ncache) {
-              const uint16_t *vr = &VC16[(size_t(kvh) * s->cap + from + j) * hd];
-              for (int e = 0; e < hd; ++e) blk[e] = std::fma(p[j], f16v(vr[e]), blk[e]);
+              cache_row(true, kvh, from + int(j), crow.data());
+              for (int e = 0; e < hd; ++e) blk[e] = std::fma(p[j], crow[e], blk[e]);
             } else {
               const float *vr = &v[(size_t(j - ncache) * KV + kvh) * hd];
               for (int e = 0; e < hd; ++e) blk[e] = std::fma(p[j], vr[e], blk[e]);
@@ -370,16 +558,50 @@ OR_API int32_t or_step(or_session *s, const int32_t *tokens, int32_t n, int32_t 
         }
       }
     });
-    // decode.Session.keep (decode.go:1685-1705): the step's rows into the cache as fp16
+    // decode.Session.keep (decode.go:1685-1705): the step's rows into the cache as fp16, or into the
+    // int8 pages in position order
     for (int t = 0; t < n; ++t)
-      for (int h = 0; h < KV; ++h)
-        for (int e = 0; e < hd; ++e) {
-          s->kc[li][(size_t(h) * s->cap + pos + t) * hd + e] = or_f16_bits(k[(size_t(t) * KV + h) * hd + e]);
-          s->vc[li][(size_t(h) * s->cap + pos + t) * hd + e] = or_f16_bits(v[(size_t(t) * KV + h) * hd + e]);
+      for (int h = 0; h < KV; ++h) {
+        if (!paged) {
+          for (int e = 0; e < hd; ++e) {
+            s->kc[li][(size_t(h) * s->cap + pos + t) * hd + e] = or_f16_bits(k[(size_t(t) * KV + h) * hd + e]);
+            s->vc[li][(size_t(h) * s->cap + pos + t) * hd + e] = or_f16_bits(v[(size_t(t) * KV + h) * hd + e]);
+          }
+        } else {
+          const int P = pos + t, page = P / kOrPage, off = P % kOrPage;
+          const size_t base = (size_t(h) * s->cap + size_t(page) * kOrPage) * hd;
+          page_write(&s->kq[li][base], &s->ks[li][size_t(h) * npages + page], off, &k[(size_t(t) * KV + h) * hd], hd);
+          page_write(&s->vq[li][base], &s->vs[li][size_t(h) * npages + page], off, &v[(size_t(t) * KV + h) * hd], hd);
         }
+      }
     // o_proj and the residual, then the MLP (qwen3 layerRest, build.go:184-189)
     linear(pool, L.o, o.data(), n, a.data());
     for (size_t i = 0; i < x.size(); ++i) x[i] = x[i] + a[i];
+    if (L.ex.present()) {
+      // gpt-oss's layer ends at its router (gptoss/build.go:121-140, moeHead): the post-attention
+      // norm (moe_x) and the router's logits leave the program as fp16, and so does the residual
+      // (the part's y); the host routes (experts.Routing.Choose, chain/moe.go:582-610), runs the
+      // experts and returns moe_o as fp16, which the next part adds to y in float32
+      const int E = int(d.experts), K = int(d.top_k);
+      std::vector<float> mx(size_t(n) * D), lg(size_t(n) * E);
+      for (int t = 0; t < n; ++t) {
+        rms_norm(&x[size_t(t) * D], D, L.post_norm.data(), 1.0f, d.norm_eps, &mx[size_t(t) * D]);
+        for (int c = 0; c < D; ++c) mx[size_t(t) * D + c] = f16r(mx[size_t(t) * D + c]);
+      }
+      linear(pool, L.router, mx.data(), n, lg.data());
+      for (float &v : lg) v = f16r(v);
+      for (int t = 0; t < n; ++t) {
+        std::vector<int32_t> idx(K);
+        std::vector<float> wk(K), mo(D, 0.0f);
+        or_route(&lg[size_t(t) * E], E, K, 1, idx.data(), wk.data());
+        run_experts(pool, d, L.ex, &mx[size_t(t) * D], idx.data(), wk.data(), mo.data());
+        for (int c = 0; c < D; ++c) {
+          float &xv = x[size_t(t) * D + c];
+          xv = f16r(xv) + f16r(mo[c]);
+        }
+      }
+      continue;
+    }
     for (int t = 0; t < n; ++t) rms_norm(&x[size_t(t) * D], D, L.post_norm.data(), sc, d.norm_eps, &hn[size_t(t) * D]);
     linear(pool, L.gate, hn.data(), n, g.data());
     linear(pool, L.up, hn.data(), n, u.data());

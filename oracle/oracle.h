@@ -83,6 +83,12 @@ typedef struct or_session or_session;
 OR_API or_model *or_model_new(const hc_model_desc *desc, int32_t threads);
 OR_API void or_model_free(or_model *m);
 OR_API or_session *or_session_new(or_model *m, int32_t max_context);
+/* A session over a cache of kv_format: HC_KV_F16 as or_session_new, or HC_KV_INT8_PAGED, this
+ * library's own paged int8 format restated (16-position pages, an fp16 scale per page and kv head
+ * rounded up from max|x| / 127, earlier rows requantised when it grows; the reference has no such
+ * cache, so this mode is parity unpinned): the step's own keys and values are used in float32 and
+ * go into the pages after the step, as decode.Session.keep does for the fp16 cache. */
+OR_API or_session *or_session_new_kv(or_model *m, int32_t max_context, int32_t kv_format);
 OR_API void or_session_free(or_session *s);
 OR_API int32_t or_session_pos(or_session *s);
 /* Session.Step (decode.go:1221): reads n tokens; writes fp16 logits of every row

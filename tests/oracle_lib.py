@@ -45,6 +45,7 @@ SIG = {
     "or_model_new": (C.c_void_p, [C.POINTER(A.ModelDesc), C.c_int32]),
     "or_model_free": (None, [C.c_void_p]),
     "or_session_new": (C.c_void_p, [C.c_void_p, C.c_int32]),
+    "or_session_new_kv": (C.c_void_p, [C.c_void_p, C.c_int32, C.c_int32]),
     "or_session_free": (None, [C.c_void_p]),
     "or_session_pos": (C.c_int32, [C.c_void_p]),
     "or_step": (C.c_int32, [C.c_void_p, _i32p, C.c_int32, C.c_int32, _u16p]),
@@ -145,12 +146,16 @@ class OracleGen:
 class OracleSession:
     """decode.Session on the CPU interpreter for a synth.Model."""
 
-    def __init__(self, model, max_context, threads=0):
+    def __init__(self, model, max_context, threads=0, kv_format=A.HC_KV_F16, share=None):
+        """share: another OracleSession of the same model whose (large) float32 weights this one
+        uses instead of its own copy."""
         self.model = model
         self.vocab = model.cfg.vocab
-        self.m = lib().or_model_new(C.byref(model.desc()), threads or os.cpu_count())
+        self.owner = share is None
+        self.m = lib().or_model_new(C.byref(model.desc()), threads or os.cpu_count()) if share is None else share.m
         assert self.m, "oracle: model not supported"
-        self.s = lib().or_session_new(self.m, max_context)
+        self.s = lib().or_session_new_kv(self.m, max_context, kv_format)
+        assert self.s, "oracle: kv format not supported"
 
     def step(self, toks, all_rows=False):
         toks = np.ascontiguousarray(toks, np.int32)
@@ -176,5 +181,6 @@ class OracleSession:
     def close(self):
         if self.s:
             lib().or_session_free(self.s)
-            lib().or_model_free(self.m)
+            if self.owner:
+                lib().or_model_free(self.m)
             self.s = self.m = None

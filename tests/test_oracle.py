@@ -2,6 +2,7 @@
 reference cannot run here) and against an independent float64 forward. No GPU."""
 
 import ctypes as C
+from dataclasses import replace
 import math
 
 import numpy as np
@@ -321,3 +322,68 @@ def test_oracle_speculate_equals_plain():
     assert out[:12] == out_plain
     plain.close()
     spec.close()
+
+
+def test_oracle_paged_int8_close_to_fp16():
+    # the oracle's restatement of the paged int8 cache (this library's own format; no reference):
+    # stepping token by token across page boundaries (scales grow, earlier rows get requantised)
+    # stays close to the fp16 cache
+    model = synth.Model(TINY, seed=19, norm_std=0.1)
+    toks = list(synth.tokens(8, TINY.vocab, 40))
+    f16 = O.OracleSession(model, 64)
+    pg = O.OracleSession(model, 64, kv_format=A.HC_KV_INT8_PAGED, share=f16)
+    f16.step(toks[:5])
+    pg.step(toks[:5])
+    for t in toks[5:]:
+        a = synth.f16_values(f16.step([t])[0])
+        b = synth.f16_values(pg.step([t])[0])
+        assert np.abs(a - b).max() <= 5e-2 * np.abs(a).max()
+    pg.close()
+    f16.close()
+
+
+# a gpt-oss-shaped model small enough for the CPU: sliding layers of a window of 8 alternate with
+# full ones, 8 experts, top 2
+TINY_GPTOSS = synth.Config("tiny-gptoss", 2, 256, 256, 4, 2, 64, 500, A.HC_FMT_MXFP4, norm_scale=False,
+                           rope_theta=150000.0, norm_eps=1e-5, arch="gptoss", experts=8, top_k=2, window=8,
+                           attn_fmt=A.HC_FMT_BF16, yarn=(32.0, 32.0, 1.0, 4096, False))
+
+
+def test_oracle_yarn_matches_formula():
+    # gptoss.Config.RopeInvFreq (gptoss/config.go:136-166) restated in numpy: the oracle's rotary
+    # tables (scaled by 0.1 ln(factor) + 1) drive its logits; a model with YaRN off differs
+    dim, theta, factor, bf, bs, orig = 64, 150000.0, 32.0, 32.0, 1.0, 4096
+    corr = lambda rot: dim * np.log(orig / (rot * 2 * np.pi)) / (2 * np.log(theta))
+    low, high = max(corr(bf), 0.0), min(corr(bs), dim - 1.0)
+    i = np.arange(dim // 2)
+    pos = theta ** (2 * i / dim)
+    ramp = np.clip((i - low) / (high - low), 0, 1)
+    inv = (1 / (factor * pos)) * ramp + (1 / pos) * (1 - ramp)
+    assert inv[0] == 1.0 and abs(inv[-1] - 1 / (factor * pos[-1])) < 1e-15
+    model = synth.Model(TINY_GPTOSS, seed=3, norm_std=0.1)
+    plain = synth.Model(replace(TINY_GPTOSS, yarn=(1.0, 32.0, 1.0, 4096, False)), seed=3, norm_std=0.1)
+    toks = list(synth.tokens(4, TINY_GPTOSS.vocab, 12))
+    a, b = O.OracleSession(model, 32), O.OracleSession(plain, 32)
+    la, lb = a.step(toks)[0], b.step(toks)[0]
+    assert not np.array_equal(la, lb)
+    a.close()
+    b.close()
+
+
+def test_oracle_gptoss_cached_matches_full():
+    # TestCachedMatchesFull's property for gpt-oss: stepping token by token over the caches (a
+    # sliding window of 8 crossed) equals one pass. The bound is twice qwen3's 5e-3: the fp16 cache
+    # against the pass's float32 keys moves moe_x a little, and its int8 quantisation per 32 in the
+    # experts (mxfp4.Vec.Quantize) turns that into whole steps of 1/127 of a group's largest value
+    model = synth.Model(TINY_GPTOSS, seed=5, norm_std=0.1)
+    toks = synth.tokens(6, TINY_GPTOSS.vocab, 14)
+    full = O.OracleSession(model, 32)
+    ref = synth.f16_values(full.step(toks, all_rows=True))
+    s = O.OracleSession(model, 32, share=full)
+    worst = 0.0
+    for i, t in enumerate(toks):
+        got = synth.f16_values(s.step([t])[0])
+        worst = max(worst, rel(got, ref[i]))
+    s.close()
+    full.close()
+    assert worst <= 1e-2, worst
