@@ -20,7 +20,8 @@ here) on the host's cores for the same metric: weights built by the oracle's own
 call into libhwnpu_cuda.so), per-token decode costs sampled at two contexts and the prefill rate,
 extrapolated to the same C5 schedule; rank 0 only.
 
-Workloads c2 / c1 (bs1 lines), c4 (speculative), linear (one GEMV) remain as --workload.
+Workloads c2 / c1 (bs1 lines), c3 (the MoE model at batch 1 and 16), c4 (speculative), linear
+(one GEMV) remain as --workload.
 """
 
 import argparse
@@ -549,6 +550,139 @@ def run_bs1_line(args, rank, world, local, dist, workload):
     print(json.dumps(line), flush=True)
 
 
+C3_PROMPT = 2048
+
+
+def run_c3(args, rank, world, local, dist):
+    """C3: the gpt-oss-shaped MoE model (24 layers, 32 MXFP4 experts of
+    2880, top 4, bf16 attention with sinks and 128-token windows on alternate layers), greedy decode
+    after 2048-id prompts at batch 1 (value: the device-resident loop, hc_generate) and batch 16 (16
+    sequences stepped together by hc_step, their experts grouped over the 16 tokens). One replica a
+    GPU. Weights: seeded synthetic tensors of the architecture (router N(0, 1/hidden) so that its
+    logits are about N(0, 1))."""
+    import torch
+
+    import hwnpu_b200 as hb
+    from hwnpu_b200 import replicas, synth
+
+    K, W = min(args.steps, 256), max(3, args.warmup)
+    torch.cuda.set_device(local)
+    dev = hb.Device(local)
+    t0 = time.perf_counter()
+    model = hb.Model(hb.C3, seed=0)
+    build_s = time.perf_counter() - t0
+    lm = dev.load_model(model)
+    load_s = time.perf_counter() - t0 - build_s
+    cfg = model.cfg
+    ctx = C3_PROMPT + K + W + 8
+    clocks = Clocks(local)
+    clocks.start()
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # batch 1: device-resident loop (value) and the per-token public call (e2e)
+    s1 = lm.session(max_context=ctx, max_step=8)
+    first = s1.greedy(synth.tokens(1, cfg.vocab, C3_PROMPT))
+    base = s1.pos()
+    s1.generate(first, W)
+    s1.truncate(base)
+    st1 = torch.cuda.ExternalStream(s1.stream())
+    l0 = s1.stats()["launches"]
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st1)
+    s1.generate(first, K)
+    e1.record(st1)
+    torch.cuda.synchronize()
+    ms1 = e0.elapsed_time(e1)
+    launches1 = s1.stats()["launches"] - l0
+    s1.truncate(base)
+    E = min(K, 64)
+    tok = first
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(st1)
+    for _ in range(E):
+        tok = s1.greedy([tok])
+    f1.record(st1)
+    torch.cuda.synchronize()
+    ms1_e2e = f0.elapsed_time(f1)
+    s1.close()
+
+    # batch 16: every sequence's next token in one hc_step a step
+    B = 16
+    s16 = lm.session(max_context=ctx, max_seqs=B, max_step=8)
+    last = []
+    t_fill = time.perf_counter()
+    for i in range(B):
+        _, am = s16.step_batch([i], [synth.tokens(10 + i, cfg.vocab, C3_PROMPT)], want_logits=False)
+        last.append(int(am[0]))
+    torch.cuda.synchronize()
+    fill_s = time.perf_counter() - t_fill
+    st16 = torch.cuda.ExternalStream(s16.stream())
+
+    def run(steps):
+        dev_ms = 0.0
+        for _ in range(steps):
+            _, am = s16.step_batch(list(range(B)), [[t] for t in last], want_logits=False)
+            last[:] = [int(a) for a in am]
+            dev_ms += s16.stats()["last_step_us"] / 1e3
+        return dev_ms
+
+    run(W)
+    l0 = s16.stats()["launches"]
+    barrier()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(st16)
+    dev16 = run(K)
+    g1.record(st16)
+    torch.cuda.synchronize()
+    ms16_e2e = g0.elapsed_time(g1)
+    launches16 = s16.stats()["launches"] - l0
+    s16.close()
+    clk = clocks.stop()
+    barrier()
+    t1 = replicas.job_time(ms1, dist, "cuda")
+    t1e = replicas.job_time(ms1_e2e, dist, "cuda")
+    t16 = replicas.job_time(dev16, dist, "cuda")
+    t16e = replicas.job_time(ms16_e2e, dist, "cuda")
+    peak, peak_kind = peaks()
+    # bytes a token reads at batch 1: the attention, router and head weights, top_k experts (the
+    # model's weight_bytes), and the cache its layers attend to (windowed layers 128 positions)
+    kv_pos = cfg.kv_heads * cfg.head_dim * 2 * 2
+    mid = C3_PROMPT + K / 2.0
+    kv_tok = kv_pos * (cfg.layers // 2) * (mid + min(mid, cfg.window))
+    b1 = lm.weight_bytes + kv_tok
+    per1 = K / (t1 / 1e3)
+    lm.close()
+    dev.close()
+    if rank != 0:
+        return
+    line = {"metric": "decode tokens/s (C3 MoE, batch 16; batch 1 nested)", "value": world * B * K / (t16 / 1e3),
+            "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": t16 / K,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "MXFP4 experts x int8 activations (integer block sums); bf16 attention/router/head x f32",
+            "data": "synthetic (seeded weights of the architecture, uniform ids)",
+            "config": {"workload": f"C3 greedy decode after {C3_PROMPT}-id prompts, batch 16 (16 sequences a "
+                                   f"replica), {K} steps", "model": "C3 24L d2880 64q/8kv hd64, 32 MXFP4 experts "
+                                   "(2880) top-4, window 128 on even layers, sinks, YaRN, V201088",
+                       "global_batch": world * B, "seq_len": ctx, "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2 (the attention and head weights, ~2.4 GB, stream every step)"},
+            "e2e": {"value": world * B * K / (t16e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * B * 3,
+                    "d2h_bytes_per_step": 4 * B, "api": "hc_step over the 16 sequences a step"},
+            "gpu_launches": int(launches16), "clocks": clk, "model_build_s": build_s, "model_load_s": load_s,
+            "fill": {"sequences": B, "seconds": fill_s},
+            "bs1": {"value": world * K / (t1 / 1e3), "unit": "tokens/s", "ms_per_step": t1 / K,
+                    "e2e": {"value": world * E / (t1e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                            "d2h_bytes_per_step": 4, "api": "hc_step per token"},
+                    "gpu_launches": int(launches1),
+                    "step_roofline": {"bytes_per_token": b1, "achieved_gbs": b1 * per1 / 1e9,
+                                      "frac": b1 * per1 / 1e9 / peak, "peak": peak, "peak_kind": peak_kind}}}
+    print(json.dumps(line), flush=True)
+
+
 def run_c4(args, rank, world, local, dist):
     """C4: greedy speculative decoding, the C1-shaped int8 draft (vocab
     151936) drafting k = 4 tokens a round and the C2 target verifying the 5 rows in one hc_speculate
@@ -703,9 +837,9 @@ def main():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["default", "c5", "c2", "c1", "c4", "linear"], default="default",
+    ap.add_argument("--workload", choices=["default", "c5", "c2", "c1", "c3", "c4", "linear"], default="default",
                     help="default: the C5 64-sequence ragged decode line with the C2 bs1 figures nested; "
-                         "c2 / c1: a bs1 line alone; c4: speculative decoding (C1-shaped int8 draft with V151936 "
+                         "c2 / c1: a bs1 line alone; c3: the gpt-oss-shaped MoE at batch 1 and 16; c4: speculative decoding (C1-shaped int8 draft with V151936 "
                          "-> C2 target, k=4, 512 tokens from a 512-id prompt); linear: one GEMV")
     ap.add_argument("--rows", type=int, default=12288, help="--workload linear: matrix rows")
     ap.add_argument("--cols", type=int, default=2048, help="--workload linear: matrix columns")
@@ -743,6 +877,8 @@ def main():
         run_default(args, rank, world, local, dist)
     elif args.workload == "c4":
         run_c4(args, rank, world, local, dist)
+    elif args.workload == "c3":
+        run_c3(args, rank, world, local, dist)
     else:
         run_bs1_line(args, rank, world, local, dist, args.workload)
     if dist:

@@ -253,12 +253,14 @@ const float kE2M1[8] = {0, 0.5f, 1, 1.5f, 2, 3, 4, 6};
 uint8_t e2m1_nearest(double x) {
   uint8_t sign = 0;
   if (x < 0) { sign = 8; x = -x; }
-  uint8_t c = 7;
-  for (uint8_t k = 0; k < 7; ++k) {
-    double mid = double(float(kE2M1[k] + kE2M1[k + 1])) / 2;
-    if (x < mid || (x == mid && k % 2 == 0)) { c = k; break; }
-    if (x == mid) { c = k + 1; break; }
-  }
+  // the midpoints between neighbouring magnitudes, as the rule computes them
+  static const struct Mids {
+    double v[7];
+    Mids() { for (int k = 0; k < 7; ++k) v[k] = double(float(kE2M1[k] + kE2M1[k + 1])) / 2; }
+  } mids;
+  // the code is the number of midpoints below x; a tie goes to the even code (k, or k + 1 when k is odd)
+  int c = 0;
+  for (int k = 0; k < 7; ++k) c += int(x > mids.v[k]) + int(x == mids.v[k] && (k & 1));
   return c == 0 ? 0 : uint8_t(sign | c);
 }
 
@@ -292,9 +294,10 @@ HC_API char *hc_mxfp4_encode(const float *w, uint32_t rows, uint32_t cols, uint8
             const int eb = x + 127;
             if (eb < 1 || eb > 254) continue;
             const double s = double(ffrom(uint32_t(eb) << 23));
+            const double inv = 1.0 / s;  // exact: s is a power of two
             double se = 0;
             for (int j = 0; j < 32; ++j) {
-              double d = double(blk[j]) - e2m1_value(e2m1_nearest(double(blk[j]) / s)) * s;
+              double d = double(blk[j]) - e2m1_value(e2m1_nearest(double(blk[j]) * inv)) * s;
               se += d * d;
             }
             if (se < best_err) { best = uint8_t(eb); best_err = se; }
@@ -305,8 +308,8 @@ HC_API char *hc_mxfp4_encode(const float *w, uint32_t rows, uint32_t cols, uint8
           exps[r * nb + b] = 0;
           continue;
         }
-        const double s = double(ffrom(uint32_t(best) << 23));
-        for (int j = 0; j < 32; ++j) codes[j] = e2m1_nearest(double(blk[j]) / s);
+        const double inv = 1.0 / double(ffrom(uint32_t(best) << 23));
+        for (int j = 0; j < 32; ++j) codes[j] = e2m1_nearest(double(blk[j]) * inv);
         for (int j = 0; j < 16; ++j) wb[j] = uint8_t(codes[2 * j] | (codes[2 * j + 1] << 4));
         exps[r * nb + b] = best;
       }

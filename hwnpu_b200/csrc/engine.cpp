@@ -2,6 +2,7 @@
 // repacked into integer-MMA tiles and copied to HBM once; the decode step lives in step.cpp.
 #include "engine.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -95,6 +96,178 @@ char *check_linear(const hc_linear_desc &l, uint32_t rows, uint32_t cols, const 
 // The fp16 constant of an epsilon after the norm's scale (qwen3 build.go:143).
 float eps16_of(double eps, double scale) { return f16_value(f16_bits(float(eps / (scale * scale)))); }
 
+// A device array of n floats (zeros where p is NULL).
+char *float_vec(hc_model *m, const float *p, size_t n, float **out) {
+  std::vector<float> v(n, 0.0f);
+  if (p) std::copy(p, p + n, v.begin());
+  void *d = nullptr;
+  if (char *e = hc::dev_alloc(&d, n * 4, "biases")) return e;
+  m->allocs.push_back(d);
+  if (char *e = hc::copy_h2d(d, v.data(), n * 4, nullptr)) return e;
+  HC_TRY_CUDA(cudaStreamSynchronize(nullptr));
+  *out = static_cast<float *>(d);
+  return nullptr;
+}
+
+// The rows of the parts (bf16 or fp16 [rows][cols], one format) one after another as a device
+// matrix of 16-bit floats, with their biases. to_f16: the values rounded to fp16 (gpt-oss's
+// programs hold the router's weights and bias as fp16, gptoss/build.go:125-140).
+char *load_dense(hc_model *m, const std::vector<const hc_linear_desc *> &parts, bool to_f16, hc::DevDense *out,
+                 const char *what) {
+  const int fmt = parts[0]->format;
+  const uint32_t cols = parts[0]->cols;
+  uint32_t rows = 0;
+  bool any_bias = false;
+  for (auto *d : parts) {
+    if (d->format != HC_FMT_BF16 && d->format != HC_FMT_F16)
+      return hc::make_error(std::string(what) + ": gpt-oss's attention, router and head take bf16 or fp16");
+    if (d->format != fmt || d->cols != cols) return hc::make_error(std::string(what) + ": parts of different formats");
+    rows += d->rows;
+    any_bias |= d->bias != nullptr;
+  }
+  if (cols % 8) return hc::make_error(std::string(what) + ": columns not a multiple of 8");
+  std::vector<uint16_t> w(size_t(rows) * cols);
+  std::vector<float> b(rows, 0.0f);
+  size_t r0 = 0;
+  for (auto *d : parts) {
+    const uint16_t *src = static_cast<const uint16_t *>(d->data);
+    const size_t n = size_t(d->rows) * cols;
+    for (size_t i = 0; i < n; ++i) {
+      uint16_t v = src[i];
+      if (to_f16 && fmt == HC_FMT_BF16) {
+        uint32_t u = uint32_t(v) << 16;
+        float f;
+        std::memcpy(&f, &u, 4);
+        v = f16_bits(f);
+      }
+      w[r0 * cols + i] = v;
+    }
+    if (d->bias)
+      for (uint32_t r = 0; r < d->rows; ++r) b[r0 + r] = to_f16 ? f16_value(f16_bits(d->bias[r])) : d->bias[r];
+    r0 += d->rows;
+  }
+  void *dw = nullptr;
+  if (char *e = hc::dev_alloc(&dw, w.size() * 2, what)) return e;
+  m->allocs.push_back(dw);
+  if (char *e = hc::copy_h2d(dw, w.data(), w.size() * 2, nullptr)) return e;
+  HC_TRY_CUDA(cudaStreamSynchronize(nullptr));
+  out->w = static_cast<const uint16_t *>(dw);
+  out->rows = int(rows);
+  out->cols = int(cols);
+  out->bf16 = fmt == HC_FMT_BF16 && !to_f16;
+  out->bias = nullptr;
+  if (any_bias) {
+    float *db = nullptr;
+    if (char *e = float_vec(m, b.data(), b.size(), &db)) return e;
+    out->bias = db;
+  }
+  return nullptr;
+}
+
+// gptoss.Config.RopeInvFreq (internal/llm/gptoss/config.go:136-166): YaRN's inverse frequencies and
+// the factor its rotary tables are scaled by (0.1 ln(factor) + 1).
+void yarn(const hc_model_desc &d, std::vector<double> &inv, float &factor) {
+  const int dim = int(d.head_dim), half = dim / 2;
+  inv.assign(half, 0.0);
+  if (d.yarn_factor <= 1) {
+    for (int i = 0; i < half; ++i) inv[i] = 1 / std::pow(d.rope_theta, double(2 * i) / double(dim));
+    factor = 1.f;
+    return;
+  }
+  auto corr = [&](double rot) {
+    return double(dim) * std::log(double(d.yarn_original) / (rot * 2 * M_PI)) / (2 * std::log(d.rope_theta));
+  };
+  double low = corr(d.yarn_beta_fast), high = corr(d.yarn_beta_slow);
+  if (d.yarn_truncate) {
+    low = std::floor(low);
+    high = std::ceil(high);
+  }
+  low = std::max(low, 0.0);
+  high = std::min(high, double(dim - 1));
+  if (low == high) high += 0.001;
+  for (int i = 0; i < half; ++i) {
+    const double pos = std::pow(d.rope_theta, double(2 * i) / double(dim));
+    const double ramp = std::min(std::max((double(i) - low) / (high - low), 0.0), 1.0);
+    const double ef = 1 - ramp;  // the share of extrapolation
+    inv[i] = (1 / (d.yarn_factor * pos)) * (1 - ef) + (1 / pos) * ef;
+  }
+  factor = float(0.1 * std::log(d.yarn_factor) + 1);
+}
+
+char *check_shape(const hc_linear_desc &l, uint32_t rows, uint32_t cols, const char *what) {
+  if (l.format == HC_FMT_NONE) return hc::make_error(std::string(what) + ": missing");
+  if (l.rows != rows || l.cols != cols)
+    return hc::make_error(std::string(what) + ": shape " + std::to_string(l.rows) + "x" + std::to_string(l.cols) +
+                          ", expected " + std::to_string(rows) + "x" + std::to_string(cols));
+  return nullptr;
+}
+
+// The weights of a gpt-oss model (HC_ARCH_GPTOSS, internal/llm/gptoss): bf16 q/k/v/o with biases,
+// sinks, sliding and full layers, YaRN, a router and MXFP4 experts with biases, an untied bf16 head.
+char *load_gptoss(hc_model *m, const hc_model_desc &d) {
+  const uint32_t D = d.hidden, hd = d.head_dim, I = d.inter, E = d.experts, K = d.top_k;
+  if (!E || !K || K > E || K > 8) return hc::make_error("hc_model_load: gpt-oss needs experts and 1 <= top_k <= 8 of them");
+  if (!d.embed) return hc::make_error("hc_model_load: gpt-oss's head is untied: an embedding table is needed");
+  if (D % 32 || I % 32) return hc::make_error("hc_model_load: hidden and inter must be multiples of MXFP4's 32");
+  m->gptoss = true;
+  m->norm_in0 = m->norm_mid = m->norm_head = {1.f, eps16_of(d.norm_eps, 1)};
+  uint64_t expert_bytes = 0;
+  for (uint32_t i = 0; i < d.layers; ++i) {
+    const hc_layer_desc &L = d.layer[i];
+    const std::string p = "layer " + std::to_string(i) + " ";
+    if (char *e = check_shape(L.q, d.heads * hd, D, (p + "q").c_str())) return e;
+    if (char *e = check_shape(L.k, d.kv_heads * hd, D, (p + "k").c_str())) return e;
+    if (char *e = check_shape(L.v, d.kv_heads * hd, D, (p + "v").c_str())) return e;
+    if (char *e = check_shape(L.o, D, d.heads * hd, (p + "o").c_str())) return e;
+    if (char *e = check_shape(L.router, E, D, (p + "router").c_str())) return e;
+    if (char *e = check_shape(L.experts_gate_up, E * 2 * I, D, (p + "experts gate_up").c_str())) return e;
+    if (char *e = check_shape(L.experts_down, E * D, I, (p + "experts down").c_str())) return e;
+    if (L.experts_gate_up.format != HC_FMT_MXFP4 || L.experts_down.format != HC_FMT_MXFP4)
+      return hc::make_error(p + "experts: MXFP4 only");
+    hc::LayerW w;
+    if (char *e = load_dense(m, {&L.q, &L.k, &L.v}, false, &w.qkv16, "qkv")) return e;
+    if (char *e = load_dense(m, {&L.o}, false, &w.o16, "o")) return e;
+    if (char *e = load_dense(m, {&L.router}, true, &w.router16, "router")) return e;
+    // gate rows 2j and up rows 2j + 1 of every expert into GLU tiles, expert after expert
+    std::vector<hc::RowRef> gu;
+    for (uint32_t x = 0; x < E; ++x) {
+      auto r = hc::rows_glu(L.experts_gate_up, x * 2 * I, 2, L.experts_gate_up, x * 2 * I + 1, 2, I);
+      gu.insert(gu.end(), r.begin(), r.end());
+    }
+    w.egu = std::make_unique<hc::DevLinear>();
+    w.edown = std::make_unique<hc::DevLinear>();
+    if (char *e = hc::load_linear(gu, w.egu.get(), nullptr)) return e;
+    w.egu->m.rows = int(E * I);  // the gated unit's outputs
+    if (char *e = hc::load_linear(hc::rows_of(L.experts_down), w.edown.get(), nullptr)) return e;
+    if (char *e = float_vec(m, L.experts_gate_up.bias, size_t(E) * 2 * I, &w.egb)) return e;
+    if (char *e = float_vec(m, L.experts_down.bias, size_t(E) * D, &w.edb)) return e;
+    if (char *e = norm_vec(m, L.input_norm, D, &w.in_norm)) return e;
+    if (char *e = norm_vec(m, L.post_norm, D, &w.post_norm)) return e;
+    if (L.sinks) {
+      std::vector<uint16_t> s16(d.heads);
+      for (uint32_t h = 0; h < d.heads; ++h) s16[h] = f16_bits(L.sinks[h]);
+      if (char *e = norm_vec(m, s16.data(), d.heads, &w.sinks)) return e;
+    }
+    w.window = int(L.sliding_window);
+    expert_bytes = (w.egu->bytes + w.edown->bytes) / E;
+    m->weight_bytes += (uint64_t(w.qkv16.rows) + w.o16.rows + w.router16.rows) * D * 2 + K * expert_bytes;
+    m->layers.push_back(std::move(w));
+  }
+  if (char *e = norm_vec(m, d.final_norm, D, &m->final_norm)) return e;
+  if (char *e = check_shape(d.head, d.vocab, D, "head")) return e;
+  if (char *e = load_dense(m, {&d.head}, false, &m->head16, "head")) return e;
+  m->weight_bytes += uint64_t(d.vocab) * D * 2 + uint64_t(D) * 2;
+  void *p = nullptr;
+  const size_t n = size_t(d.vocab) * D * 2;
+  if (char *e = hc::dev_alloc(&p, n, "embedding table")) return e;
+  m->allocs.push_back(p);
+  if (char *e = hc::copy_h2d(p, d.embed, n, nullptr)) return e;
+  HC_TRY_CUDA(cudaStreamSynchronize(nullptr));
+  m->embed = static_cast<uint16_t *>(p);
+  yarn(d, m->inv_freq, m->rope_factor);
+  return nullptr;
+}
+
 }  // namespace
 
 extern "C" {
@@ -104,7 +277,7 @@ HC_API char *hc_model_load(hc_device *dev, const hc_model_desc *desc, hc_model *
   *out = nullptr;
   const hc_model_desc &d = *desc;
   if (d.abi != HC_ABI) return hc::make_error("hc_model_load: descriptor of ABI " + std::to_string(d.abi));
-  if (d.arch != HC_ARCH_QWEN3)
+  if (d.arch != HC_ARCH_QWEN3 && d.arch != HC_ARCH_GPTOSS)
     return hc::make_error("hc_model_load: architecture " + std::to_string(d.arch) + " is not supported by this build");
   if (!d.layers || !d.hidden || !d.heads || !d.kv_heads || !d.vocab || !d.layer)
     return hc::make_error("hc_model_load: empty shape");
@@ -129,6 +302,11 @@ HC_API char *hc_model_load(hc_device *dev, const hc_model_desc *desc, hc_model *
   m->norm_mid = scaled ? hc::NormCfg{64.f, eps16_of(d.norm_eps, 64)} : m->norm_in0;
   m->norm_head = m->norm_mid;
   m->score_scale = f16_value(f16_bits(float(1 / std::sqrt(double(hd)))));
+  if (d.arch == HC_ARCH_GPTOSS) {
+    if (char *e = load_gptoss(m.get(), d)) return e;
+    *out = m.release();
+    return nullptr;
+  }
   for (uint32_t i = 0; i < d.layers; ++i) {
     const hc_layer_desc &L = d.layer[i];
     const std::string p = "layer " + std::to_string(i) + " ";

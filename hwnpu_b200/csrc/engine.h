@@ -33,6 +33,11 @@ struct LayerW {
   float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
   float *sinks = nullptr;  // fp16-rounded sink logits, or nullptr
   int window = 0;
+  // gpt-oss: 16-bit-float attention and router, the experts' MXFP4 tiles (gate/up as GLU tiles of
+  // each expert's even and odd rows, down) and their float32 biases
+  DevDense qkv16, o16, router16;
+  std::unique_ptr<DevLinear> egu, edown;
+  float *egb = nullptr, *edb = nullptr;
 };
 
 // Norm settings of one RMS norm: the scale of qwen3's normScaled and its fp16 epsilon.
@@ -50,6 +55,8 @@ struct hc_model {
   float *final_norm = nullptr;
   std::unique_ptr<hc::DevLinear> head;
   uint16_t *embed = nullptr;  // fp16 [vocab][hidden], or nullptr when tied
+  bool gptoss = false;
+  hc::DevDense head16;        // gpt-oss's bf16 head
   std::vector<double> inv_freq;
   float rope_factor = 1.f;
   hc::NormCfg norm_in0, norm_mid, norm_head;
@@ -84,6 +91,12 @@ struct hc_session {
   float *x = nullptr, *qkv = nullptr, *q = nullptr, *h = nullptr;
   uint8_t *act = nullptr;
   float *part_ml = nullptr, *part_o = nullptr;
+  // gpt-oss: normed rows (moe_x), the attention output, router logits, the routing (indices and
+  // weights [tokens][top_k]), each expert's pairs, the pairs' activation tiles, gated rows and outputs
+  float *xn = nullptr, *oatt = nullptr, *mlog = nullptr, *mw = nullptr, *hh = nullptr, *ey = nullptr;
+  int32_t *midx = nullptr;
+  int *mcnt = nullptr, *mlist = nullptr;
+  uint8_t *act2 = nullptr;
   hc::StepTok *toks_dev = nullptr, *toks_host = nullptr;
   uint16_t *logits_dev = nullptr;
   unsigned long long *amax = nullptr;

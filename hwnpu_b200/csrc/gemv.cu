@@ -525,8 +525,8 @@ void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cud
 }
 
 void act_quant(const float *x, int ldx, int n, int ntok, const float *norm_w, float scale,
-               float eps16, uint8_t *act, int ktiles, cudaStream_t st, const StepTok *rows) {
-  const int nb = act_tn_blocks(ntok);
+               float eps16, uint8_t *act, int ktiles, cudaStream_t st, const StepTok *rows, bool token_major) {
+  const int nb = token_major ? 0 : act_tn_blocks(ntok);
   launch_pdl(act_quant_kernel, dim3(ktiles, nb ? 8 * nb : ntok), dim3(256), 0, st, x, ldx, n, norm_w, scale, eps16,
              act, ktiles, ntok, nb, rows);
 }

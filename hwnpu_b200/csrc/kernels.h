@@ -4,6 +4,7 @@
 
 #include "common.h"
 
+#include <algorithm>
 #include <utility>
 
 namespace hc {
@@ -76,9 +77,11 @@ inline int act_tn_blocks(int ntok) { return ntok > 8 ? (ntok + 7) / 8 : 0; }
 // token rows, padding included), after an optional RMS norm: when norm_w is set,
 // x is normed as qwen3's normScaled with scale (1 or 64) and epsilon eps16 (the fp16 constant
 // f16(eps / scale^2)) and multiplied by norm_w (float32 values of fp16 weights).
-// With rows set, token t's input is row rows[t].head_src of x (the head's rows of a chunk).
+// With rows set, token t's input is row rows[t].head_src of x (the head's rows of a chunk);
+// token_major: the token-major layout at any ntok (the expert GEMVs read rows by pair).
 void act_quant(const float *x, int ldx, int n, int ntok, const float *norm_w, float scale,
-               float eps16, uint8_t *act, int ktiles, cudaStream_t st, const StepTok *rows = nullptr);
+               float eps16, uint8_t *act, int ktiles, cudaStream_t st, const StepTok *rows = nullptr,
+               bool token_major = false);
 
 // Attention partials -> merged o (float32 [ntok][heads*hd]) -> activation tiles of the output
 // projection (Flash-Decoding's merge with gpt-oss's sinks, paged.go:252-310); batched_layout: the
@@ -130,6 +133,36 @@ void embed(const StepTok *toks, int ntok, const uint16_t *table, const DevMat *h
 
 // Reads the greedy choice out of amax keys.
 void amax_to_index(const unsigned long long *amax, int ntok, int32_t *out, cudaStream_t st);
+
+// ---- gpt-oss (moe.cu) -------------------------------------------------------------------------
+// A dense matrix of 16-bit floats on the device: bf16 (the checkpoint's attention and head) or fp16
+// (the router, whose weights gpt-oss's programs hold as fp16), row-major [rows][cols], cols a
+// multiple of 8; float32 biases or null.
+struct DevDense {
+  const uint16_t *w = nullptr;
+  int rows = 0, cols = 0;
+  bool bf16 = true;
+  const float *bias = nullptr;
+};
+
+// RMS norm (scale 1) of ntok rows of x into float32 y, rounded to fp16 when round16; with rows set,
+// row t of y is row rows[t].head_src of x.
+void rms_rows(const float *x, int ldx, int n, int ntok, const float *w, float eps16, float *y, int ldy, bool round16,
+              cudaStream_t st, const StepTok *rows = nullptr);
+// y = x W^T (+ bias) of ntok float32 rows; mode 0 store, 1 add into y, 2 store rounded to fp16,
+// 3 fp16 logits (stride ldy) and greedy keys into amax.
+void gemv16(const DevDense &W, const float *x, int ldx, int ntok, int mode, float *y, int ldy, uint16_t *logits,
+            unsigned long long *amax, cudaStream_t st);
+// The pairs (token, k) of each expert from the routing's idx ([npairs]): cnt[E], list[E][maxp].
+void moe_group(const int32_t *idx, int npairs, int E, int *cnt, int *list, int maxp, cudaStream_t st);
+// The experts' MXFP4 GEMV grouped by expert (W: all experts' tiles, experts row blocks of equal
+// size): mode 0 gate/up (GLU tiles) + bias through gpt-oss's gated unit into out[pair][inter],
+// act = the tokens' activation tiles; mode 1 down into out[pair][hidden], act = the pairs' tiles.
+void moe_gemv(const DevMat &W, int experts, int mode, const int *cnt, const int *list, int maxp, int K,
+              const uint8_t *act, const float *bias, float alpha, float limit, float *out, int ldo, cudaStream_t st);
+// x[t] = f16(x[t]) + f16(sum over token t's experts in ascending number of w (y + down bias)).
+void moe_combine(const float *y, const int32_t *idx, const float *w, int K, const float *dbias, int H, int ntok,
+                 float *x, cudaStream_t st);
 
 // Float32 values of rows [row0, row0+nrows) of a repacked matrix (the format's arithmetic).
 void dequant(const DevMat &W, int row0, int nrows, float *out, cudaStream_t st);

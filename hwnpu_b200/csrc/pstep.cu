@@ -173,7 +173,7 @@ __device__ __forceinline__ bool grid_sync(const PsParams &p, int &epoch) {
   if (threadIdx.x == 0 && !s_abort) {
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
     asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
-    const unsigned target = unsigned(epoch) * gridDim.x;
+    const unsigned target = unsigned(epoch) * gridDim.x + (epoch == 1 ? unsigned(p.stall_first_barrier) : 0u);
     const long long t0 = clock64();
     int polls = 0;
     while (ld_acquire_u32(p.bar) < target) {

@@ -51,6 +51,8 @@ struct PsParams {
   unsigned *bar;                        // grid barrier counter (zeroed before each launch)
   int *status;                          // 0, or the phase + 1 of the wait that gave up
   long long spin_limit;                 // clock cycles any wait may take before it gives up
+  int stall_first_barrier;              // 1: the first grid barrier waits for one arrival more than
+                                        // the grid has, so it runs out (the failure tests)
   unsigned long long *trace;            // null, or [phases][3] global-timer ns of CTA 0: inputs ready,
                                         // work done, barrier passed
   int stages, stage_bytes;              // the ring

@@ -30,6 +30,9 @@ hc_session::~hc_session() {
                   (void *)act, (void *)part_ml, (void *)part_o, (void *)toks_dev, (void *)logits_dev,
                   (void *)amax, (void *)am_dev, (void *)res_dev})
     if (p) cudaFree(p);
+  for (void *p : {(void *)xn, (void *)oatt, (void *)mlog, (void *)mw, (void *)hh, (void *)ey, (void *)midx,
+                  (void *)mcnt, (void *)mlist, (void *)act2})
+    if (p) cudaFree(p);
   if (toks_host) cudaFreeHost(toks_host);
   if (am_host) cudaFreeHost(am_host);
   if (res_host) cudaFreeHost(res_host);
@@ -180,6 +183,70 @@ int enqueue_chunk(hc_session *s, int n, bool accept, int splits, int heads) {
   return k;
 }
 
+// The gpt-oss step of a chunk (gptoss/build.go's attention part and moeHead, then
+// experts.Host.runRow, experts/host.go:478-591, for every row): per layer the RMS norm, the bf16
+// q|k|v projection and its biases, RoPE with YaRN's tables, attention over the cache with the
+// layer's window and sinks, the bf16 o projection into the residual; then the post-attention norm
+// rounded to fp16 (moe_x), the fp16 router's logits (rounded to fp16), the top-k routing, the
+// token-grouped MXFP4 experts and their weighted sum, which ends the layer as x = f16(x) + f16(moe).
+// Same contract as enqueue_chunk.
+int enqueue_chunk_gptoss(hc_session *s, int n, bool accept, int splits, int heads) {
+  hc_model *m = s->m;
+  const auto &d = m->d;
+  const int D = int(d.hidden), I = int(d.inter), H = int(d.heads), KV = int(d.kv_heads);
+  const int hd = int(d.head_dim), V = int(d.vocab), E = int(d.experts), K = int(d.top_k);
+  const int W = (H + 2 * KV) * hd;
+  const int ktD = (D + hc::kTileCols - 1) / hc::kTileCols, ktI = (I + hc::kTileCols - 1) / hc::kTileCols;
+  const int ktO = (H * hd + hc::kTileCols - 1) / hc::kTileCols;
+  const int maxp = kMaxChunk * K, c8 = (n + 7) / 8;
+  const float alpha = float(d.swiglu_alpha), limit = float(d.swiglu_limit), eps = m->norm_in0.eps16;
+  cudaStream_t st = s->st;
+  int k = 0;
+  hc::embed(s->toks_dev, n, m->embed, nullptr, D, s->x, s->amax, st);
+  ++k;
+  for (size_t li = 0; li < m->layers.size(); ++li) {
+    const hc::LayerW &w = m->layers[li];
+    uint16_t *kcl = s->paged ? nullptr : s->kc + li * s->layer_kv;
+    uint16_t *vcl = s->paged ? nullptr : s->vc + li * s->layer_kv;
+    const hc::PagedKV pk = s->paged ? paged_of(s, li) : hc::PagedKV{};
+    const hc::AttnGeom g = geom(s, w.window);
+    hc::rms_rows(s->x, D, D, n, w.in_norm, eps, s->xn, D, false, st);
+    hc::gemv16(w.qkv16, s->xn, D, n, 0, s->qkv, W, nullptr, nullptr, st);
+    hc::qkv_post(s->qkv, s->toks_dev, n, g, nullptr, nullptr, 1.f, eps, s->rope, s->q, kcl, vcl, s->kv_stage, st);
+    if (s->paged) {
+      hc::kv_append_int8(s->kv_stage, s->toks_dev, n, KV, hd, pk, st);
+      ++k;
+    }
+    hc::attn_split(s->q, s->toks_dev, n, g, kcl, vcl, splits, s->part_ml, s->part_o, st, s->paged ? &pk : nullptr);
+    hc::attn_merge_quant(s->part_ml, s->part_o, w.sinks, n, H, hd, splits, s->act, ktO, s->oatt, st, false);
+    hc::gemv16(w.o16, s->oatt, H * hd, n, 1, s->x, D, nullptr, nullptr, st);
+    hc::rms_rows(s->x, D, D, n, w.post_norm, eps, s->xn, D, true, st);
+    hc::gemv16(w.router16, s->xn, D, n, 2, s->mlog, E, nullptr, nullptr, st);
+    hc::route(s->mlog, n, E, K, s->midx, s->mw, st);
+    hc::moe_group(s->midx, n * K, E, s->mcnt, s->mlist, maxp, st);
+    hc::act_quant(s->xn, D, D, n, nullptr, 1.f, 0.f, s->act, ktD, st, nullptr, true);
+    hc::moe_gemv(w.egu->m, E, 0, s->mcnt, s->mlist, maxp, K, s->act, w.egb, alpha, limit, s->hh, I, st);
+    hc::act_quant(s->hh, I, I, n * K, nullptr, 1.f, 0.f, s->act2, ktI, st, nullptr, true);
+    hc::moe_gemv(w.edown->m, E, 1, s->mcnt, s->mlist, maxp, K, s->act2, nullptr, 0.f, 0.f, s->ey, D, st);
+    hc::moe_combine(s->ey, s->midx, s->mw, K, w.edb, D, n, s->x, st);
+    k += 11 + 3 * c8;
+  }
+  if (heads > 0) {
+    hc::rms_rows(s->x, D, D, heads, m->final_norm, m->norm_head.eps16, s->xn, D, false, st,
+                 heads == n ? nullptr : s->toks_dev);
+    hc::gemv16(m->head16, s->xn, D, heads, 3, nullptr, V, s->logits_dev, s->amax, st);
+    hc::amax_to_index(s->amax, heads, s->am_dev, st);
+    k += 2 + (heads + 7) / 8;
+  }
+  if (accept) { hc::spec_accept(s->am_dev, s->toks_dev, n, s->res_dev, st); ++k; }
+  return k;
+}
+
+// The model's kernel sequence for a chunk.
+int enqueue_model(hc_session *s, int n, bool accept, int splits, int heads) {
+  return s->m->gptoss ? enqueue_chunk_gptoss(s, n, accept, splits, heads) : enqueue_chunk(s, n, accept, splits, heads);
+}
+
 constexpr long long kSpinLimit = 4000000000ll;  // ~2 s of SM clocks: a wait of the persistent step
 
 // The persistent step's parameters for the n tokens in toks_dev; gen: hc_generate's feedback.
@@ -235,6 +302,7 @@ hc::PsParams ps_params(hc_session *s, int n, bool gen, long long spin) {
   p.bar = s->ps_sync;
   p.status = s->ps_status;
   p.spin_limit = spin;
+  p.stall_first_barrier = spin != kSpinLimit ? 1 : 0;
   p.trace = s->ps_trace;
   hc::ps_layout(p, s->ps_kind);
   return p;
@@ -272,7 +340,7 @@ char *run_chunk(hc_session *s, int n, bool accept, int heads) {
       cudaMemcpyAsync(s->ps_status_host, s->ps_status, sizeof(int), cudaMemcpyDeviceToHost, st);
       cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
     } else {
-      k = enqueue_chunk(s, n, accept, splits, heads);
+      k = enqueue_model(s, n, accept, splits, heads);
       if (heads > 0) cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * heads, cudaMemcpyDeviceToHost, st);
     }
     if (accept) cudaMemcpyAsync(s->res_host, s->res_dev, sizeof(int32_t) * 2, cudaMemcpyDeviceToHost, st);
@@ -457,10 +525,27 @@ HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session
   if (char *e = hc::copy_h2d(s->rope, rope.data(), rope.size() * 4, nullptr)) return e;
   HC_TRY_CUDA(cudaStreamSynchronize(nullptr));
   int ktiles = 0;
-  for (auto &w : m->layers)
-    ktiles = std::max({ktiles, w.qkv->m.ktiles, w.o->m.ktiles, w.gu->m.ktiles, w.down->m.ktiles});
-  ktiles = std::max(ktiles, m->head->m.ktiles);
+  if (m->gptoss) {
+    ktiles = (std::max({D, F, H * hd}) + hc::kTileCols - 1) / hc::kTileCols;
+  } else {
+    for (auto &w : m->layers)
+      ktiles = std::max({ktiles, w.qkv->m.ktiles, w.o->m.ktiles, w.gu->m.ktiles, w.down->m.ktiles});
+    ktiles = std::max(ktiles, m->head->m.ktiles);
+  }
   const int T = kMaxChunk;
+  if (m->gptoss) {
+    const int E = int(d.experts), K = int(d.top_k), ktI = (F + hc::kTileCols - 1) / hc::kTileCols;
+    if (char *e = alloc(&s->xn, size_t(T) * D, "normed rows")) return e;
+    if (char *e = alloc(&s->oatt, size_t(T) * H * hd, "attention output")) return e;
+    if (char *e = alloc(&s->mlog, size_t(T) * E, "router logits")) return e;
+    if (char *e = alloc(&s->midx, size_t(T) * K, "routing")) return e;
+    if (char *e = alloc(&s->mw, size_t(T) * K, "routing weights")) return e;
+    if (char *e = alloc(&s->mcnt, size_t(E), "expert counts")) return e;
+    if (char *e = alloc(&s->mlist, size_t(E) * T * K, "expert lists")) return e;
+    if (char *e = alloc(&s->act2, size_t(T) * K * ktI * hc::kActTile, "expert activation tiles")) return e;
+    if (char *e = alloc(&s->hh, size_t(T) * K * F, "expert activations")) return e;
+    if (char *e = alloc(&s->ey, size_t(T) * K * D, "expert outputs")) return e;
+  }
   if (char *e = alloc(&s->x, size_t(T) * D, "hidden states")) return e;
   if (char *e = alloc(&s->qkv, size_t(T) * (H + 2 * KV) * hd, "qkv")) return e;
   if (s->paged)
@@ -623,7 +708,7 @@ HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, i
       // return at once (they see it set)
       s->launches_per_chunk[0] = uint64_t(enqueue_ps(s, 1, true, kSpinLimit));
     } else {
-      s->launches_per_chunk[0] = uint64_t(enqueue_chunk(s, 1, false, splits_for(s, 1, 0), 1)) + 1;
+      s->launches_per_chunk[0] = uint64_t(enqueue_model(s, 1, false, splits_for(s, 1, 0), 1)) + 1;
       hc::advance(s->toks_dev, s->am_dev, s->gen_out, s->gen_count, st);
     }
     cudaError_t e = cudaStreamEndCapture(st, &graph);

@@ -323,10 +323,11 @@ HC_API char *hc_profile_get(hc_session *s, double *us, uint32_t cap, uint32_t *n
  * "step:N" the N-th hc_step, each with an error string; "stall:MS" (MS <= 2000) makes the next
  * hc_step, hc_speculate or hc_generate first wait MS milliseconds on the device, so that a shorter
  * timeout_ms runs out (HC_STATE_TIMEOUT, the sequences poisoned until hc_seq_reset); "spin:N" gives
- * every wait of the next persistent step (grid barriers, ring stages) a limit of N clock cycles, so
- * that a small N makes them give up and the call return the step's error; "" clears. Nothing faults
- * or hangs on the GPU: the stall is a bounded wait on the global timer, and a persistent step whose
- * wait gave up lets its copies land and returns. */
+ * every wait of the next persistent step (grid barriers, ring stages) a limit of N clock cycles and
+ * makes its first grid barrier wait for one arrival more than the grid has, so that the barrier runs
+ * out and the call returns the step's error; "" clears. Nothing faults or hangs on the GPU: the
+ * stall is a bounded wait on the global timer, and a persistent step whose wait gave up lets its
+ * copies land and returns. */
 HC_API char *hc_set_fault(const char *spec);
 
 /* ---------------------------------------------------------------------------------------- */

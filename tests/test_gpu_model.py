@@ -133,15 +133,16 @@ def test_persistent_batch_of_four(device, models):
 
 
 def test_persistent_wait_limit_returns_an_error(device, models):
-    # the persistent step's bounded waits: "spin:1" gives every grid barrier and ring stage of the
-    # next step a limit of one clock cycle, so they give up; the step lets its copies land and
-    # returns, the call reports the error, and after hc_seq_reset the session decodes as a fresh one
+    # the persistent step's bounded waits: "spin:2000000" gives every wait of the next step a limit
+    # of about 1 ms and makes its first grid barrier wait for an arrival that never comes; the
+    # barrier runs out, the step lets its copies land and returns, the call reports the error, and
+    # after hc_seq_reset the session decodes as a fresh one
     model = get(models, C2_2L)
     lm = device.load_model(model)
     s = lm.session(max_context=64, persistent=True)
     fresh = lm.session(max_context=64, persistent=True)
     toks = list(synth.tokens(5, C2_2L.vocab, 4))  # a chunk the persistent step takes
-    A.check(A.lib().hc_set_fault(b"spin:1"))
+    A.check(A.lib().hc_set_fault(b"spin:2000000"))
     with pytest.raises(hb.HcError, match="timed out"):
         s.step_tokens(toks)
     with pytest.raises(hb.HcError, match="reset"):

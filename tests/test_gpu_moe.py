@@ -1,0 +1,153 @@
+"""gpt-oss (C3's architecture) on a B200 through the C ABI against the CPU oracle on identical seeded
+weights: bf16 attention with biases, YaRN rotary tables, sinks and alternating sliding windows,
+the fp16 router and softmax top-k routing, the MXFP4 experts with gpt-oss's gated unit, and the
+ascending-expert combine (experts.Host.runRow, internal/llm/experts/host.go:478-591). Logits
+within max-abs 2e-2 and cosine >= 0.9999, greedy tokens identical wherever the oracle's top-2
+margin exceeds the tolerance; one sequence and a batch of 16 in one step."""
+
+from dataclasses import replace
+
+import numpy as np
+import pytest
+
+import oracle_lib as O
+from hwnpu_b200 import _abi as A
+from hwnpu_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+
+# gpt-oss shapes small enough for quick oracle runs: a window of 8 crossed by the prompts
+TINY = synth.Config("tiny-gptoss", 2, 256, 256, 4, 2, 64, 500, A.HC_FMT_MXFP4, norm_scale=False,
+                    rope_theta=150000.0, norm_eps=1e-5, arch="gptoss", experts=8, top_k=2, window=8,
+                    attn_fmt=A.HC_FMT_BF16, yarn=(32.0, 32.0, 1.0, 4096, False))
+# C3's layer shapes (2880 hidden, 64/8 heads of 64, 32 experts of 2880, top 4, window 128) on 2
+# layers and an 8,192-id vocabulary (the full vocabulary only widens the head)
+C3_2L = replace(synth.C3, name="c3-2layers", layers=2, vocab=8192)
+
+
+def cosine(a, b):
+    a, b = a.astype(np.float64), b.astype(np.float64)
+    return float(a @ b / np.sqrt((a @ a) * (b @ b)))
+
+
+def compare(got, want):
+    err = np.abs(got - want).max()
+    assert err <= TOL, err
+    assert cosine(got, want) >= 0.9999
+
+
+def top2_margin(v):
+    s = np.sort(v)
+    return float(s[-1] - s[-2])
+
+
+@pytest.fixture(scope="module")
+def models():
+    return {}
+
+
+def get(models, cfg, seed=0):
+    if cfg.name not in models:
+        models[cfg.name] = synth.Model(cfg, seed=seed, norm_std=0.1)
+    return models[cfg.name]
+
+
+@pytest.mark.parametrize("cfg,prompt,steps", [(TINY, 13, 8), (C3_2L, 150, 4)], ids=lambda v: getattr(v, "name", str(v)))
+def test_gptoss_decode_matches_oracle(device, models, cfg, prompt, steps):
+    # one sequence: a prompt read in one step (past the sliding window), then greedy decode steps
+    model = get(models, cfg)
+    lm = device.load_model(model)
+    sess = lm.session(max_context=prompt + steps + 4)
+    ref = O.OracleSession(model, prompt + steps + 4)
+    toks = list(synth.tokens(31, cfg.vocab, prompt))
+    got = sess.step_tokens(toks)
+    want = synth.f16_values(ref.step(toks)[0])
+    compare(got, want)
+    for _ in range(steps):
+        if top2_margin(want) > 2 * TOL:
+            assert int(np.argmax(got)) == int(np.argmax(want))
+        t = int(np.argmax(want))
+        got = sess.step_tokens([t])
+        want = synth.f16_values(ref.step([t])[0])
+        compare(got, want)
+    assert sess.pos() == ref.pos() == prompt + steps
+    sess.close()
+    lm.close()
+    ref.close()
+
+
+@pytest.mark.parametrize("cfg", [TINY, C3_2L], ids=lambda v: v.name)
+def test_gptoss_batch16_matches_oracle(device, models, cfg):
+    # 16 sequences of ragged prompts (3 to 78 ids) decode together: every row of the
+    # batched step (its experts grouped over all 16 tokens) against its own oracle session
+    model = get(models, cfg)
+    lm = device.load_model(model)
+    lens = [3 + 5 * i for i in range(16)]
+    cap = max(lens) + 8
+    sess = lm.session(max_context=cap, max_seqs=16, max_step=max(lens))
+    first = O.OracleSession(model, cap)
+    refs = [first] + [O.OracleSession(model, cap, share=first) for _ in lens[1:]]
+    nxt = []
+    for i, n in enumerate(lens):
+        prompt = list(synth.tokens(50 + i, cfg.vocab, n))
+        lg, _ = sess.step_batch([i], [prompt])
+        want = synth.f16_values(refs[i].step(prompt)[0])
+        compare(synth.f16_values(lg[0]), want)
+        nxt.append(int(np.argmax(want)))
+    for _ in range(3):
+        lg, am = sess.step_batch(list(range(16)), [[t] for t in nxt])
+        for i in range(16):
+            want = synth.f16_values(refs[i].step([nxt[i]])[0])
+            compare(synth.f16_values(lg[i]), want)
+            if top2_margin(want) > 2 * TOL:
+                assert int(am[i]) == int(np.argmax(want))
+            nxt[i] = int(np.argmax(want))
+    for r in refs[1:]:
+        r.close()
+    first.close()
+    sess.close()
+    lm.close()
+
+
+def test_gptoss_generate_and_speculate_equal_steps(device, models):
+    # hc_generate (the device-side feedback loop) and hc_speculate (a verify chunk) against plain
+    # one-token steps of the same model: identical tokens
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    prompt = list(synth.tokens(77, TINY.vocab, 10))
+    a = lm.session(max_context=64)
+    b = lm.session(max_context=64)
+    c = lm.session(max_context=64)
+    first = int(np.argmax(a.step_tokens(prompt)))
+    b.step_tokens(prompt)
+    c.step_tokens(prompt)
+    steps = [first]
+    for _ in range(12):
+        steps.append(int(np.argmax(a.step_tokens([steps[-1]]))))
+    gen = b.generate(first, 12)
+    assert list(gen) == steps[1:]
+    kept, nx, _ = c.speculate_tokens(steps[:8])
+    assert kept == 8 and nx == steps[8]
+    for s in (a, b, c):
+        s.close()
+    lm.close()
+
+
+def test_gptoss_paged_matches_oracle(device, models):
+    # the paged int8 cache under gpt-oss's windows and sinks, against the oracle's paged mode
+    model = get(models, TINY)
+    lm = device.load_model(model)
+    sess = lm.session(max_context=64, kv_format=A.HC_KV_INT8_PAGED, page_size=16)
+    ref = O.OracleSession(model, 64, kv_format=A.HC_KV_INT8_PAGED)
+    toks = list(synth.tokens(8, TINY.vocab, 20))
+    compare(sess.step_tokens(toks), synth.f16_values(ref.step(toks)[0]))
+    t = int(toks[-1])
+    for _ in range(6):
+        want = synth.f16_values(ref.step([t])[0])
+        compare(sess.step_tokens([t]), want)
+        t = int(np.argmax(want))
+    sess.close()
+    ref.close()
+    lm.close()
