@@ -323,13 +323,13 @@ def kernel_roofline(dev, lin, ntok, label, profile_name, reps=50):
             "ms_per_launch": ms, "tokens": ntok}
 
 
-def run_bs1(args, lm, model, dev, world, dist, K, W, persistent):
+def run_bs1(args, lm, model, dev, world, dist, K, W):
     """C2 bs1 on this rank: the device-resident loop (value) and the public per-token call (e2e)."""
     import torch
 
     from hwnpu_b200 import replicas, synth
 
-    sess = lm.session(max_context=PROMPT + PASS + W + 8, max_step=8, persistent=persistent)
+    sess = lm.session(max_context=PROMPT + PASS + W + 8, max_step=8)
     prompt = synth.tokens(1, model.cfg.vocab, PROMPT)
     first = sess.greedy(prompt)
     base = sess.pos()
@@ -379,7 +379,7 @@ def run_bs1(args, lm, model, dev, world, dist, K, W, persistent):
     return {"value": world * K / (t_max / 1e3), "unit": "tokens/s", "ms_per_step": t_max / K, "steps": K,
             "e2e": {"value": world * E / (t_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * world,
                     "d2h_bytes_per_step": 4 * world, "api": "hc_step per token (token in, greedy choice out)"},
-            "gpu_launches": int(launches), "path": "persistent step" if persistent else "kernel sequence",
+            "gpu_launches": int(launches), "path": "kernel sequence (CUDA graph, PDL-chained)",
             "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": bytes_tok * per_gpu / 1e9,
                               "frac": bytes_tok * per_gpu / 1e9 / peak, "peak": peak, "peak_kind": peak_kind,
                               "ideal_tokens_per_s": peak * 1e9 / bytes_tok},
@@ -484,7 +484,7 @@ def run_default(args, rank, world, local, dist):
     clocks.start()
     c5 = run_c5(args, lm, world, rank, dist, K, W)
     clk = clocks.stop()
-    bs1 = run_bs1(args, lm, model, dev, world, dist, K, W, args.persistent)
+    bs1 = run_bs1(args, lm, model, dev, world, dist, K, W)
     # the dominant kernel class of the C5 step: the batched GEMV (64 tokens on the MMA's n), on the
     # largest matrix of a layer (gate/up, 12288 x 2048)
     gu = hb.synth.Linear.quantize(hb.synth.normal(5, "bench.gate_up", 12288 * 2048, 0.02).reshape(12288, 2048),
@@ -534,7 +534,7 @@ def run_bs1_line(args, rank, world, local, dist, workload):
     lm = dev.load_model(model)
     clocks = Clocks(local)
     clocks.start()
-    r = run_bs1(args, lm, model, dev, world, dist, K, W, args.persistent)
+    r = run_bs1(args, lm, model, dev, world, dist, K, W)
     clk = clocks.stop()
     lm.close()
     dev.close()
@@ -845,10 +845,6 @@ def main():
     ap.add_argument("--cols", type=int, default=2048, help="--workload linear: matrix columns")
     ap.add_argument("--ntok", type=int, default=64, help="--workload linear: tokens a call")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--persistent", action="store_true",
-                    help="run bs1 decode steps as the persistent one-launch step instead of the kernel sequence")
-    ap.add_argument("--phases", action="store_true",
-                    help="print the persistent step's per-phase timing (hc_profile_get) of C2 bs1 and exit")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -858,9 +854,6 @@ def main():
         return
     if args.workload == "linear":
         run_linear(args, local)
-        return
-    if args.phases:
-        run_phases(args, local)
         return
 
     import torch
@@ -884,36 +877,6 @@ def main():
     if dist:
         dist.barrier()
         dist.destroy_process_group()
-
-
-def run_phases(args, local):
-    import torch
-
-    import hwnpu_b200 as hb
-    from hwnpu_b200 import synth
-
-    torch.cuda.set_device(local)
-    dev = hb.Device(local)
-    model = hb.Model(hb.C2, seed=0)
-    lm = dev.load_model(model)
-    sess = lm.session(max_context=PROMPT + 64, profile=True, persistent=True)
-    first = sess.greedy(synth.tokens(1, model.cfg.vocab, PROMPT))
-    sess.generate(first, 4)
-    acc = 0
-    units = 0
-    for _ in range(8):
-        sess.generate(first, 1)
-        acc = acc + sess.profile()
-        units = units + sess.last_units
-    acc /= 8
-    units /= 8
-    L = model.cfg.layers
-    names = ["qkv", "attention", "o", "gate/up", "down"]
-    per = {n: [round(float(x), 3) for x in acc[i:5 * L:5].mean(axis=0)] for i, n in enumerate(names)}
-    print(json.dumps({"phase_us_per_layer_inputs_work_barrier_stagewait": per, "head": acc[5 * L].tolist(),
-                      "total_us": float(acc[:, :3].sum()),
-                      "merging_unit_us_inputs_stages_partial_ticket_merge":
-                          [round(float(x), 3) for x in units[:, :5].mean(axis=0)]}), flush=True)
 
 
 if __name__ == "__main__":

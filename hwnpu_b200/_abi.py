@@ -21,7 +21,7 @@ HC_FMT_INT8_ROW, HC_FMT_INT4_SYM_G32, HC_FMT_INT4_ASYM_G32, HC_FMT_MXFP4 = 2, 3,
 HC_ARCH_QWEN3, HC_ARCH_GPTOSS = 1, 2
 HC_MODEL_QK_NORM, HC_MODEL_TIED, HC_MODEL_NORM_SCALE, HC_MODEL_ATTN_BIAS = 1, 2, 4, 8
 HC_KV_F16, HC_KV_INT8_PAGED = 0, 1
-HC_SESSION_NO_GRAPH, HC_SESSION_PERSISTENT, HC_SESSION_PROFILE = 1, 2, 4
+HC_SESSION_NO_GRAPH = 1
 HC_STEP_ALL_ROWS = 1
 
 _p = C.c_void_p
@@ -101,7 +101,6 @@ SIGNATURES = {
     "hc_seq_import_rows": (_err, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                                   C.c_uint64]),
     "hc_stats_get": (_err, [C.c_void_p, C.POINTER(Stats)]),
-    "hc_profile_get": (_err, [C.c_void_p, C.POINTER(C.c_double), C.c_uint32, C.POINTER(C.c_uint32)]),
     "hc_set_fault": (_err, [C.c_char_p]),
     "hc_synth_normal": (_err, [C.c_uint64, C.c_char_p, _f32p, _f32p, C.c_uint64]),
     "hc_synth_tokens": (_err, [C.c_uint64, C.c_int32, _i32p, C.c_uint64]),
@@ -118,6 +117,7 @@ SIGNATURES = {
     "hc_attention_run": (_err, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                 C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                 C.c_int32, _f32p, C.c_void_p]),
+    "hc_device_check": (_err, [C.c_void_p]),
     "hc_attention_run_static": (_err, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                        C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                        C.c_int32, _f32p, C.c_void_p]),

@@ -7,7 +7,7 @@
 #include <string>
 #include <vector>
 
-#include "common.h"
+#include "kernels.h"
 
 namespace hc {
 
@@ -31,10 +31,8 @@ std::atomic<long> g_stall_ms{0};  // "stall:MS": the next step first waits MS ms
 long take_stall_ms() { return g_stall_ms.exchange(0); }
 
 namespace {
-std::atomic<long long> g_spin_cycles{0};  // "spin:N": the next persistent step's waits give up after N cycles
 }  // namespace
 
-long long take_spin_cycles() { return g_spin_cycles.exchange(0); }
 
 bool fault_fires(FaultPoint p) {
   std::lock_guard<std::mutex> g(g_fault_mu);
@@ -126,10 +124,6 @@ HC_API char *hc_set_fault(const char *spec) {
   std::string point = s.substr(0, colon);
   long n = std::strtol(s.c_str() + colon + 1, nullptr, 10);
   if (n < 1) return hc::make_error("hc_set_fault: N must be at least 1");
-  if (point == "spin") {
-    hc::g_spin_cycles = n;
-    return nullptr;
-  }
   if (point == "stall") {
     if (n > 2000) return hc::make_error("hc_set_fault: a stall is at most 2000 ms");
     hc::g_stall_ms = n;
@@ -202,6 +196,15 @@ HC_API char *hc_device_info(hc_device *d, int key, char *buf, size_t n, size_t *
     std::memcpy(buf, v.data(), k);
     buf[k] = 0;
   }
+  return nullptr;
+}
+
+HC_API char *hc_device_check(hc_device *d) {
+  if (!d) return hc::make_error("hc_device_check: NULL device");
+  HC_TRY_CUDA(cudaSetDevice(d->ordinal));
+  HC_TRY_CUDA(cudaDeviceSynchronize());
+  const int code = hc::tc_status_take();
+  if (code) return hc::make_error("a tensor-core GEMV wait ran out (code " + std::to_string(code) + ")");
   return nullptr;
 }
 

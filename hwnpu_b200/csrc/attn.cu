@@ -77,17 +77,15 @@ __global__ void __launch_bounds__(128) qkv_post_kernel(const float *__restrict__
       return;
     }
     const float *vs = qkv + size_t(t) * width + size_t(g.heads + g.kv_heads + kvh) * hd;
-    if (!kcache) {
-      // paged int8 cache: the rows go to kv_append_int8 in float32 ([t][k|v][kv head][hd])
-      float *kd = kv_stage + ((size_t(t) * 2) * g.kv_heads + kvh) * hd;
-      float *vd = kd + size_t(g.kv_heads) * hd;
+    // the stage rows ([t][k|v][kv head][hd] float32): the chunk's attention and kv_append_int8
+    float *kd = kv_stage + ((size_t(t) * 2) * g.kv_heads + kvh) * hd;
+    float *vd = kd + size_t(g.kv_heads) * hd;
 #pragma unroll
-      for (int k = 0; k < E; ++k) {
-        kd[lane + 32 * k] = y[k];
-        vd[lane + 32 * k] = vs[lane + 32 * k];
-      }
-      return;
+    for (int k = 0; k < E; ++k) {
+      kd[lane + 32 * k] = y[k];
+      vd[lane + 32 * k] = vs[lane + 32 * k];
     }
+    if (!kcache) return;
     const size_t row = ((size_t(tk.slot) * g.kv_heads + kvh) * g.cap + tk.pos) * hd;
 #pragma unroll
     for (int k = 0; k < E; ++k) {
@@ -109,7 +107,8 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
                                                          const uint16_t *__restrict__ vcache,
                                                          PagedKV pk,
                                                          int splits, float *__restrict__ part_ml,
-                                                         float *__restrict__ part_o) {
+                                                         float *__restrict__ part_o,
+                                                         const float *__restrict__ kv_stage) {
   pdl_trigger();
   pdl_wait();
   constexpr int E = HD / 8;  // elements a lane: 16 (hd 128) or 8 (hd 64)
@@ -124,6 +123,9 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
   const int n = P - lo + 1;
   const int chunk = (n + splits - 1) / splits;
   const int k0 = lo + s * chunk, k1 = min(P + 1, k0 + chunk);
+  // positions from p0 on are this token's piece: float32 stage rows (row t - (P - j) for key j)
+  const int p0 = tk.run0 >= 0 ? P - (t - tk.run0) : P + 1;
+  const int kc1 = min(k1, max(k0, p0));  // cached keys [k0, kc1), stage keys [kc1, k1)
   float qv[REP][E];
 #pragma unroll
   for (int r = 0; r < REP; ++r) {
@@ -158,7 +160,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
 #pragma unroll
     for (int i = 0; i < KW; ++i) r.k[i] = r.v[i] = 0u;
     r.ks = r.vs = 0.f;
-    if (j >= k1) return;
+    if (j >= kc1) return;
     const uint32_t *kp, *vp;
     if (PAGED) {
       // key j of the sequence: row j % 16 of its page, int8 times the (page, head) scale
@@ -190,29 +192,8 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
       }
     }
   };
-  Raw cur;
-  fetch(k0 + grp, cur);
-  for (int j0 = k0; j0 < k1; j0 += 16) {
-    const int j = j0 + grp;
-    const bool valid = j < k1;
-    Raw nxt;
-    fetch(j + 16, nxt);
-    float kf[E], vf[E];
-    if (PAGED) {
-#pragma unroll
-      for (int i = 0; i < E; ++i) {
-        kf[i] = float(int8_t((cur.k[i / 4] >> (8 * (i % 4))) & 0xff)) * cur.ks;
-        vf[i] = float(int8_t((cur.v[i / 4] >> (8 * (i % 4))) & 0xff)) * cur.vs;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < E / 2; ++i) {
-        const __half2 k2 = *reinterpret_cast<const __half2 *>(&cur.k[i]);
-        const __half2 v2 = *reinterpret_cast<const __half2 *>(&cur.v[i]);
-        kf[2 * i] = __low2float(k2); kf[2 * i + 1] = __high2float(k2);
-        vf[2 * i] = __low2float(v2); vf[2 * i + 1] = __high2float(v2);
-      }
-    }
+  // one key of the online softmax for every query head of the group
+  auto step = [&](const float (&kf)[E], const float (&vf)[E], bool valid) {
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
       float d = 0.f;
@@ -231,7 +212,52 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
         m[r] = mn;
       }
     }
+  };
+  Raw cur;
+  fetch(k0 + grp, cur);
+  for (int j0 = k0; j0 < kc1; j0 += 16) {
+    const int j = j0 + grp;
+    const bool valid = j < kc1;
+    Raw nxt;
+    fetch(j + 16, nxt);
+    float kf[E], vf[E];
+    if (PAGED) {
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        kf[i] = float(int8_t((cur.k[i / 4] >> (8 * (i % 4))) & 0xff)) * cur.ks;
+        vf[i] = float(int8_t((cur.v[i / 4] >> (8 * (i % 4))) & 0xff)) * cur.vs;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < E / 2; ++i) {
+        const __half2 k2 = *reinterpret_cast<const __half2 *>(&cur.k[i]);
+        const __half2 v2 = *reinterpret_cast<const __half2 *>(&cur.v[i]);
+        kf[2 * i] = __low2float(k2); kf[2 * i + 1] = __high2float(k2);
+        vf[2 * i] = __low2float(v2); vf[2 * i + 1] = __high2float(v2);
+      }
+    }
+    step(kf, vf, valid);
     cur = nxt;
+  }
+  // the piece's own keys and values, float32 from the stage rows
+  for (int j0 = kc1; j0 < k1; j0 += 16) {
+    const int j = j0 + grp;
+    const bool valid = j < k1;
+    float kf[E], vf[E];
+#pragma unroll
+    for (int k = 0; k < E; ++k) kf[k] = vf[k] = 0.f;
+    if (valid) {
+      const float4 *kp = reinterpret_cast<const float4 *>(
+          kv_stage + ((size_t(t - (P - j)) * 2) * g.kv_heads + kvh) * HD + l8 * E);
+      const float4 *vp = kp + size_t(g.kv_heads) * HD / 4;
+#pragma unroll
+      for (int k = 0; k < E / 4; ++k) {
+        const float4 a = kp[k], b = vp[k];
+        kf[4 * k] = a.x; kf[4 * k + 1] = a.y; kf[4 * k + 2] = a.z; kf[4 * k + 3] = a.w;
+        vf[4 * k] = b.x; vf[4 * k + 1] = b.y; vf[4 * k + 2] = b.z; vf[4 * k + 3] = b.w;
+      }
+    }
+    step(kf, vf, valid);
   }
   // merge the 4 groups of the warp (lanes differing in bits 3 and 4)
 #pragma unroll
@@ -300,7 +326,7 @@ void qkv_post(const float *qkv, const StepTok *toks, int ntok, const AttnGeom &g
 
 void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g,
                 const uint16_t *kcache, const uint16_t *vcache, int splits, float *part_ml,
-                float *part_o, cudaStream_t st, const PagedKV *paged) {
+                float *part_o, cudaStream_t st, const PagedKV *paged, const float *kv_stage) {
   dim3 grid(splits, g.kv_heads, ntok);
   const int rep = g.heads / g.kv_heads;
   const PagedKV pk = paged ? *paged : PagedKV{};
@@ -308,10 +334,10 @@ void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g
   if (g.hd == D && rep == R) {                                                                \
     if (paged)                                                                                \
       launch_pdl(attn_split_kernel<D, R, true>, grid, dim3(128), 0, st, q, toks, g, kcache,   \
-                 vcache, pk, splits, part_ml, part_o);                                        \
+                 vcache, pk, splits, part_ml, part_o, kv_stage);                              \
     else                                                                                      \
       launch_pdl(attn_split_kernel<D, R, false>, grid, dim3(128), 0, st, q, toks, g, kcache,  \
-                 vcache, pk, splits, part_ml, part_o);                                        \
+                 vcache, pk, splits, part_ml, part_o, kv_stage);                              \
     return;                                                                                   \
   }
   HC_ATT(128, 1) HC_ATT(128, 2) HC_ATT(128, 4) HC_ATT(128, 8)

@@ -109,8 +109,6 @@ enum FaultPoint { kFaultAlloc = 0, kFaultH2D = 1, kFaultStep = 2 };
 bool fault_fires(FaultPoint p);
 // The armed device stall in milliseconds (hc_set_fault "stall:MS"), cleared by the call; 0: none.
 long take_stall_ms();
-// The armed wait limit of the next persistent step in clock cycles ("spin:N"), cleared; 0: none.
-long long take_spin_cycles();
 
 // cudaMalloc that honours the alloc fault and returns an error string.
 char *dev_alloc(void **p, size_t n, const char *what);

@@ -65,6 +65,16 @@ __device__ __forceinline__ uint32_t e2m1x4(uint32_t w, uint32_t wsh, uint32_t si
   return (pos & ~m) | (neg & m);
 }
 
+// Byte offset of token t's value of column k in the tensor-core GEMV's fp16 operand (kActF16,
+// npad rows): per column tile npad x 512 bytes; in it per 16 columns (one MMA's K) npad x 32 bytes
+// of core matrices, 8 tokens x 16 bytes each, the two 8-column halves 128 bytes apart, the 8-token
+// groups 256 bytes apart (tcgemm.cu's descriptors: LBO 128, SBO 256).
+__device__ __forceinline__ size_t f16op_offset(int t, int k, int npad) {
+  const int cc = k & (kTileCols - 1);
+  return size_t(k / kTileCols) * npad * (kTileCols * 2) + (cc >> 4) * (npad * 32) + (t >> 3) * 256 +
+         ((cc >> 3) & 1) * 128 + (t & 7) * 16 + (cc & 7) * 2;
+}
+
 // fp16 bits as a key whose unsigned order is the value order (-0 as +0), for argmax.
 __device__ __forceinline__ uint32_t f16_order(uint16_t h) {
   if (h == 0x8000) h = 0;

@@ -7,7 +7,6 @@
 #include <vector>
 
 #include "kernels.h"
-#include "pstep.h"
 #include "repack.h"
 
 namespace hc {
@@ -97,22 +96,15 @@ struct hc_session {
   int32_t *midx = nullptr;
   int *mcnt = nullptr, *mlist = nullptr;
   uint8_t *act2 = nullptr;
+  float *tc_ws = nullptr;  // the tensor-core GEMV's split-K partials and tickets
+  int *tc_tickets = nullptr;
+  size_t tc_ws_floats = 0;
   hc::StepTok *toks_dev = nullptr, *toks_host = nullptr;
   uint16_t *logits_dev = nullptr;
   unsigned long long *amax = nullptr;
   int32_t *am_dev = nullptr, *am_host = nullptr, *res_dev = nullptr, *res_host = nullptr;
   int32_t *gen_out = nullptr, *gen_count = nullptr;  // hc_generate's tokens [cap] and counter
   cudaGraphExec_t gen_graph = nullptr;
-  // the persistent step (pstep.h), when the model and the device have one
-  bool ps = false;
-  int ps_ctas = 0, ps_kind = 0, ps_max_splits = 0, ps_max_tok = 0;
-  hc::PsLayer *ps_layers = nullptr;     // device [layers]
-  unsigned *ps_sync = nullptr;          // [0]: the grid barrier, from [4]: the merge and head tickets
-  size_t ps_sync_bytes = 0;
-  int *ps_status = nullptr, *ps_status_host = nullptr;
-  float *ps_attn = nullptr, *ps_part_ml = nullptr, *ps_part_o = nullptr, *ps_dx = nullptr;
-  unsigned long long *ps_trace = nullptr;  // HC_SESSION_PROFILE: CTA 0's barrier times
-  bool chunk_ps = false;                // the last chunk ran as the persistent step
   // captured step graphs by (tokens, accept kernel)
   std::map<int, cudaGraphExec_t> graphs;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;

@@ -380,14 +380,20 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const float *__restrict_
                                                         int n, const float *__restrict__ norm_w,
                                                         float scale, float eps16,
                                                         uint8_t *__restrict__ act, int ktiles,
-                                                        int ntok, int nb, const StepTok *__restrict__ rows) {
+                                                        int ntok, int nb, const StepTok *__restrict__ rows,
+                                                        int f16pad) {
   __shared__ double red[32];
   pdl_trigger();
   pdl_wait();
   const int t = blockIdx.y, kt = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (t >= ntok) {  // padding of the batched layout (uniform over the CTA)
-    quant_group_tn(0.f, act, kt, warp, t, nb, lane);
+  if (t >= ntok) {  // padding of the batched layouts (uniform over the CTA)
+    if (f16pad) {
+      const int col = (kt * kGroupsPerTile + warp) * kGroup + lane;
+      *reinterpret_cast<__half *>(act + f16op_offset(t, col, f16pad)) = __float2half_rn(0.f);
+    } else {
+      quant_group_tn(0.f, act, kt, warp, t, nb, lane);
+    }
     return;
   }
   const float *xt = x + size_t(rows ? rows[t].head_src : t) * ldx;
@@ -414,7 +420,8 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const float *__restrict_
       v = y * norm_w[col];
     }
   }
-  if (nb) quant_group_tn(v, act, kt, warp, t, nb, lane);
+  if (f16pad) *reinterpret_cast<__half *>(act + f16op_offset(t, col, f16pad)) = __float2half_rn(v);
+  else if (nb) quant_group_tn(v, act, kt, warp, t, nb, lane);
   else quant_group(v, act + (size_t(t) * ktiles + kt) * kActTile, warp, lane);
 }
 
@@ -426,7 +433,7 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict
                                                          const float *__restrict__ sinks,
                                                          int heads, int hd, int splits,
                                                          uint8_t *__restrict__ act, int ktiles,
-                                                         int nb, float *__restrict__ o_out) {
+                                                         int nb, float *__restrict__ o_out, int f16pad) {
   __shared__ float wsh[64];
   __shared__ float stat[2];
   pdl_trigger();
@@ -474,7 +481,8 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict
     // one warp a group of 32: warp w of this head holds columns h*hd + 32w .. + 31
     const int gcol = h * hd + d;
     const int grp = gcol / kGroup;
-    if (nb) quant_group_tn(o, act, grp / kGroupsPerTile, grp % kGroupsPerTile, t, nb, lane);
+    if (f16pad) *reinterpret_cast<__half *>(act + f16op_offset(t, gcol, f16pad)) = __float2half_rn(o);
+    else if (nb) quant_group_tn(o, act, grp / kGroupsPerTile, grp % kGroupsPerTile, t, nb, lane);
     else quant_group(o, act + (size_t(t) * ktiles + grp / kGroupsPerTile) * kActTile, grp % kGroupsPerTile, lane);
   }
 }
@@ -490,6 +498,10 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ tiles, const float *_
   }
 }
 
+}  // namespace
+
+namespace {
+int g_sms[64];  // SMs of each device (gemv_prepare)
 }  // namespace
 
 char *gemv_prepare() {
@@ -509,11 +521,19 @@ char *gemv_prepare() {
   HC_SET_K(kKindInt8) HC_SET_K(kKindInt4) HC_SET_K(kKindMx)
 #undef HC_SET_K
 #undef HC_SET
+  if (char *e = tc_gemm_prepare()) return e;
+  HC_TRY_CUDA(cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev));
   done[dev] = true;
   return nullptr;
 }
 
 void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cudaStream_t st) {
+  if (act_layout(W, ntok) == kActF16) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    tc_gemm(W, act, ntok, out, g_sms[dev & 63] ? g_sms[dev & 63] : 148, st);
+    return;
+  }
   const int wpr = W.ktiles >= 8 ? 8 : (W.ktiles >= 4 ? 4 : (W.ktiles >= 2 ? 2 : 1));
   const int rpc = 8 / wpr;
   const int grid = (W.rtiles + rpc - 1) / rpc;
@@ -525,26 +545,30 @@ void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cud
 }
 
 void act_quant(const float *x, int ldx, int n, int ntok, const float *norm_w, float scale,
-               float eps16, uint8_t *act, int ktiles, cudaStream_t st, const StepTok *rows, bool token_major) {
-  const int nb = token_major ? 0 : act_tn_blocks(ntok);
-  launch_pdl(act_quant_kernel, dim3(ktiles, nb ? 8 * nb : ntok), dim3(256), 0, st, x, ldx, n, norm_w, scale, eps16,
-             act, ktiles, ntok, nb, rows);
+               float eps16, uint8_t *act, int ktiles, cudaStream_t st, const StepTok *rows, ActLayout layout) {
+  const int f16pad = layout == kActF16 ? tc_npad(ntok) : 0;
+  const int nb = layout == kActAuto ? act_tn_blocks(ntok) : 0;
+  launch_pdl(act_quant_kernel, dim3(ktiles, f16pad ? f16pad : (nb ? 8 * nb : ntok)), dim3(256), 0, st, x, ldx, n,
+             norm_w, scale, eps16, act, ktiles, ntok, nb, rows, f16pad);
 }
 
 void attn_merge_quant(const float *part_ml, const float *part_o, const float *sinks, int ntok,
                       int heads, int hd, int splits, uint8_t *act, int ktiles, float *o_out,
-                      cudaStream_t st, bool batched_layout) {
-  const int nb = batched_layout ? act_tn_blocks(ntok) : 0;
+                      cudaStream_t st, ActLayout layout) {
+  const int nb = layout == kActAuto ? act_tn_blocks(ntok) : 0;
+  const int f16pad = layout == kActF16 ? tc_npad(ntok) : 0;
   // columns past heads*hd in the last tile are zero groups; so are the padding tokens of a batch
   const int n = heads * hd;
-  if (nb) {
+  if (f16pad) {
+    cudaMemsetAsync(act, 0, size_t(ktiles) * f16pad * kTileCols * 2, st);
+  } else if (nb) {
     cudaMemsetAsync(act, 0, size_t(ktiles) * kGroupsPerTile * nb * kActTile, st);
   } else if (n % kTileCols) {
     for (int t = 0; t < ntok; ++t)
       cudaMemsetAsync(act + (size_t(t) * ktiles + ktiles - 1) * kActTile, 0, kActTile, st);
   }
   launch_pdl(attn_merge_kernel, dim3(heads, ntok), dim3(hd), 0, st, part_ml, part_o, sinks, heads, hd, splits, act,
-             ktiles, nb, o_out);
+             ktiles, nb, o_out, f16pad);
 }
 
 void dequant(const DevMat &W, int row0, int nrows, float *out, cudaStream_t st) {

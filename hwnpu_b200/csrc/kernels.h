@@ -51,15 +51,40 @@ struct GemvOut {
   int ldy = 0;
   uint16_t *logits = nullptr;           // kLogits: [t][ldy] fp16 bits, or nullptr
   unsigned long long *amax = nullptr;   // kLogits: [t], see argmax_key in misc.cu
+  // the tensor-core GEMV's split-K partials (ws_floats floats) and its per-row-tile tickets (zeroed
+  // once; each launch leaves them zero), or null: no split
+  float *ws = nullptr;
+  int *tickets = nullptr;
+  size_t ws_floats = 0;
 };
+
+// The activation operand a GEMV of ntok tokens reads (act_quant, attn_merge_quant):
+//  kActAuto        int8 hi/lo tiles, token-major up to 8 tokens, the batched layout above (the
+//                  MMA-sync GEMV kernels)
+//  kActTokenMajor  int8 hi/lo tiles, token-major at any count (the expert GEMVs)
+//  kActF16         fp16 values in the tensor-core GEMV's operand layout (tcgemm.cu): per column tile
+//                  npad x 256 values, npad = ntok rounded up to 16, padding rows zero
+enum ActLayout : int { kActAuto = 0, kActTokenMajor = 1, kActF16 = 2 };
+// The layout gemv() reads for W at ntok tokens: 9..64 tokens of int8 / int4 go to the tensor cores.
+inline ActLayout act_layout(const DevMat &W, int ntok) {
+  return ntok > 8 && W.kind != kKindMx ? kActF16 : kActAuto;
+}
+inline int tc_npad(int ntok) { return (ntok + 15) / 16 * 16; }
 
 // Sets, once a device (call it with the device current, outside stream capture), the shared
 // memory the batched GEMV asks for; hc_session_new and hc_linear_load call it.
 char *gemv_prepare();
 
-// y = x W^T for ntok (1..64) tokens whose activations act_quant wrote into act: up to 8 tokens a
-// token per MMA column group (gemv_kernel), 9..64 tokens on the MMA's n (gemm_tn_kernel).
+// y = x W^T for ntok (1..64) tokens whose activations act_quant wrote into act (in the layout
+// act_layout(W, ntok) names): up to 8 tokens a token per MMA column group (gemv_kernel); 9..64
+// tokens on the tensor cores (tc_gemm, int8 and int4) or on the MMA's n (gemm_tn_kernel, MXFP4).
 void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cudaStream_t st);
+// The tensor-core GEMV (tcgemm.cu) of 9..64 tokens: xop in kActF16 layout; sms: the device's SMs.
+void tc_gemm(const DevMat &W, const uint8_t *xop, int ntok, const GemvOut &out, int sms, cudaStream_t st);
+char *tc_gemm_prepare();
+// The error code of the first tensor-core GEMV wait that ran out on the current device since the
+// last call (0: none), cleared.
+int tc_status_take();
 
 // Per-token position data of a step, in device memory so that a captured graph replays it.
 struct StepTok {
@@ -67,6 +92,10 @@ struct StepTok {
   int32_t slot;   // sequence slot
   int32_t pos;    // position of this token
   int32_t head_src;  // entry j < the chunk's head rows: the chunk token whose logits are row j
+  // the chunk index of the first token of this token's piece (its sequence's consecutive tokens
+  // in the chunk): the keys and values of the piece's positions are read in float32 from the
+  // chunk's stage rows, the earlier ones from the cache; -1: every key from the cache
+  int32_t run0 = -1;
 };
 
 // Blocks of 8 tokens of the batched activation layout that 9..64 tokens take (0: token-major).
@@ -78,17 +107,16 @@ inline int act_tn_blocks(int ntok) { return ntok > 8 ? (ntok + 7) / 8 : 0; }
 // x is normed as qwen3's normScaled with scale (1 or 64) and epsilon eps16 (the fp16 constant
 // f16(eps / scale^2)) and multiplied by norm_w (float32 values of fp16 weights).
 // With rows set, token t's input is row rows[t].head_src of x (the head's rows of a chunk);
-// token_major: the token-major layout at any ntok (the expert GEMVs read rows by pair).
+// layout: see ActLayout (the normed values are the same in all three).
 void act_quant(const float *x, int ldx, int n, int ntok, const float *norm_w, float scale,
                float eps16, uint8_t *act, int ktiles, cudaStream_t st, const StepTok *rows = nullptr,
-               bool token_major = false);
+               ActLayout layout = kActAuto);
 
-// Attention partials -> merged o (float32 [ntok][heads*hd]) -> activation tiles of the output
-// projection (Flash-Decoding's merge with gpt-oss's sinks, paged.go:252-310); batched_layout: the
-// tiles as act_quant lays out ntok tokens for the GEMV (else token-major, ntok tiles a k-tile).
+// Attention partials -> merged o (float32 [ntok][heads*hd]) -> activation operand of the output
+// projection in the given layout (Flash-Decoding's merge with gpt-oss's sinks, paged.go:252-310).
 void attn_merge_quant(const float *part_ml, const float *part_o, const float *sinks, int ntok,
                       int heads, int hd, int splits, uint8_t *act, int ktiles, float *o_out,
-                      cudaStream_t st, bool batched_layout = false);
+                      cudaStream_t st, ActLayout layout = kActTokenMajor);
 
 
 struct AttnGeom {
@@ -111,20 +139,24 @@ struct PagedKV {
   int max_pages = 0;
 };
 
+// Every token's rotated key and its value also go to kv_stage ([ntok][2][kv_heads][hd] float32),
+// where the attention of the chunk reads its own pieces' keys (StepTok::run0); with kcache NULL (the
+// paged int8 cache) nothing else is written, and kv_append_int8 quantises the rows into the pages
+// after the chunk's attention.
 void qkv_post(const float *qkv, const StepTok *toks, int ntok, const AttnGeom &g,
               const float *qn, const float *kn, float norm_scale, float eps16,
               const uint32_t *rope, float *q_out, uint16_t *kcache, uint16_t *vcache,
               float *kv_stage, cudaStream_t st);
-// With kcache NULL (the paged int8 cache) qkv_post leaves the new rows in kv_stage
-// ([ntok][2][kv_heads][hd] float32) and kv_append_int8 quantises them into the pages.
 void kv_append_int8(const float *stage, const StepTok *toks, int ntok, int kv_heads, int hd, const PagedKV &pk,
                     cudaStream_t st);
 
 // Split-K decode attention over the fp16 cache: token t attends keys [lo, pos] of its slot
-// (lo = pos - window + 1 with a window); `splits` partials of (m, l) and unnormalised o.
+// (lo = pos - window + 1 with a window); `splits` partials of (m, l) and unnormalised o. The keys of
+// a token's own piece come from kv_stage (float32, as qkv_post wrote them), the others from the cache.
 void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g,
                 const uint16_t *kcache, const uint16_t *vcache, int splits, float *part_ml,
-                float *part_o, cudaStream_t st, const PagedKV *paged = nullptr);
+                float *part_o, cudaStream_t st, const PagedKV *paged = nullptr,
+                const float *kv_stage = nullptr);
 
 // Embedding rows of the step's tokens into x (float32 [ntok][hidden]): from an fp16 table, or
 // (table nullptr) from the tied head's tiles, dequantised and rounded to fp16. Also resets amax.

@@ -19,16 +19,14 @@ hc_session::~hc_session() {
   for (auto &g : graphs) cudaGraphExecDestroy(g.second);
   if (gen_graph) cudaGraphExecDestroy(gen_graph);
   if (gen_out) cudaFree(gen_out);
-  for (void *p : {(void *)ps_layers, (void *)ps_sync, (void *)ps_status, (void *)ps_trace, (void *)ps_attn,
-                  (void *)ps_part_ml, (void *)ps_part_o, (void *)ps_dx})
-    if (p) cudaFree(p);
-  if (ps_status_host) cudaFreeHost(ps_status_host);
   if (gen_count) cudaFree(gen_count);
   for (void *p : {(void *)kp, (void *)vp, (void *)kps, (void *)vps, (void *)btab_dev, (void *)kv_stage})
     if (p) cudaFree(p);
   for (void *p : {(void *)kc, (void *)vc, (void *)rope, (void *)x, (void *)qkv, (void *)q, (void *)h,
                   (void *)act, (void *)part_ml, (void *)part_o, (void *)toks_dev, (void *)logits_dev,
                   (void *)amax, (void *)am_dev, (void *)res_dev})
+    if (p) cudaFree(p);
+  for (void *p : {(void *)tc_ws, (void *)tc_tickets})
     if (p) cudaFree(p);
   for (void *p : {(void *)xn, (void *)oatt, (void *)mlog, (void *)mw, (void *)hh, (void *)ey, (void *)midx,
                   (void *)mcnt, (void *)mlist, (void *)act2})
@@ -44,6 +42,7 @@ hc_session::~hc_session() {
 namespace {
 
 constexpr int kMaxSplits = 64;
+constexpr int kTcTickets = 4096;  // row tiles of 128 rows a tensor-core GEMV may have (524,288 rows)
 constexpr int kSplitKeys = 1024;  // keys a split reads, at most, for the chunk's longest context
 
 // Attention splits of every (token, kv head) of a chunk of n tokens whose longest context is
@@ -127,6 +126,15 @@ void release_pages(hc_session *s, int seq, int len) {
     }
 }
 
+// The output settings every GEMV of a session shares: its split-K workspace.
+hc::GemvOut gemv_out(const hc_session *s) {
+  hc::GemvOut o;
+  o.ws = s->tc_ws;
+  o.tickets = s->tc_tickets;
+  o.ws_floats = s->tc_ws_floats;
+  return o;
+}
+
 // Enqueues one chunk of n tokens (already in toks_dev) on the session's stream; returns the
 // number of kernels launched. Only `heads` rows go through the final norm and the head: row j is
 // chunk token toks[j].head_src (the rows a caller reads; none for the inside of a long prompt).
@@ -147,33 +155,38 @@ int enqueue_chunk(hc_session *s, int n, bool accept, int splits, int heads) {
     uint16_t *vcl = s->paged ? nullptr : s->vc + li * s->layer_kv;
     const hc::PagedKV pk = s->paged ? paged_of(s, li) : hc::PagedKV{};
     const hc::AttnGeom g = geom(s, w.window);
-    hc::act_quant(s->x, D, D, n, w.in_norm, nc.scale, nc.eps16, s->act, w.qkv->m.ktiles, st);
-    hc::GemvOut o1;
+    hc::act_quant(s->x, D, D, n, w.in_norm, nc.scale, nc.eps16, s->act, w.qkv->m.ktiles, st, nullptr,
+                  hc::act_layout(w.qkv->m, n));
+    hc::GemvOut o1 = gemv_out(s);
     o1.mode = hc::kStore; o1.y = s->qkv; o1.ldy = W;
     hc::gemv(w.qkv->m, s->act, n, o1, st);
     hc::qkv_post(s->qkv, s->toks_dev, n, g, w.q_norm, w.k_norm, m->norm_mid.scale, m->norm_mid.eps16,
                  s->rope, s->q, kcl, vcl, s->kv_stage, st);
-    if (s->paged) {
+    hc::attn_split(s->q, s->toks_dev, n, g, kcl, vcl, splits, s->part_ml, s->part_o, st, s->paged ? &pk : nullptr,
+                   s->kv_stage);
+    if (s->paged) {  // the chunk's rows into the pages once its attention has read the earlier ones
       hc::kv_append_int8(s->kv_stage, s->toks_dev, n, KV, hd, pk, st);
       ++k;
     }
-    hc::attn_split(s->q, s->toks_dev, n, g, kcl, vcl, splits, s->part_ml, s->part_o, st, s->paged ? &pk : nullptr);
-    hc::attn_merge_quant(s->part_ml, s->part_o, w.sinks, n, H, hd, splits, s->act, w.o->m.ktiles, nullptr, st, true);
-    hc::GemvOut o2;
+    hc::attn_merge_quant(s->part_ml, s->part_o, w.sinks, n, H, hd, splits, s->act, w.o->m.ktiles, nullptr, st,
+                         hc::act_layout(w.o->m, n));
+    hc::GemvOut o2 = gemv_out(s);
     o2.mode = hc::kAdd; o2.y = s->x; o2.ldy = D;
     hc::gemv(w.o->m, s->act, n, o2, st);
-    hc::act_quant(s->x, D, D, n, w.post_norm, m->norm_mid.scale, m->norm_mid.eps16, s->act, w.gu->m.ktiles, st);
-    hc::GemvOut o3;
+    hc::act_quant(s->x, D, D, n, w.post_norm, m->norm_mid.scale, m->norm_mid.eps16, s->act, w.gu->m.ktiles, st,
+                  nullptr, hc::act_layout(w.gu->m, n));
+    hc::GemvOut o3 = gemv_out(s);
     o3.mode = hc::kGlu; o3.y = s->h; o3.ldy = F;
     hc::gemv(w.gu->m, s->act, n, o3, st);
-    hc::act_quant(s->h, F, F, n, nullptr, 1.f, 0.f, s->act, w.down->m.ktiles, st);
+    hc::act_quant(s->h, F, F, n, nullptr, 1.f, 0.f, s->act, w.down->m.ktiles, st, nullptr,
+                  hc::act_layout(w.down->m, n));
     hc::gemv(w.down->m, s->act, n, o2, st);
     k += 10;
   }
   if (heads > 0) {
     hc::act_quant(s->x, D, D, heads, m->final_norm, m->norm_head.scale, m->norm_head.eps16, s->act,
-                  m->head->m.ktiles, st, heads == n ? nullptr : s->toks_dev);
-    hc::GemvOut oh;
+                  m->head->m.ktiles, st, heads == n ? nullptr : s->toks_dev, hc::act_layout(m->head->m, heads));
+    hc::GemvOut oh = gemv_out(s);
     oh.mode = hc::kLogits; oh.ldy = V; oh.logits = s->logits_dev; oh.amax = s->amax;
     hc::gemv(m->head->m, s->act, heads, oh, st);
     hc::amax_to_index(s->amax, heads, s->am_dev, st);
@@ -213,20 +226,21 @@ int enqueue_chunk_gptoss(hc_session *s, int n, bool accept, int splits, int head
     hc::rms_rows(s->x, D, D, n, w.in_norm, eps, s->xn, D, false, st);
     hc::gemv16(w.qkv16, s->xn, D, n, 0, s->qkv, W, nullptr, nullptr, st);
     hc::qkv_post(s->qkv, s->toks_dev, n, g, nullptr, nullptr, 1.f, eps, s->rope, s->q, kcl, vcl, s->kv_stage, st);
+    hc::attn_split(s->q, s->toks_dev, n, g, kcl, vcl, splits, s->part_ml, s->part_o, st, s->paged ? &pk : nullptr,
+                   s->kv_stage);
     if (s->paged) {
       hc::kv_append_int8(s->kv_stage, s->toks_dev, n, KV, hd, pk, st);
       ++k;
     }
-    hc::attn_split(s->q, s->toks_dev, n, g, kcl, vcl, splits, s->part_ml, s->part_o, st, s->paged ? &pk : nullptr);
-    hc::attn_merge_quant(s->part_ml, s->part_o, w.sinks, n, H, hd, splits, s->act, ktO, s->oatt, st, false);
+    hc::attn_merge_quant(s->part_ml, s->part_o, w.sinks, n, H, hd, splits, s->act, ktO, s->oatt, st);
     hc::gemv16(w.o16, s->oatt, H * hd, n, 1, s->x, D, nullptr, nullptr, st);
     hc::rms_rows(s->x, D, D, n, w.post_norm, eps, s->xn, D, true, st);
     hc::gemv16(w.router16, s->xn, D, n, 2, s->mlog, E, nullptr, nullptr, st);
     hc::route(s->mlog, n, E, K, s->midx, s->mw, st);
     hc::moe_group(s->midx, n * K, E, s->mcnt, s->mlist, maxp, st);
-    hc::act_quant(s->xn, D, D, n, nullptr, 1.f, 0.f, s->act, ktD, st, nullptr, true);
+    hc::act_quant(s->xn, D, D, n, nullptr, 1.f, 0.f, s->act, ktD, st, nullptr, hc::kActTokenMajor);
     hc::moe_gemv(w.egu->m, E, 0, s->mcnt, s->mlist, maxp, K, s->act, w.egb, alpha, limit, s->hh, I, st);
-    hc::act_quant(s->hh, I, I, n * K, nullptr, 1.f, 0.f, s->act2, ktI, st, nullptr, true);
+    hc::act_quant(s->hh, I, I, n * K, nullptr, 1.f, 0.f, s->act2, ktI, st, nullptr, hc::kActTokenMajor);
     hc::moe_gemv(w.edown->m, E, 1, s->mcnt, s->mlist, maxp, K, s->act2, nullptr, 0.f, 0.f, s->ey, D, st);
     hc::moe_combine(s->ey, s->midx, s->mw, K, w.edb, D, n, s->x, st);
     k += 11 + 3 * c8;
@@ -247,109 +261,22 @@ int enqueue_model(hc_session *s, int n, bool accept, int splits, int heads) {
   return s->m->gptoss ? enqueue_chunk_gptoss(s, n, accept, splits, heads) : enqueue_chunk(s, n, accept, splits, heads);
 }
 
-constexpr long long kSpinLimit = 4000000000ll;  // ~2 s of SM clocks: a wait of the persistent step
-
-// The persistent step's parameters for the n tokens in toks_dev; gen: hc_generate's feedback.
-hc::PsParams ps_params(hc_session *s, int n, bool gen, long long spin) {
-  hc_model *m = s->m;
-  const auto &d = m->d;
-  hc::PsParams p{};
-  p.layers = int(d.layers);
-  p.D = int(d.hidden);
-  p.F = int(d.inter);
-  p.H = int(d.heads);
-  p.KV = int(d.kv_heads);
-  p.hd = int(d.head_dim);
-  p.V = int(d.vocab);
-  p.cap = s->cap;
-  p.ntok = n;
-  p.kt_d = m->layers[0].qkv->m.ktiles;
-  p.kt_f = m->layers[0].down->m.ktiles;
-  p.kt_o = m->layers[0].o->m.ktiles;
-  p.rt_qkv = m->layers[0].qkv->m.rtiles;
-  p.rt_o = m->layers[0].o->m.rtiles;
-  p.rt_gu = m->layers[0].gu->m.rtiles;
-  p.rt_down = m->layers[0].down->m.rtiles;
-  p.rt_head = m->head->m.rtiles;
-  p.max_splits = s->ps_max_splits;
-  p.sc_in0 = m->norm_in0.scale;
-  p.eps_in0 = m->norm_in0.eps16;
-  p.sc = m->norm_mid.scale;
-  p.eps = m->norm_mid.eps16;
-  p.sc_head = m->norm_head.scale;
-  p.eps_head = m->norm_head.eps16;
-  p.score_scale = m->score_scale;
-  p.L = s->ps_layers;
-  p.head = m->head->m.tiles;
-  p.head_scale = m->head->m.row_scale;
-  p.embed = m->embed;
-  p.final_norm = m->final_norm;
-  p.rope = s->rope;
-  p.toks = s->toks_dev;
-  p.dx_o = s->x;
-  p.dx_down = s->ps_dx;
-  p.qkv = s->qkv;
-  p.attn = s->ps_attn;
-  p.h = s->h;
-  p.part_ml = s->ps_part_ml;
-  p.part_o = s->ps_part_o;
-  p.tickets = reinterpret_cast<int *>(s->ps_sync + 4);
-  p.logits = gen ? nullptr : s->logits_dev;
-  p.amax = s->amax;
-  p.am = s->am_dev;
-  p.gen_out = gen ? s->gen_out : nullptr;
-  p.gen_count = gen ? s->gen_count : nullptr;
-  p.bar = s->ps_sync;
-  p.status = s->ps_status;
-  p.spin_limit = spin;
-  p.stall_first_barrier = spin != kSpinLimit ? 1 : 0;
-  p.trace = s->ps_trace;
-  hc::ps_layout(p, s->ps_kind);
-  return p;
-}
-
-// Enqueues the persistent step (its barrier and tickets zeroed first); returns its launches.
-int enqueue_ps(hc_session *s, int n, bool gen, long long spin) {
-  cudaMemsetAsync(s->ps_sync, 0, s->ps_sync_bytes, s->st);
-  hc::ps_launch(ps_params(s, n, gen, spin), s->ps_kind, s->ps_ctas, s->st);
-  return 1;
-}
-
-bool ps_chunk(const hc_session *s, int n) { return s->ps && n <= s->ps_max_tok; }
-
 // The whole chunk: tokens in, greedy choices (and the accept result) out, as one graph. heads:
 // the rows read out (toks_host[j].head_src for j < heads; all n rows for accept).
 char *run_chunk(hc_session *s, int n, bool accept, int heads) {
   for (int i = 0; i < n; ++i)
     if (char *e = ensure_pages(s, s->toks_host[i].slot, s->toks_host[i].pos, s->toks_host[i].pos + 1)) return e;
   cudaStream_t st = s->st;
-  // an armed "spin:N" fault runs this chunk once, outside the graphs, with waits of N cycles
-  const long long spin_fault = hc::take_spin_cycles();
-  const bool ps = ps_chunk(s, n);
-  const bool use_graph = !(s->o.flags & HC_SESSION_NO_GRAPH) && !(ps && spin_fault);
-  const int splits = ps ? 0 : splits_for(s, n, chunk_max_len(s, n));
-  const int key = ((splits * 128 + n) * 128 + heads) * 4 + (accept ? 1 : 0) + (ps ? 2 : 0);
-  s->chunk_ps = ps;
+  const bool use_graph = !(s->o.flags & HC_SESSION_NO_GRAPH);
+  const int splits = splits_for(s, n, chunk_max_len(s, n));
+  const int key = ((splits * 128 + n) * 128 + heads) * 2 + (accept ? 1 : 0);
   auto enqueue_all = [&]() -> int {
     cudaMemcpyAsync(s->toks_dev, s->toks_host, sizeof(hc::StepTok) * n, cudaMemcpyHostToDevice, st);
-    int k = 0;
-    if (ps) {
-      // every row's logits and greedy choice (row t: token t); the host picks the rows it reads
-      k = enqueue_ps(s, n, false, spin_fault ? spin_fault : kSpinLimit);
-      if (accept) { hc::spec_accept(s->am_dev, s->toks_dev, n, s->res_dev, st); ++k; }
-      cudaMemcpyAsync(s->ps_status_host, s->ps_status, sizeof(int), cudaMemcpyDeviceToHost, st);
-      cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, st);
-    } else {
-      k = enqueue_model(s, n, accept, splits, heads);
-      if (heads > 0) cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * heads, cudaMemcpyDeviceToHost, st);
-    }
+    const int k = enqueue_model(s, n, accept, splits, heads);
+    if (heads > 0) cudaMemcpyAsync(s->am_host, s->am_dev, sizeof(int32_t) * heads, cudaMemcpyDeviceToHost, st);
     if (accept) cudaMemcpyAsync(s->res_host, s->res_dev, sizeof(int32_t) * 2, cudaMemcpyDeviceToHost, st);
     return k;
   };
-  if (ps) {
-    *s->ps_status_host = 0;
-    cudaMemsetAsync(s->ps_status, 0, sizeof(int), st);
-  }
   if (use_graph && !s->graphs.count(key)) {
     cudaGraph_t graph = nullptr;
     HC_TRY_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
@@ -371,17 +298,8 @@ char *run_chunk(hc_session *s, int n, bool accept, int heads) {
   }
   HC_TRY_CUDA(cudaGetLastError());
   HC_TRY_CUDA(cudaEventRecord(s->ev1, st));
-  s->stats.launches += use_graph ? s->launches_per_key[key] : s->launches_per_key[key];
+  s->stats.launches += s->launches_per_key[key];
   return nullptr;
-}
-
-// The persistent step's status after a wait: an error string when one of its waits gave up.
-char *ps_status_error(hc_session *s) {
-  if (!s->ps || !*s->ps_status_host) return nullptr;
-  const int c = *s->ps_status_host;
-  std::string what = c < 100000 ? "grid barrier " + std::to_string(c) : c < 200000 ? "ring stage release (producer)"
-                     : c < 300000 ? "weight stage " + std::to_string(c - 200000) : "key stage " + std::to_string(c - 300000);
-  return hc::make_error("step: a device wait timed out (" + what + ")");
 }
 
 // Waits for the last chunk with a deadline (xrtshim.h's xs_run_wait with timeout_ms).
@@ -407,63 +325,6 @@ char *wait_done(hc_session *s, uint32_t timeout_ms, int32_t *state) {
   cudaEventElapsedTime(&ms, s->ev0, s->ev1);
   s->stats.last_step_us = double(ms) * 1000.0;
   if (state) *state = HC_STATE_COMPLETED;
-  return nullptr;
-}
-
-// Sets up the persistent step when the model and the device allow it (a dense model of one integer
-// kind throughout, the fp16 cache, a cooperative launch of one CTA a SM).
-char *ps_setup(hc_session *s) {
-  hc_model *m = s->m;
-  const auto &d = m->d;
-  if (!(s->o.flags & HC_SESSION_PERSISTENT) || s->paged || d.arch != HC_ARCH_QWEN3) return nullptr;
-  const int kind = m->head->m.kind, rep = int(d.heads / d.kv_heads);
-  if (!hc::ps_supported(kind, int(d.head_dim), rep, s->cap)) return nullptr;
-  for (auto &w : m->layers)
-    if (w.qkv->m.kind != kind || w.o->m.kind != kind || w.gu->m.kind != kind || w.down->m.kind != kind ||
-        w.gu->m.bias || w.down->m.bias || w.sinks || w.qkv->m.ktiles != m->layers[0].qkv->m.ktiles)
-      return nullptr;
-  if (m->head->m.ktiles != m->layers[0].qkv->m.ktiles) return nullptr;
-  HC_TRY_CUDA(hc::ps_prepare());
-  s->ps_ctas = hc::ps_ctas(m->ordinal);
-  if (!s->ps_ctas) return nullptr;
-  s->ps_kind = kind;
-  s->ps_max_splits = (s->cap + hc::kPsSplitKeys - 1) / hc::kPsSplitKeys;
-  // the most tokens a launch takes: its residual rows and activation tiles share the SM's shared
-  // memory with a ring of at least 4 stages
-  s->ps_max_tok = 0;
-  for (int n = 1; n <= hc::kPsMaxTok; ++n) {
-    hc::PsParams probe = ps_params(s, n, false, kSpinLimit);
-    if (hc::ps_layout(probe, kind)) s->ps_max_tok = n;
-  }
-  if (!s->ps_max_tok) return nullptr;
-  std::vector<hc::PsLayer> L(d.layers);
-  for (size_t i = 0; i < L.size(); ++i) {
-    const hc::LayerW &w = m->layers[i];
-    L[i] = hc::PsLayer{w.qkv->m.tiles, w.o->m.tiles, w.gu->m.tiles, w.down->m.tiles,
-                       w.qkv->m.row_scale, w.o->m.row_scale, w.gu->m.row_scale, w.down->m.row_scale,
-                       w.qkv->m.bias, w.o->m.bias, w.in_norm, w.post_norm, w.q_norm, w.k_norm, w.sinks,
-                       s->kc + i * s->layer_kv, s->vc + i * s->layer_kv, w.window};
-  }
-  const int T = hc::kPsMaxTok, H = int(d.heads), hd = int(d.head_dim);
-  if (char *e = alloc(&s->ps_layers, L.size(), "step layer table")) return e;
-  HC_TRY_CUDA(cudaMemcpy(s->ps_layers, L.data(), sizeof(hc::PsLayer) * L.size(), cudaMemcpyHostToDevice));
-  s->ps_sync_bytes = sizeof(unsigned) * (4 + size_t(T) * d.kv_heads + 1);
-  if (char *e = alloc(&s->ps_sync, s->ps_sync_bytes / sizeof(unsigned), "grid barrier and tickets")) return e;
-  HC_TRY_CUDA(cudaMemset(s->ps_sync, 0, s->ps_sync_bytes));
-  if (char *e = alloc(&s->ps_status, 1, "step status")) return e;
-  HC_TRY_CUDA(cudaMemset(s->ps_status, 0, sizeof(int)));
-  HC_TRY_CUDA(cudaHostAlloc(&s->ps_status_host, sizeof(int), cudaHostAllocDefault));
-  *s->ps_status_host = 0;
-  if (char *e = alloc(&s->ps_attn, size_t(T) * H * hd, "attention output")) return e;
-  if (char *e = alloc(&s->ps_dx, size_t(T) * d.hidden, "down projection rows")) return e;
-  if (char *e = alloc(&s->ps_part_ml, size_t(T) * H * s->ps_max_splits * 2, "attention partials")) return e;
-  if (char *e = alloc(&s->ps_part_o, size_t(T) * H * s->ps_max_splits * hd, "attention partials")) return e;
-  if (s->o.flags & HC_SESSION_PROFILE) {
-    const size_t n = size_t(4) * hc::ps_phases(int(d.layers)) + size_t(8) * d.layers;
-    if (char *e = alloc(&s->ps_trace, n, "phase trace")) return e;
-    HC_TRY_CUDA(cudaMemset(s->ps_trace, 0, n * sizeof(unsigned long long)));
-  }
-  s->ps = true;
   return nullptr;
 }
 
@@ -548,8 +409,11 @@ HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session
   }
   if (char *e = alloc(&s->x, size_t(T) * D, "hidden states")) return e;
   if (char *e = alloc(&s->qkv, size_t(T) * (H + 2 * KV) * hd, "qkv")) return e;
-  if (s->paged)
-    if (char *e = alloc(&s->kv_stage, size_t(T) * 2 * KV * hd, "new key and value rows")) return e;
+  if (char *e = alloc(&s->kv_stage, size_t(T) * 2 * KV * hd, "new key and value rows")) return e;
+  s->tc_ws_floats = size_t(4) << 20;  // 16 MB of split-K partials
+  if (char *e = alloc(&s->tc_ws, s->tc_ws_floats, "split-K partials")) return e;
+  if (char *e = alloc(&s->tc_tickets, size_t(kTcTickets), "split-K tickets")) return e;
+  HC_TRY_CUDA(cudaMemset(s->tc_tickets, 0, sizeof(int) * kTcTickets));
   if (char *e = alloc(&s->q, size_t(T) * H * hd, "queries")) return e;
   if (char *e = alloc(&s->h, size_t(T) * F, "mlp activations")) return e;
   if (char *e = alloc(&s->act, size_t(T) * ktiles * hc::kActTile, "activation tiles")) return e;
@@ -571,7 +435,6 @@ HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session
   s->pos.assign(o.max_seqs, 0);
   s->poisoned.assign(o.max_seqs, false);
   HC_TRY_CUDA(cudaMemset(s->amax, 0, sizeof(unsigned long long) * T * hc::kAmaxSlots));
-  if (char *e = ps_setup(s.get())) return e;
   *out = s.release();
   return nullptr;
 }
@@ -595,23 +458,40 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
       if (seq_ids[j] == sq) return hc::make_error("hc_step: sequence listed twice");
     if (s->pos[sq] + n > s->cap) return hc::make_error("hc_step: sequence " + std::to_string(sq) + " would exceed max_context");
   }
+  // The chunks of up to kMaxChunk tokens: a sequence's tokens are cut into pieces of kMaxChunk from
+  // its first, and a piece never straddles two chunks, so that the keys a token reads in float32
+  // (its piece's) do not depend on the other sequences of the call.
+  std::vector<std::pair<size_t, size_t>> chunks;  // [begin, end) of `all`
+  size_t cb = 0;
   int off = 0;
   for (int i = 0; i < nseq; ++i) {
     for (int j = 0; j < n_tokens[i]; ++j) {
       const int tok = tokens[off + j];
       if (tok < 0 || tok >= V) return hc::make_error("hc_step: token " + std::to_string(tok) + " out of the vocabulary");
-      all.push_back(hc::StepTok{tok, seq_ids[i], s->pos[seq_ids[i]] + j, 0});
-      if ((flags & HC_STEP_ALL_ROWS) || j == n_tokens[i] - 1) want.push_back(int(all.size()) - 1);
+    }
+    for (int p = 0; p < n_tokens[i]; p += kMaxChunk) {
+      const int len = std::min(kMaxChunk, n_tokens[i] - p);
+      if (all.size() - cb + len > size_t(kMaxChunk)) {
+        chunks.push_back({cb, all.size()});
+        cb = all.size();
+      }
+      const int32_t r0 = int32_t(all.size() - cb);
+      for (int j = p; j < p + len; ++j) {
+        all.push_back(hc::StepTok{tokens[off + j], seq_ids[i], s->pos[seq_ids[i]] + j, 0, r0});
+        if ((flags & HC_STEP_ALL_ROWS) || j == n_tokens[i] - 1) want.push_back(int(all.size()) - 1);
+      }
     }
     off += n_tokens[i];
   }
+  chunks.push_back({cb, all.size()});
   if (hc::fault_fires(hc::kFaultStep)) return hc::make_error("injected fault: step");
   HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
   size_t wi = 0;
   int row = 0;
   double step_us = 0;  // the call's device time: the sum over its chunks
-  for (size_t c0 = 0; c0 < all.size(); c0 += kMaxChunk) {
-    const int n = int(std::min<size_t>(kMaxChunk, all.size() - c0));
+  for (const auto &ch : chunks) {
+    const size_t c0 = ch.first;
+    const int n = int(ch.second - ch.first);
     std::memcpy(s->toks_host, &all[c0], sizeof(hc::StepTok) * n);
     int heads = 0;  // the chunk's rows that are read out, in order
     for (size_t w = wi; w < want.size() && size_t(want[w]) < c0 + n; ++w) s->toks_host[heads++].head_src = int(want[w] - c0);
@@ -621,7 +501,6 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
     }
     int32_t st_ = HC_STATE_ERROR;
     char *e = wait_done(s, timeout_ms, &st_);
-    if (!e && st_ == HC_STATE_COMPLETED && s->chunk_ps) e = ps_status_error(s);
     if (e || st_ != HC_STATE_COMPLETED) {
       for (int i = 0; i < nseq; ++i) s->poisoned[seq_ids[i]] = true;
       if (state) *state = e ? HC_STATE_ERROR : st_;
@@ -629,10 +508,8 @@ HC_API char *hc_step(hc_session *s, const int32_t *seq_ids, const int32_t *n_tok
     }
     step_us += s->stats.last_step_us;
     for (int j = 0; wi < want.size() && size_t(want[wi]) < c0 + n; ++wi, ++row, ++j) {
-      // the kernel sequence writes the read rows in order; the persistent step every token's row
-      const int src = s->chunk_ps ? s->toks_host[j].head_src : j;
-      if (argmax) argmax[row] = s->am_host[src];
-      if (logits) HC_TRY_CUDA(cudaMemcpy(logits + size_t(row) * V, s->logits_dev + size_t(src) * V, size_t(V) * 2, cudaMemcpyDeviceToHost));
+      if (argmax) argmax[row] = s->am_host[j];
+      if (logits) HC_TRY_CUDA(cudaMemcpy(logits + size_t(row) * V, s->logits_dev + size_t(j) * V, size_t(V) * 2, cudaMemcpyDeviceToHost));
     }
   }
   uint64_t kv = 0;
@@ -660,14 +537,13 @@ HC_API char *hc_speculate(hc_session *s, int32_t seq, const int32_t *toks, int32
   const int V = int(s->m->d.vocab);
   for (int j = 0; j < n; ++j) {
     if (toks[j] < 0 || toks[j] >= V) return hc::make_error("hc_speculate: token out of the vocabulary");
-    s->toks_host[j] = hc::StepTok{toks[j], seq, s->pos[seq] + j, j};
+    s->toks_host[j] = hc::StepTok{toks[j], seq, s->pos[seq] + j, j, 0};
   }
   if (hc::fault_fires(hc::kFaultStep)) return hc::make_error("injected fault: step");
   HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
   if (char *e = run_chunk(s, n, true, n)) { s->poisoned[seq] = true; return e; }
   int32_t st_ = HC_STATE_ERROR;
   char *e = wait_done(s, timeout_ms, &st_);
-  if (!e && st_ == HC_STATE_COMPLETED && s->chunk_ps) e = ps_status_error(s);
   if (e || st_ != HC_STATE_COMPLETED) {
     s->poisoned[seq] = true;
     if (state) *state = e ? HC_STATE_ERROR : st_;
@@ -698,19 +574,12 @@ HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, i
   HC_TRY_CUDA(cudaSetDevice(s->m->ordinal));
   if (char *e = ensure_pages(s, seq, s->pos[seq], s->pos[seq] + n)) return e;
   cudaStream_t st = s->st;
-  s->toks_host[0] = hc::StepTok{first, seq, s->pos[seq], 0};
-  const bool ps = ps_chunk(s, 1);
+  s->toks_host[0] = hc::StepTok{first, seq, s->pos[seq], 0, 0};
   if (!s->gen_graph) {
     cudaGraph_t graph = nullptr;
     HC_TRY_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    if (ps) {
-      // the status word is zeroed once before the loop: after a failed launch the later ones
-      // return at once (they see it set)
-      s->launches_per_chunk[0] = uint64_t(enqueue_ps(s, 1, true, kSpinLimit));
-    } else {
-      s->launches_per_chunk[0] = uint64_t(enqueue_model(s, 1, false, splits_for(s, 1, 0), 1)) + 1;
-      hc::advance(s->toks_dev, s->am_dev, s->gen_out, s->gen_count, st);
-    }
+    s->launches_per_chunk[0] = uint64_t(enqueue_model(s, 1, false, splits_for(s, 1, 0), 1)) + 1;
+    hc::advance(s->toks_dev, s->am_dev, s->gen_out, s->gen_count, st);
     cudaError_t e = cudaStreamEndCapture(st, &graph);
     if (e != cudaSuccess) return hc::make_error(std::string("graph capture: ") + cudaGetErrorString(e));
     e = cudaGraphInstantiate(&s->gen_graph, graph, 0);
@@ -719,22 +588,13 @@ HC_API char *hc_generate(hc_session *s, int32_t seq, int32_t first, int32_t n, i
   }
   HC_TRY_CUDA(cudaMemcpyAsync(s->toks_dev, s->toks_host, sizeof(hc::StepTok), cudaMemcpyHostToDevice, st));
   HC_TRY_CUDA(cudaMemsetAsync(s->gen_count, 0, sizeof(int32_t), st));
-  if (ps) {
-    *s->ps_status_host = 0;
-    HC_TRY_CUDA(cudaMemsetAsync(s->ps_status, 0, sizeof(int), st));
-  }
   HC_TRY_CUDA(cudaEventRecord(s->ev0, st));
   hc::device_stall(hc::take_stall_ms(), st);
   for (int i = 0; i < n; ++i) HC_TRY_CUDA(cudaGraphLaunch(s->gen_graph, st));
   HC_TRY_CUDA(cudaEventRecord(s->ev1, st));
-  if (ps) HC_TRY_CUDA(cudaMemcpyAsync(s->ps_status_host, s->ps_status, sizeof(int), cudaMemcpyDeviceToHost, st));
   s->stats.launches += uint64_t(n) * s->launches_per_chunk[0];
   int32_t st_ = HC_STATE_ERROR;
   char *e = wait_done(s, timeout_ms, &st_);
-  if (!e && st_ == HC_STATE_COMPLETED && ps) {
-    HC_TRY_CUDA(cudaStreamSynchronize(st));
-    e = ps_status_error(s);
-  }
   if (e || st_ != HC_STATE_COMPLETED) {
     s->poisoned[seq] = true;
     if (state) *state = e ? HC_STATE_ERROR : st_;
@@ -823,42 +683,6 @@ HC_API char *hc_seq_import_rows(hc_session *s, int32_t seq, int32_t start, int32
   if (char *e = rows_copy(s, seq, start, n, const_cast<void *>(src), false)) return e;
   s->pos[seq] = start + n;
   s->poisoned[seq] = false;
-  return nullptr;
-}
-
-HC_API char *hc_profile_get(hc_session *s, double *us, uint32_t cap, uint32_t *n) {
-  if (!s || !n) return hc::make_error("hc_profile_get: NULL argument");
-  if (!s->ps_trace)
-    return hc::make_error("hc_profile_get: the session was not opened with HC_SESSION_PROFILE and the persistent step");
-  const int P = hc::ps_phases(int(s->m->d.layers));
-  *n = uint32_t(P);
-  if (!us) return nullptr;
-  std::vector<unsigned long long> t(size_t(4) * P);
-  HC_TRY_CUDA(cudaStreamSynchronize(s->st));
-  HC_TRY_CUDA(cudaMemcpy(t.data(), s->ps_trace, t.size() * 8, cudaMemcpyDeviceToHost));
-  auto d = [](unsigned long long a, unsigned long long b) { return b > a ? double(b - a) / 1e3 : 0.0; };
-  for (int i = 0; i < P; ++i) {
-    const unsigned long long start = i ? t[4 * (i - 1) + 2] : t[0];
-    const double v[4] = {d(start, t[4 * i]), d(t[4 * i], t[4 * i + 1]), i + 1 < P ? d(t[4 * i + 1], t[4 * i + 2]) : 0.0,
-                         double(t[4 * i + 3]) / 1e3};
-    for (int k = 0; k < 4; ++k)
-      if (uint32_t(4 * i + k) < cap) us[4 * i + k] = v[k];
-  }
-  // then, per layer, the attention unit that merged (token 0, kv head 0): microseconds from the
-  // unit's start to its inputs loaded, its stages in, its partial written, its ticket taken, the
-  // merge written; then the CTA and the unit's index in the CTA
-  const int L = int(s->m->d.layers);
-  if (cap >= uint32_t(4 * P + 8 * L)) {
-    std::vector<unsigned long long> u(size_t(8) * L);
-    HC_TRY_CUDA(cudaMemcpy(u.data(), s->ps_trace + size_t(4) * P, u.size() * 8, cudaMemcpyDeviceToHost));
-    for (int l = 0; l < L; ++l) {
-      const unsigned long long *m = &u[size_t(8) * l];
-      for (int k = 1; k < 6; ++k) us[4 * P + 8 * l + k - 1] = d(m[0], m[k]);
-      us[4 * P + 8 * l + 5] = double(m[6]);
-      us[4 * P + 8 * l + 6] = double(m[7]);
-      us[4 * P + 8 * l + 7] = 0;
-    }
-  }
   return nullptr;
 }
 

@@ -1,0 +1,475 @@
+// tcgemm.cu: the batched GEMV of the int8 and int4 formats (9..64 tokens: prompt chunks, ragged
+// decode batches, speculative verify chunks past 8 rows) on the 5th-generation tensor cores.
+//
+// Y[t][r] = sum_k X[t][k] W[r][k] for n <= 64 tokens. A CTA owns a tile of 128 weight rows (8 of
+// the 16-row repacked tiles) over a range of column tiles (all of them, or a split of them when
+// there are too few row tiles to fill the SMs), and all n tokens: one tcgen05.mma of M = 128,
+// N = n rounded up to 16, K = 16 (kind::f16, float32 accumulator in tensor memory) per 16 columns.
+//
+//   warp 0      producer: bulk copies (cp.async.bulk, no multicast) of each column tile's 8 weight
+//               tiles and of the tokens' fp16 operand into a 2-stage ring (mbarrier complete_tx)
+//   warp 1      allocates the tensor memory; one lane issues the MMAs and their commits
+//   warps 2..5  dequantise each half column tile of weights from the ring into the MMA's A operand
+//               (fp16, K-major, no swizzle), then run the epilogue from the accumulator
+//
+// Arithmetic. A weight is dequantised with its format's float32 arithmetic (int4: (q - z) s,
+// milcpu shiftScale) and rounded to fp16; int8 codes go in as exact integers and their row scale is
+// applied to the float32 sum. The tokens' values are rounded to fp16 once (act_quant's fp16
+// operand). Products and sums are exact/float32 in the tensor core. So a row of a 9..64-token chunk
+// differs from the same row computed by the one-token GEMV (int8 hi/lo activations) by the fp16
+// roundings, about 2^-12 of a product; both are within the model tolerance of the oracle.
+//
+// With splits > 1 each CTA writes its float32 partial sums to a workspace, and the last CTA of a
+// row tile (a ticket) adds them in split order and runs the epilogue: the result does not depend
+// on which CTA finishes first.
+//
+// Every mbarrier wait is bounded (about a second of SM clocks): a wait that runs out records an
+// error code in *status and proceeds, so that no thread waits forever; the kernel still waits for
+// its own bulk copies and MMAs before it frees the tensor memory and exits.
+#include <algorithm>
+
+#include "device.cuh"
+#include "kernels.h"
+
+namespace hc {
+namespace {
+
+constexpr int kTcRows = 128;                       // rows of a CTA tile: 8 row tiles (the MMA's M)
+constexpr int kTcTiles = kTcRows / kTileRows;      // 8
+constexpr int kTcStages = 2;                       // ring stages, a column tile each
+constexpr int kTcThreads = 6 * 32;
+constexpr int kTcHalf = kTileCols / 2;             // columns of one A buffer
+constexpr int kTcABytes = kTcRows * kTcHalf * 2;   // 32 KB
+constexpr int kTcStepA = kTcRows * 16 * 2;         // bytes of A per 16 columns (one MMA's K)
+constexpr int kTcMaxN = 64;
+constexpr long long kTcSpin = 2000000000ll;        // clock cycles a wait may take
+
+__device__ __forceinline__ uint32_t tc_saddr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void tc_bar_init(uint64_t *b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc_saddr(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void tc_arrive(uint64_t *b) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(tc_saddr(b)) : "memory");
+}
+__device__ __forceinline__ void tc_expect_tx(uint64_t *b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(tc_saddr(b)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool tc_try(uint64_t *b, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred P;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 P, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, P;\n}\n"
+      : "=r"(ok)
+      : "r"(tc_saddr(b)), "r"(parity), "n"(1000)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase of the given parity to complete, at most kTcSpin cycles; on running out it
+// records code in *status (the first one) and returns.
+__device__ __forceinline__ void tc_wait(uint64_t *b, unsigned parity, int *status, int code) {
+  const long long t0 = clock64();
+  while (!tc_try(b, parity)) {
+    if (clock64() - t0 > kTcSpin) {
+      atomicCAS(status, 0, code);
+      return;
+    }
+  }
+}
+__device__ __forceinline__ void tc_bulk(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(tc_saddr(dst)),
+      "l"(src), "r"(bytes), "r"(tc_saddr(bar))
+      : "memory");
+}
+
+// ---- tcgen05 --------------------------------------------------------------------------------
+// Shared-memory matrix descriptor of a K-major operand without swizzle: core matrices of 8 rows x
+// 16 bytes (128 contiguous bytes); lbo: bytes between the two core matrices of one MMA's 16
+// columns, sbo: bytes between core matrices 8 rows apart; version 1 (bits 46-47).
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
+         (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46);
+}
+// Instruction descriptor of kind::f16: fp16 A and B, K-major both, float32 D, M = 128, N = n.
+__host__ __device__ constexpr uint32_t tc_idesc(int n) {
+  return (1u << 4) | (uint32_t(n >> 3) << 17) | (uint32_t(kTcRows >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// Arrives on b once every MMA this thread issued before has completed.
+__device__ __forceinline__ void tc_commit(uint64_t *b) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(tc_saddr(b))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+// Makes this thread's shared-memory stores visible to the tensor core (the async proxy).
+__device__ __forceinline__ void tc_fence_proxy() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 16 columns of the accumulator for this warp's 32 lanes (rows) into v.
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- dequantisation into the A operand --------------------------------------------------------
+// Byte offset, in one half buffer (128 rows x 128 columns), of the 16-byte run of 8 columns
+// kl..kl+7 (kl a multiple of 8) of row r: K-steps of 16 columns (kTcStepA bytes), in a step the core
+// matrices of 8 rows (256 bytes a row group: the two 8-column halves, 128 bytes apart).
+__device__ __forceinline__ int tc_aoff(int r, int kl) {
+  return (kl >> 4) * kTcStepA + (r >> 3) * 256 + ((kl >> 3) & 1) * 128 + (r & 7) * 16;
+}
+
+// Packs 8 float values rounded to fp16 into 16 bytes.
+__device__ __forceinline__ uint4 tc_pack8(const float (&f)[8]) {
+  uint4 o;
+  __half2 h;
+  h = __floats2half2_rn(f[0], f[1]); o.x = *reinterpret_cast<uint32_t *>(&h);
+  h = __floats2half2_rn(f[2], f[3]); o.y = *reinterpret_cast<uint32_t *>(&h);
+  h = __floats2half2_rn(f[4], f[5]); o.z = *reinterpret_cast<uint32_t *>(&h);
+  h = __floats2half2_rn(f[6], f[7]); o.w = *reinterpret_cast<uint32_t *>(&h);
+  return o;
+}
+
+// float(q) of the byte (or nibble) codes 0..255 by the exponent trick (exact).
+__device__ __forceinline__ float tc_u2f(uint32_t q) { return __uint_as_float(0x4B000000u | q) - 8388608.0f; }
+
+// Half h (columns 128h .. 128h + 127) of one repacked 16 x 256 tile into the A buffer at rows
+// 16 i .. 16 i + 15. The tile's 16-byte pieces (common.h's tile_pos): piece (o, lane = 4 g + c)
+// holds rows g and g + 8, elements 8o .. 8o + 7 of group c (and, int4, group c + 4 in the high
+// nibbles; int8: pieces 4h + o). A thread takes 4 pieces (o = 0..3) of one lane; the lanes of a
+// warp are ordered so that 8 consecutive threads write one 128-byte run.
+template <int KIND>
+__device__ __forceinline__ void tc_dequant_half(const uint8_t *__restrict__ tile, int h, uint8_t *abuf, int i,
+                                                int lane_ord, bool present) {
+  const int lane = 4 * (lane_ord & 7) + (lane_ord >> 3);  // lane (g, c) of the tile's layout
+  const int g = lane >> 2, c = lane & 3;
+  float s0 = 0.f, z0 = 0.f, s1 = 0.f, z1 = 0.f;
+  if (KIND == kKindInt4 && present) {
+    const uint4 sz = *reinterpret_cast<const uint4 *>(tile + kTileCodes4 + lane * 16);
+    const uint32_t sw = h ? sz.y : sz.x, zw = h ? sz.w : sz.z;  // (s, s) of rows g, g + 8 at half h
+    s0 = __half2float(__ushort_as_half(uint16_t(sw & 0xFFFF)));
+    s1 = __half2float(__ushort_as_half(uint16_t(sw >> 16)));
+    z0 = __half2float(__ushort_as_half(uint16_t(zw & 0xFFFF)));
+    z1 = __half2float(__ushort_as_half(uint16_t(zw >> 16)));
+  }
+#pragma unroll
+  for (int o = 0; o < 4; ++o) {
+    uint4 out0 = make_uint4(0, 0, 0, 0), out1 = make_uint4(0, 0, 0, 0);
+    if (present) {
+      const int piece = KIND == kKindInt8 ? 4 * h + o : o;
+      const uint4 w = *reinterpret_cast<const uint4 *>(tile + (piece * 32 + lane) * 16);
+      float a[8], b[8];
+      if (KIND == kKindInt8) {
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          a[p] = float(int8_t((w.x >> (8 * p)) & 0xFF));
+          a[4 + p] = float(int8_t((w.z >> (8 * p)) & 0xFF));
+          b[p] = float(int8_t((w.y >> (8 * p)) & 0xFF));
+          b[4 + p] = float(int8_t((w.w >> (8 * p)) & 0xFF));
+        }
+      } else {
+        const int sh = 4 * h;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          a[p] = __fmul_rn(__fsub_rn(tc_u2f((w.x >> (8 * p + sh)) & 15u), z0), s0);
+          a[4 + p] = __fmul_rn(__fsub_rn(tc_u2f((w.z >> (8 * p + sh)) & 15u), z0), s0);
+          b[p] = __fmul_rn(__fsub_rn(tc_u2f((w.y >> (8 * p + sh)) & 15u), z1), s1);
+          b[4 + p] = __fmul_rn(__fsub_rn(tc_u2f((w.w >> (8 * p + sh)) & 15u), z1), s1);
+        }
+      }
+      out0 = tc_pack8(a);
+      out1 = tc_pack8(b);
+    }
+    const int kl = 32 * c + 8 * o;
+    *reinterpret_cast<uint4 *>(abuf + tc_aoff(16 * i + g, kl)) = out0;
+    *reinterpret_cast<uint4 *>(abuf + tc_aoff(16 * i + g + 8, kl)) = out1;
+  }
+}
+
+struct TcArgs {
+  const uint8_t *tiles;
+  const float *row_scale, *bias;
+  const uint8_t *xop;  // the tokens' fp16 operand: per column tile npad x 256 values (act_quant)
+  int rtiles, ktiles, rows, tile_bytes, ntok, npad, splits;
+  GemvOut out;
+  int *status;
+};
+
+__device__ int tc_status_word;  // the first wait that ran out in any launch (0: none)
+
+// The epilogue's named barrier over the four dequant warps.
+__device__ __forceinline__ void tc_epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int KIND>
+__global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) {
+  extern __shared__ __align__(1024) uint8_t tc_smem[];
+  __shared__ uint64_t full[kTcStages], empty[kTcStages], afull[2], aempty[2], done;
+  __shared__ uint32_t tmem_base;
+  __shared__ int last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = blockIdx.x / a.splits, sp = blockIdx.x % a.splits;
+  const int per = a.ktiles / a.splits, rem = a.ktiles % a.splits;
+  const int kt0 = sp * per + min(sp, rem), nkt = per + (sp < rem ? 1 : 0);
+  const int raw_bytes = kTcTiles * a.tile_bytes, b_bytes = a.npad * kTileCols * 2;
+  uint8_t *raw = tc_smem;
+  uint8_t *bop = raw + kTcStages * raw_bytes;
+  uint8_t *aop = bop + kTcStages * b_bytes;
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      tc_bar_init(&full[s], 1);
+      tc_bar_init(&empty[s], 5);  // the 4 dequant warps (weights read) + the MMA commit (tokens read)
+    }
+    for (int h = 0; h < 2; ++h) {
+      tc_bar_init(&afull[h], 4);
+      tc_bar_init(&aempty[h], 1);
+    }
+    tc_bar_init(&done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc_saddr(&tmem_base)),
+                 "r"(kTcMaxN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    // producer: the 8 weight tiles and the tokens' operand of each column tile
+    if (lane == 0) {
+      int present = 0;
+      for (int i = 0; i < kTcTiles; ++i) present += mt * kTcTiles + i < a.rtiles;
+      for (int j = 0; j < nkt; ++j) {
+        const int s = j % kTcStages, kt = kt0 + j;
+        if (j >= kTcStages) tc_wait(&empty[s], ((j / kTcStages) - 1) & 1, a.status, 1);
+        tc_expect_tx(&full[s], unsigned(present * a.tile_bytes + b_bytes));
+        for (int i = 0; i < kTcTiles; ++i) {
+          const int rt = mt * kTcTiles + i;
+          if (rt < a.rtiles)
+            tc_bulk(raw + s * raw_bytes + i * a.tile_bytes, a.tiles + (size_t(rt) * a.ktiles + kt) * a.tile_bytes,
+                    unsigned(a.tile_bytes), &full[s]);
+        }
+        if (j == 0) pdl_wait();  // the operand is the previous kernel's output
+        tc_bulk(bop + s * b_bytes, a.xop + size_t(kt) * b_bytes, unsigned(b_bytes), &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // MMA issue: 8 MMAs (K = 16 each) per half column tile
+    if (lane == 0) {
+      const uint32_t idesc = tc_idesc(a.npad);
+      int acc = 0;
+      for (int j = 0; j < nkt; ++j) {
+        const int s = j % kTcStages;
+        tc_wait(&full[s], (j / kTcStages) & 1, a.status, 2);
+        for (int h = 0; h < 2; ++h) {
+          tc_wait(&afull[h], j & 1, a.status, 3);
+          tc_fence_after();
+          const uint32_t abase = tc_saddr(aop + h * kTcABytes);
+          const uint32_t bbase = tc_saddr(bop + s * b_bytes);
+#pragma unroll
+          for (int st = 0; st < 8; ++st) {
+            const uint64_t ad = tc_desc(abase + st * kTcStepA, 128, 256);
+            const uint64_t bd = tc_desc(bbase + (h * 8 + st) * a.npad * 32, 128, 256);
+            tc_mma(tmem, ad, bd, idesc, acc);
+            acc = 1;
+          }
+          tc_commit(&aempty[h]);
+        }
+        tc_commit(&empty[s]);
+      }
+      tc_commit(&done);
+    }
+  } else {
+    // dequantisation (warps 2..5), then the epilogue
+    const int dw = warp - 2;
+    for (int j = 0; j < nkt; ++j) {
+      const int s = j % kTcStages;
+      tc_wait(&full[s], (j / kTcStages) & 1, a.status, 4);
+      const uint8_t *rs = raw + s * raw_bytes;
+      for (int h = 0; h < 2; ++h) {
+        if (j >= 1) tc_wait(&aempty[h], (j - 1) & 1, a.status, 5);
+        uint8_t *ab = aop + h * kTcABytes;
+        for (int i = dw; i < kTcTiles; i += 4)
+          tc_dequant_half<KIND>(rs + i * a.tile_bytes, h, ab, i, lane, mt * kTcTiles + i < a.rtiles);
+        tc_fence_proxy();
+        __syncwarp();
+        if (lane == 0) tc_arrive(&afull[h]);
+      }
+      __syncwarp();
+      if (lane == 0) tc_arrive(&empty[s]);
+    }
+    tc_wait(&done, 0, a.status, 6);
+    tc_fence_after();
+    // this warp's quarter of the accumulator: rows 32 q + lane, all npad columns (tokens)
+    const int q = warp & 3;
+    const int rl = 32 * q + lane;
+    float v[kTcMaxN];
+#pragma unroll
+    for (int c = 0; c < kTcMaxN / 16; ++c) {
+      if (c * 16 < a.npad) {
+        float t16[16];
+        tc_ld16(tmem + (uint32_t(32 * q) << 16) + uint32_t(16 * c), t16);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[16 * c + e] = t16[e];
+      }
+    }
+    pdl_wait();
+    const int rows_pad = (gridDim.x / a.splits) * kTcRows;
+    const int row = mt * kTcRows + rl;  // tile row index (16 rows a tile)
+    if (a.splits > 1) {
+      float *w = a.out.ws + size_t(sp) * kTcMaxN * rows_pad + row;
+#pragma unroll
+      for (int t = 0; t < kTcMaxN; ++t)
+        if (t < a.ntok) w[size_t(t) * rows_pad] = v[t];
+      __threadfence();
+      tc_epi_sync();
+      if (dw == 0 && lane == 0) last = atomicAdd(&a.out.tickets[mt], 1) == a.splits - 1;
+      tc_epi_sync();
+      if (!last) goto teardown;
+      __threadfence();
+#pragma unroll
+      for (int t = 0; t < kTcMaxN; ++t) {
+        if (t < a.ntok) {
+          float acc = 0.f;
+          for (int k = 0; k < a.splits; ++k) acc += __ldcg(a.out.ws + (size_t(k) * kTcMaxN + t) * rows_pad + row);
+          v[t] = acc;
+        }
+      }
+      if (dw == 0 && lane == 0) a.out.tickets[mt] = 0;  // for the next launch
+    }
+    {
+      const GemvOut &out = a.out;
+      const bool valid = row < a.rtiles * kTileRows;
+      float scale = 1.f, bias = 0.f;
+      if (valid && KIND == kKindInt8) scale = a.row_scale[row];
+      if (valid && a.bias) bias = a.bias[row];
+#pragma unroll
+      for (int t = 0; t < kTcMaxN; ++t) v[t] = v[t] * scale + bias;
+      if (out.mode == kGlu) {
+        // tile rows 0-7 gate, 8-15 up: lane l (l % 16 < 8) pairs with lane l + 8
+        const int r16 = lane & 15, o = (row >> 4) * (kTileRows / 2) + r16;
+#pragma unroll
+        for (int t = 0; t < kTcMaxN; ++t) {
+          const float u = __shfl_down_sync(0xffffffffu, v[t], 8);
+          if (t < a.ntok && valid && r16 < 8 && o < a.rows) {
+            const float gv = v[t];
+            // blocks.SiLU: x / (1 + exp(-x)) (internal/llm/blocks/blocks.go:395-399)
+            out.y[size_t(t) * out.ldy + o] = gv / (1.0f + expf(-gv)) * u;
+          }
+        }
+      } else if (out.mode == kLogits) {
+#pragma unroll
+        for (int t = 0; t < kTcMaxN; ++t) {
+          if (t >= a.ntok) continue;
+          unsigned long long key = 0ull;
+          if (valid && row < a.rows) {
+            const uint16_t hb = __half_as_ushort(__float2half_rn(v[t]));
+            if (out.logits) out.logits[size_t(t) * out.ldy + row] = hb;
+            key = argmax_key(hb, uint32_t(row));
+          }
+#pragma unroll
+          for (int off = 16; off; off >>= 1) {
+            const unsigned long long o2 = __shfl_xor_sync(0xffffffffu, key, off);
+            key = o2 > key ? o2 : key;
+          }
+          if (lane == 0 && key) atomicMax(&out.amax[t * kAmaxSlots + (mt % kAmaxSlots)], key);
+        }
+      } else if (valid && row < a.rows) {
+#pragma unroll
+        for (int t = 0; t < kTcMaxN; ++t) {
+          if (t >= a.ntok) continue;
+          float *p = out.y + size_t(t) * out.ldy + row;
+          *p = out.mode == kAdd ? *p + v[t] : v[t];
+        }
+      }
+    }
+  }
+teardown:
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcMaxN) : "memory");
+  }
+}
+
+size_t tc_smem_bytes(int tile_bytes, int npad) {
+  return size_t(kTcStages) * (kTcTiles * tile_bytes + npad * kTileCols * 2) + 2 * kTcABytes;
+}
+
+}  // namespace
+
+namespace {
+int *g_tc_status[64];  // each device's tc_status_word (tc_gemm_prepare, outside any capture)
+}  // namespace
+
+char *tc_gemm_prepare() {
+  int dev = 0;
+  HC_TRY_CUDA(cudaGetDevice(&dev));
+  HC_TRY_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&g_tc_status[dev & 63]), tc_status_word));
+  const int mx = int(tc_smem_bytes(kTileCodes8, kTcMaxN));
+  HC_TRY_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<kKindInt8>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx));
+  HC_TRY_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<kKindInt4>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx));
+  return nullptr;
+}
+
+int tc_splits(const DevMat &W, int sms, size_t ws_floats) {
+  const int mtiles = (W.rtiles + kTcTiles - 1) / kTcTiles;
+  int best = 1;
+  long best_cost = -1;
+  for (int s = 1; s <= std::min(W.ktiles, 16); ++s) {
+    if (s > 1 && size_t(s) * kTcMaxN * mtiles * kTcRows > ws_floats) break;
+    const long waves = (long(mtiles) * s + sms - 1) / sms;
+    const long cost = waves * ((W.ktiles + s - 1) / s);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
+void tc_gemm(const DevMat &W, const uint8_t *xop, int ntok, const GemvOut &out, int sms, cudaStream_t st) {
+  const int npad = (ntok + 15) / 16 * 16;
+  const int mtiles = (W.rtiles + kTcTiles - 1) / kTcTiles;
+  const int splits = (out.ws && out.tickets) ? tc_splits(W, sms, out.ws_floats) : 1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int *status = g_tc_status[dev & 63];
+  const TcArgs a{W.tiles, W.row_scale, W.bias, xop, W.rtiles, W.ktiles, W.rows, W.tile_bytes, ntok, npad, splits,
+                 out, status};
+  const size_t smem = tc_smem_bytes(W.tile_bytes, npad);
+  if (W.kind == kKindInt8)
+    launch_pdl(tc_gemm_kernel<kKindInt8>, dim3(mtiles * splits), dim3(kTcThreads), smem, st, a);
+  else
+    launch_pdl(tc_gemm_kernel<kKindInt4>, dim3(mtiles * splits), dim3(kTcThreads), smem, st, a);
+}
+
+int tc_status_take() {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, tc_status_word, sizeof(int)) != cudaSuccess) return 0;
+  if (v) cudaMemcpyToSymbol(tc_status_word, &zero, sizeof(int));
+  return v;
+}
+
+}  // namespace hc

@@ -95,12 +95,8 @@ class LoadedModel:
     def weight_bytes(self):
         return A.lib().hc_model_weight_bytes(self.h)
 
-    def session(self, max_context, max_seqs=1, max_step=8, kv_format=A.HC_KV_F16, page_size=16, graphs=True,
-                persistent=False, profile=False):
-        """persistent: chunks of up to 8 tokens run as the persistent step where the model allows
-        (HC_SESSION_PERSISTENT; else the kernel sequence)."""
-        flags = (0 if graphs else A.HC_SESSION_NO_GRAPH) | (A.HC_SESSION_PERSISTENT if persistent else 0) | \
-                (A.HC_SESSION_PROFILE if profile else 0)
+    def session(self, max_context, max_seqs=1, max_step=8, kv_format=A.HC_KV_F16, page_size=16, graphs=True):
+        flags = 0 if graphs else A.HC_SESSION_NO_GRAPH
         return Session(self, max_context, max_seqs, max_step, kv_format, page_size, flags)
 
     def close(self):
@@ -205,19 +201,6 @@ class Session:
     def import_rows(self, start, n, rows, seq=0):
         rows = np.ascontiguousarray(rows, np.uint8)
         A.check(A.lib().hc_seq_import_rows(self.h, seq, start, n, rows.ctypes.data_as(C.c_void_p), rows.nbytes))
-
-    def profile(self):
-        """Per-phase microseconds of the persistent step's last launch (hc_profile_get), as an
-        array [phases][4]: inputs ready, work done, next barrier passed, and of the work the time spent waiting for ring stages (5 phases a layer: qkv,
-        attention, o, gate/up, down; then the head)."""
-        n = C.c_uint32()
-        A.check(A.lib().hc_profile_get(self.h, None, 0, C.byref(n)))
-        L = self.lm.model.cfg.layers
-        out = np.zeros(4 * n.value + 8 * L, np.float64)
-        A.check(A.lib().hc_profile_get(self.h, out.ctypes.data_as(C.POINTER(C.c_double)), out.size, C.byref(n)))
-        # the merging attention unit of each layer: inputs, stages, partial, ticket, merge (us), cta, unit
-        self.last_units = out[4 * n.value:].reshape(L, 8)
-        return out[:4 * n.value].reshape(n.value, 4)
 
     def stats(self):
         s = A.Stats()

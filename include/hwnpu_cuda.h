@@ -78,6 +78,11 @@ HC_API void hc_device_free(hc_device *d);
 /* Replaces xs_device_info (xrtshim.h:80): writes the value, NUL terminated, into buf of n
  * bytes; *need is its length with the NUL. */
 HC_API char *hc_device_info(hc_device *d, int key, char *buf, size_t n, size_t *need);
+/* Health of the library's kernels on the device: an error string when a bounded wait inside one of
+ * them (the tensor-core GEMV's pipeline waits, about a second each) ran out since the last call --
+ * the results of that launch are not to be trusted -- else NULL; clears the record. Waits for the
+ * device's queued work first. (The reference's xs_run_wait reports a failed run the same way.) */
+HC_API char *hc_device_check(hc_device *d);
 
 /* ---------------------------------------------------------------------------------------- */
 /* Buffers: backend.Device.AllocBuffer and backend.Buffer (backend.go:54-67)                  */
@@ -218,15 +223,6 @@ enum {
 };
 enum {
   HC_SESSION_NO_GRAPH = 1 << 0,      /* launch the step's kernels one by one (no CUDA graph) */
-  /* Run chunks of up to 8 tokens (decode steps, speculative verifies, small batches) of a dense
-   * model over the fp16 cache as the persistent step: one cooperative launch, one CTA a SM, a
-   * producer warp streaming each CTA's weight rows and cached keys through a shared-memory ring,
-   * attention splits fixed by position (a row computes the same in any chunk). Without it they run
-   * as the kernel sequence (one kernel an operation, chained by programmatic dependent launch),
-   * the faster of the two on B200 today. Longer chunks and the paged int8 cache always take the
-   * kernel sequence. */
-  HC_SESSION_PERSISTENT = 1 << 1,
-  HC_SESSION_PROFILE = 1 << 2,       /* time the phases of the persistent step (hc_profile_get) */
 };
 
 typedef struct hc_session_opts {
@@ -306,28 +302,12 @@ typedef struct hc_stats {
 
 HC_API char *hc_stats_get(hc_session *s, hc_stats *out);
 
-/* Per-phase timing of the last persistent step of a session opened with HC_SESSION_PROFILE (the
- * role of decode/profile.go:13-40, per-part times of a step), as CTA 0 saw it: phases are 5 a layer
- * (qkv GEMV, attention, o GEMV, gate/up, down) and the head; for phase i, us[4 i] is the time in
- * microseconds from the previous grid barrier to the phase's inputs in shared memory, us[4 i + 1]
- * to its work done, us[4 i + 2] to the next grid barrier passed, us[4 i + 3] the part of the work
- * its first thread spent waiting for weight or key stages. *n gets the number of phases; us may be
- * NULL to ask for it. With cap >= 4 n + 8 layers, us[4 n + 8 l ..] follow for each layer l: the
- * attention unit that merged token 0's first kv head, microseconds from its start to its inputs
- * loaded, its cached keys in, its partial written, its ticket taken and its merge written, then
- * its CTA and its index among the CTA's units. */
-HC_API char *hc_profile_get(hc_session *s, double *us, uint32_t cap, uint32_t *n);
-
 /* Fault injection for tests (the reference fakes its drivers instead, testdata/zemock):
  * "alloc:N" fails the N-th device allocation from now, "h2d:N" the N-th host-to-device copy,
  * "step:N" the N-th hc_step, each with an error string; "stall:MS" (MS <= 2000) makes the next
  * hc_step, hc_speculate or hc_generate first wait MS milliseconds on the device, so that a shorter
- * timeout_ms runs out (HC_STATE_TIMEOUT, the sequences poisoned until hc_seq_reset); "spin:N" gives
- * every wait of the next persistent step (grid barriers, ring stages) a limit of N clock cycles and
- * makes its first grid barrier wait for one arrival more than the grid has, so that the barrier runs
- * out and the call returns the step's error; "" clears. Nothing faults or hangs on the GPU: the
- * stall is a bounded wait on the global timer, and a persistent step whose wait gave up lets its
- * copies land and returns. */
+ * timeout_ms runs out (HC_STATE_TIMEOUT, the sequences poisoned until hc_seq_reset); "" clears.
+ * Nothing faults or hangs on the GPU: the stall is a bounded wait on the global timer. */
 HC_API char *hc_set_fault(const char *spec);
 
 /* ---------------------------------------------------------------------------------------- */

@@ -217,6 +217,11 @@ struct or_session {
 namespace {
 
 constexpr int kOrPage = 16;  // positions a page of the int8 cache
+// Tokens of one sequence that one step reads as a program: a step's tokens go in pieces of this
+// many (the prompt programs' chunking, decode.go:597-607), each piece reading the earlier positions
+// from the cache. The library cuts a call the same way (64-token chunks, a sequence's pieces from
+// its first token), so both read the same keys in float32.
+constexpr int kOrPiece = 64;
 
 // The round-up of a float32 to fp16 (the page scale, the smallest fp16 not below v; v >= 0 and
 // finite here).
@@ -500,80 +505,82 @@ OR_API int32_t or_step(or_session *s, const int32_t *tokens, int32_t n, int32_t 
         for (int e = 0; e < hd; ++e) out[e] = float(r[e]) * sc;
       }
     };
-    pool.parallel_for(long(n) * H, 1, [&](long lo, long hi) {
-      std::vector<float> kv_k, kv_v, sc_(0), p;
-      for (long job = lo; job < hi; ++job) {
-        const int t = int(job / H), h = int(job % H), kvh = h / rep, P = pos + t;
-        const int from = L.window > 0 ? std::max(0, P - L.window + 1) : 0;
-        const float *qh = &q[(size_t(t) * H + h) * hd];
-        std::vector<const float *> vrows;
-        std::vector<float> keys_f;  // cache rows decoded
-        int nk = 0;
-        std::vector<float> scores;
-        std::vector<float> cache_v;
-        std::vector<float> crow(hd);
-        for (int j = from; j < pos; ++j) {
-          cache_row(false, kvh, j, crow.data());
-          float acc = 0;
-          for (int e = 0; e < hd; ++e) acc = std::fma(qh[e], crow[e], acc);
-          scores.push_back(acc * sscale);
-          ++nk;
-        }
-        const int ncache = nk;
-        for (int uu = 0; uu <= t; ++uu) {
-          if (L.window > 0 && P - (pos + uu) >= L.window) { scores.push_back(NAN); continue; }
-          const float *kr = &k[(size_t(uu) * KV + kvh) * hd];
-          float acc = 0;
-          for (int e = 0; e < hd; ++e) acc = std::fma(qh[e], kr[e], acc);
-          scores.push_back(acc * sscale);
-        }
-        double mx = -INFINITY;
-        for (float z : scores) if (z == z) mx = std::max(mx, double(z));
-        const bool sink = !L.sinks.empty();
-        const double sk = sink ? double(f16r(L.sinks[h])) : 0;
-        if (sink) mx = std::max(mx, sk);
-        double zsum = 0;
-        for (float z : scores) if (z == z) zsum += std::exp(double(z) - mx);
-        if (sink) zsum += std::exp(sk - mx);
-        p.assign(scores.size(), 0);
-        for (size_t j = 0; j < scores.size(); ++j)
-          p[j] = scores[j] == scores[j] ? float(std::exp(double(scores[j]) - mx) / zsum) : 0.0f;
-        float *oh = &o[(size_t(t) * H + h) * hd];
-        std::fill(oh, oh + hd, 0.0f);
-        std::vector<float> blk(hd);
-        const size_t nkeys = scores.size();
-        for (size_t j0 = 0; j0 < nkeys; j0 += KC) {
-          std::fill(blk.begin(), blk.end(), 0.0f);
-          for (size_t j = j0; j < std::min(nkeys, j0 + KC); ++j) {
-            if (scores[j] != scores[j]) continue;
-            if (int(j) < ncache) {
-              cache_row(true, kvh, from + int(j), crow.data());
-              for (int e = 0; e < hd; ++e) blk[e] = std::fma(p[j], crow[e], blk[e]);
-            } else {
-              const float *vr = &v[(size_t(j - ncache) * KV + kvh) * hd];
-              for (int e = 0; e < hd; ++e) blk[e] = std::fma(p[j], vr[e], blk[e]);
+    // The step's tokens in pieces of kOrPiece (hc_step's chunking of one sequence): a piece's
+    // tokens read the earlier positions from the cache and the piece's own keys and values in
+    // float32; then the piece's rows go into the cache (decode.Session.keep, decode.go:1685-1705):
+    // fp16, or the int8 pages in position order.
+    for (int c0 = 0; c0 < n; c0 += kOrPiece) {
+      const int c1 = std::min(n, c0 + kOrPiece);
+      pool.parallel_for(long(c1 - c0) * H, 1, [&](long lo, long hi) {
+        std::vector<float> p;
+        for (long job = lo; job < hi; ++job) {
+          const int t = c0 + int(job / H), h = int(job % H), kvh = h / rep, P = pos + t;
+          const int from = L.window > 0 ? std::max(0, P - L.window + 1) : 0;
+          const float *qh = &q[(size_t(t) * H + h) * hd];
+          int nk = 0;
+          std::vector<float> scores;
+          std::vector<float> crow(hd);
+          for (int j = from; j < pos + c0; ++j) {
+            cache_row(false, kvh, j, crow.data());
+            float acc = 0;
+            for (int e = 0; e < hd; ++e) acc = std::fma(qh[e], crow[e], acc);
+            scores.push_back(acc * sscale);
+            ++nk;
+          }
+          const int ncache = nk;
+          for (int uu = c0; uu <= t; ++uu) {
+            if (L.window > 0 && P - (pos + uu) >= L.window) { scores.push_back(NAN); continue; }
+            const float *kr = &k[(size_t(uu) * KV + kvh) * hd];
+            float acc = 0;
+            for (int e = 0; e < hd; ++e) acc = std::fma(qh[e], kr[e], acc);
+            scores.push_back(acc * sscale);
+          }
+          double mx = -INFINITY;
+          for (float z : scores) if (z == z) mx = std::max(mx, double(z));
+          const bool sink = !L.sinks.empty();
+          const double sk = sink ? double(f16r(L.sinks[h])) : 0;
+          if (sink) mx = std::max(mx, sk);
+          double zsum = 0;
+          for (float z : scores) if (z == z) zsum += std::exp(double(z) - mx);
+          if (sink) zsum += std::exp(sk - mx);
+          p.assign(scores.size(), 0);
+          for (size_t j = 0; j < scores.size(); ++j)
+            p[j] = scores[j] == scores[j] ? float(std::exp(double(scores[j]) - mx) / zsum) : 0.0f;
+          float *oh = &o[(size_t(t) * H + h) * hd];
+          std::fill(oh, oh + hd, 0.0f);
+          std::vector<float> blk(hd);
+          const size_t nkeys = scores.size();
+          for (size_t j0 = 0; j0 < nkeys; j0 += KC) {
+            std::fill(blk.begin(), blk.end(), 0.0f);
+            for (size_t j = j0; j < std::min(nkeys, j0 + KC); ++j) {
+              if (scores[j] != scores[j]) continue;
+              if (int(j) < ncache) {
+                cache_row(true, kvh, from + int(j), crow.data());
+                for (int e = 0; e < hd; ++e) blk[e] = std::fma(p[j], crow[e], blk[e]);
+              } else {
+                const float *vr = &v[(size_t(c0 + int(j) - ncache) * KV + kvh) * hd];
+                for (int e = 0; e < hd; ++e) blk[e] = std::fma(p[j], vr[e], blk[e]);
+              }
             }
+            for (int e = 0; e < hd; ++e) oh[e] += blk[e];
           }
-          for (int e = 0; e < hd; ++e) oh[e] += blk[e];
         }
-      }
-    });
-    // decode.Session.keep (decode.go:1685-1705): the step's rows into the cache as fp16, or into the
-    // int8 pages in position order
-    for (int t = 0; t < n; ++t)
-      for (int h = 0; h < KV; ++h) {
-        if (!paged) {
-          for (int e = 0; e < hd; ++e) {
-            s->kc[li][(size_t(h) * s->cap + pos + t) * hd + e] = or_f16_bits(k[(size_t(t) * KV + h) * hd + e]);
-            s->vc[li][(size_t(h) * s->cap + pos + t) * hd + e] = or_f16_bits(v[(size_t(t) * KV + h) * hd + e]);
+      });
+      for (int t = c0; t < c1; ++t)
+        for (int h = 0; h < KV; ++h) {
+          if (!paged) {
+            for (int e = 0; e < hd; ++e) {
+              s->kc[li][(size_t(h) * s->cap + pos + t) * hd + e] = or_f16_bits(k[(size_t(t) * KV + h) * hd + e]);
+              s->vc[li][(size_t(h) * s->cap + pos + t) * hd + e] = or_f16_bits(v[(size_t(t) * KV + h) * hd + e]);
+            }
+          } else {
+            const int P = pos + t, page = P / kOrPage, off = P % kOrPage;
+            const size_t base = (size_t(h) * s->cap + size_t(page) * kOrPage) * hd;
+            page_write(&s->kq[li][base], &s->ks[li][size_t(h) * npages + page], off, &k[(size_t(t) * KV + h) * hd], hd);
+            page_write(&s->vq[li][base], &s->vs[li][size_t(h) * npages + page], off, &v[(size_t(t) * KV + h) * hd], hd);
           }
-        } else {
-          const int P = pos + t, page = P / kOrPage, off = P % kOrPage;
-          const size_t base = (size_t(h) * s->cap + size_t(page) * kOrPage) * hd;
-          page_write(&s->kq[li][base], &s->ks[li][size_t(h) * npages + page], off, &k[(size_t(t) * KV + h) * hd], hd);
-          page_write(&s->vq[li][base], &s->vs[li][size_t(h) * npages + page], off, &v[(size_t(t) * KV + h) * hd], hd);
         }
-      }
+    }
     // o_proj and the residual, then the MLP (qwen3 layerRest, build.go:184-189)
     linear(pool, L.o, o.data(), n, a.data());
     for (size_t i = 0; i < x.size(); ++i) x[i] = x[i] + a[i];

@@ -101,9 +101,14 @@ def test_gemv(device, fmt, shape, ntok):
         tol = 1e-5
     else:
         want = x.astype(np.float64) @ oracle_dequant(lin).astype(np.float64).T
-        tol = 1e-4
+        # up to 8 tokens: int8 hi/lo activations (about 15 bits); 9..64: the tensor-core GEMV's fp16
+        # operands (the weight and the activation each rounded to fp16, about 2^-12 of a product)
+        tol = 1e-4 if ntok <= 8 else 1e-3
     scale = np.abs(want).max()
     assert np.abs(got - want).max() <= tol * scale + 1e-7, np.abs(got - want).max() / scale
+    if ntok > 8 and fmt != A.HC_FMT_MXFP4:
+        # and no wait of the tensor-core GEMV ran out
+        A.check(A.lib().hc_device_check(device.h))
 
 
 def attention_ref(q, kc, vc, pos, window, sinks, scale):

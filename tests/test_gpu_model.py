@@ -78,83 +78,6 @@ def test_decode_matches_oracle(device, models, cfg, prompt, steps):
     ref.close()
 
 
-@pytest.mark.parametrize("cfg", [TINY, SYM4, C1, C2_2L], ids=lambda c: c.name)
-def test_persistent_step_matches_kernel_sequence(device, models, cfg):
-    # the persistent one-launch step (HC_SESSION_PERSISTENT) and the kernel sequence (one kernel an
-    # operation, the default) read the same logits within their float32 summation orders
-    # and make the same greedy choices
-    model = get(models, cfg)
-    lm = device.load_model(model)
-    a = lm.session(max_context=200, persistent=True)
-    b = lm.session(max_context=200, persistent=False)
-    toks = list(synth.tokens(31, cfg.vocab, 70))
-    la, lb = a.step_tokens(toks), b.step_tokens(toks)
-    assert np.abs(la - lb).max() <= 5e-3, np.abs(la - lb).max()
-    t = int(np.argmax(lb))
-    for _ in range(6):
-        la, lb = a.step_tokens([t]), b.step_tokens([t])
-        assert np.abs(la - lb).max() <= 5e-3, np.abs(la - lb).max()
-        if top2_margin(lb) > 1e-2:
-            assert int(np.argmax(la)) == int(np.argmax(lb))
-        t = int(np.argmax(lb))
-    # 3- and 8-token chunks (keys of the step's own tokens across a 64-key split boundary)
-    for n in (3, 8):
-        chunk = list(synth.tokens(40 + n, cfg.vocab, n))
-        la, lb = a.step_tokens(chunk, all_rows=True), b.step_tokens(chunk, all_rows=True)
-        assert np.abs(la - lb).max() <= 5e-3, np.abs(la - lb).max()
-    ga = a.generate(t, 12)
-    gb = b.generate(t, 12)
-    assert (ga == gb).mean() >= 0.9
-    a.close()
-    b.close()
-    lm.close()
-
-
-def test_persistent_batch_of_four(device, models):
-    # four sequences reading one token each (one persistent step of 4 tokens) against each alone
-    model = get(models, TINY)
-    lm = device.load_model(model)
-    batch = lm.session(max_context=40, max_seqs=4, persistent=True)
-    alone = [lm.session(max_context=40, persistent=True) for _ in range(4)]
-    prompts = [list(synth.tokens(50 + i, TINY.vocab, 5 + i)) for i in range(4)]
-    for i in range(4):
-        batch.step_batch([i], [prompts[i]])
-        alone[i].step_batch([0], [prompts[i]])
-    nxt = [7, 70, 700, 900]
-    lb, ab = batch.step_batch([0, 1, 2, 3], [[t] for t in nxt])
-    for i in range(4):
-        la, aa = alone[i].step_batch([0], [[nxt[i]]])
-        # every row computes as it does alone: bit for bit
-        assert np.array_equal(lb[i], la[0]) and ab[i] == aa[0]
-    for s in alone:
-        s.close()
-    batch.close()
-    lm.close()
-
-
-def test_persistent_wait_limit_returns_an_error(device, models):
-    # the persistent step's bounded waits: "spin:2000000" gives every wait of the next step a limit
-    # of about 1 ms and makes its first grid barrier wait for an arrival that never comes; the
-    # barrier runs out, the step lets its copies land and returns, the call reports the error, and
-    # after hc_seq_reset the session decodes as a fresh one
-    model = get(models, C2_2L)
-    lm = device.load_model(model)
-    s = lm.session(max_context=64, persistent=True)
-    fresh = lm.session(max_context=64, persistent=True)
-    toks = list(synth.tokens(5, C2_2L.vocab, 4))  # a chunk the persistent step takes
-    A.check(A.lib().hc_set_fault(b"spin:2000000"))
-    with pytest.raises(hb.HcError, match="timed out"):
-        s.step_tokens(toks)
-    with pytest.raises(hb.HcError, match="reset"):
-        s.step_tokens(toks)
-    s.reset()
-    assert np.array_equal(s.step_tokens(toks), fresh.step_tokens(toks))
-    assert np.array_equal(s.step_tokens([11]), fresh.step_tokens([11]))
-    s.close()
-    fresh.close()
-    lm.close()
-
-
 def test_all_rows_and_chunking(device, models):
     # 75 tokens in one call cross the 64-token chunks (a batched chunk, then 11 tokens); every row
     # against the oracle's
@@ -229,28 +152,6 @@ def test_verify_row_equals_one_token_step_bit_for_bit(device, models):
     t = a.greedy(prompt)
     assert b.greedy(prompt) == t
     rng = np.random.default_rng(5)
-    for _ in range(4):
-        drafts = [int(x) for x in rng.integers(C2_2L.vocab, size=4)]
-        kept, nxt, row = a.speculate_tokens([t] + drafts, want_logits=True)
-        want = b.step_tokens([t])
-        assert kept == 1 and np.array_equal(row, want) and nxt == int(np.argmax(want))
-        t = nxt
-    a.close()
-    b.close()
-    lm.close()
-
-
-def test_persistent_verify_row_equals_one_token_step_bit_for_bit(device, models):
-    # in the persistent step the attention splits are fixed by position and every phase has one
-    # summation order, so a verify row reads exactly what a one-token step reads
-    model = get(models, C2_2L)
-    lm = device.load_model(model)
-    a = lm.session(max_context=200, max_step=5, persistent=True)
-    b = lm.session(max_context=200, persistent=True)
-    prompt = list(synth.tokens(43, C2_2L.vocab, 120))  # past the first 64-key split
-    t = a.greedy(prompt)
-    assert b.greedy(prompt) == t
-    rng = np.random.default_rng(6)
     for _ in range(4):
         drafts = [int(x) for x in rng.integers(C2_2L.vocab, size=4)]
         kept, nxt, row = a.speculate_tokens([t] + drafts, want_logits=True)
