@@ -183,8 +183,11 @@ def test_ragged_batch_equals_single_sequences(device, models):
 
 @pytest.mark.parametrize("kv_format", [A.HC_KV_F16, A.HC_KV_INT8_PAGED], ids=["f16", "int8paged"])
 def test_wide_batch_equals_single_sequences(device, models, kv_format):
-    # 20 sequences of ragged contexts decode one token each in one call (the batched GEMV, tokens
-    # on the MMA's n) and read the logits and choices each reads alone (a token a call)
+    # 20 sequences of ragged contexts decode one token each in one call (the tensor-core GEMV, fp16
+    # operands) and read the logits and choices each reads alone (a token a call, the one-token
+    # GEMV's int8 hi/lo activations). The int8 cache turns the operands' rounding differences into
+    # whole quantisation steps now and then, hence its wider bound.
+    tol = 5e-3 if kv_format == A.HC_KV_F16 else 2e-2
     model = get(models, TINY)
     lm = device.load_model(model)
     n = 20
@@ -200,7 +203,7 @@ def test_wide_batch_equals_single_sequences(device, models, kv_format):
         lb, ab = batch.step_batch(list(range(n)), [[t] for t in nxt])
         for i in range(n):
             la, aa = alone[i].step_batch([0], [[nxt[i]]])
-            assert np.abs(synth.f16_values(lb[i]) - synth.f16_values(la[0])).max() <= 5e-3
+            assert np.abs(synth.f16_values(lb[i]) - synth.f16_values(la[0])).max() <= tol
             v = synth.f16_values(la[0])
             if top2_margin(v) > 1e-2:
                 assert ab[i] == aa[0]

@@ -17,6 +17,13 @@ from hwnpu_b200 import synth
 pytestmark = pytest.mark.gpu
 
 TOL = 2e-2
+# At C3's widths the experts requantise their inputs to int8 per 32 values (twice a layer), so the
+# float32 summation-order differences between the GPU and the oracle flip a code by one step now and
+# then; the logits then differ by up to ~0.04 (measured on a B200: 0.013-0.037 over prompts of 8 to
+# 150 ids, cosine >= 0.99996, the same argmax). The oracle itself moves as much between two valid
+# chunkings of one prompt (one pass against pieces of 64: 0.035-0.054). The C3-shaped cases take
+# this bound; the small model keeps 2e-2.
+TOL_Q = 5e-2
 
 # gpt-oss shapes small enough for quick oracle runs: a window of 8 crossed by the prompts
 TINY = synth.Config("tiny-gptoss", 2, 256, 256, 4, 2, 64, 500, A.HC_FMT_MXFP4, norm_scale=False,
@@ -32,10 +39,14 @@ def cosine(a, b):
     return float(a @ b / np.sqrt((a @ a) * (b @ b)))
 
 
-def compare(got, want):
+def compare(got, want, tol=TOL):
     err = np.abs(got - want).max()
-    assert err <= TOL, err
+    assert err <= tol, err
     assert cosine(got, want) >= 0.9999
+
+
+def tol_of(cfg):
+    return TOL_Q if cfg.hidden >= 2048 else TOL
 
 
 def top2_margin(v):
@@ -62,16 +73,17 @@ def test_gptoss_decode_matches_oracle(device, models, cfg, prompt, steps):
     sess = lm.session(max_context=prompt + steps + 4)
     ref = O.OracleSession(model, prompt + steps + 4)
     toks = list(synth.tokens(31, cfg.vocab, prompt))
+    tol = tol_of(cfg)
     got = sess.step_tokens(toks)
     want = synth.f16_values(ref.step(toks)[0])
-    compare(got, want)
+    compare(got, want, tol)
     for _ in range(steps):
-        if top2_margin(want) > 2 * TOL:
+        if top2_margin(want) > 2 * tol:
             assert int(np.argmax(got)) == int(np.argmax(want))
         t = int(np.argmax(want))
         got = sess.step_tokens([t])
         want = synth.f16_values(ref.step([t])[0])
-        compare(got, want)
+        compare(got, want, tol)
     assert sess.pos() == ref.pos() == prompt + steps
     sess.close()
     lm.close()
@@ -94,14 +106,14 @@ def test_gptoss_batch16_matches_oracle(device, models, cfg):
         prompt = list(synth.tokens(50 + i, cfg.vocab, n))
         lg, _ = sess.step_batch([i], [prompt])
         want = synth.f16_values(refs[i].step(prompt)[0])
-        compare(synth.f16_values(lg[0]), want)
+        compare(synth.f16_values(lg[0]), want, tol_of(cfg))
         nxt.append(int(np.argmax(want)))
     for _ in range(3):
         lg, am = sess.step_batch(list(range(16)), [[t] for t in nxt])
         for i in range(16):
             want = synth.f16_values(refs[i].step([nxt[i]])[0])
-            compare(synth.f16_values(lg[i]), want)
-            if top2_margin(want) > 2 * TOL:
+            compare(synth.f16_values(lg[i]), want, tol_of(cfg))
+            if top2_margin(want) > 2 * tol_of(cfg):
                 assert int(am[i]) == int(np.argmax(want))
             nxt[i] = int(np.argmax(want))
     for r in refs[1:]:
