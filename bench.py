@@ -844,6 +844,8 @@ def main():
     ap.add_argument("--rows", type=int, default=12288, help="--workload linear: matrix rows")
     ap.add_argument("--cols", type=int, default=2048, help="--workload linear: matrix columns")
     ap.add_argument("--ntok", type=int, default=64, help="--workload linear: tokens a call")
+    ap.add_argument("--profile", type=int, default=0,
+                    help="--workload linear: also run this many calls between cudaProfilerStart/Stop (for ncu)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))

@@ -6,11 +6,13 @@
 // there are too few row tiles to fill the SMs), and all n tokens: one tcgen05.mma of M = 128,
 // N = n rounded up to 16, K = 16 (kind::f16, float32 accumulator in tensor memory) per 16 columns.
 //
-//   warp 0      producer: bulk copies (cp.async.bulk, no multicast) of each column tile's 8 weight
-//               tiles and of the tokens' fp16 operand into a 2-stage ring (mbarrier complete_tx)
+//   warp 0      producers: lane 0 bulk-copies (cp.async.bulk, no multicast) each column tile's 8
+//               weight tiles into a ring of up to 6 stages, lane 16 the tokens' fp16 operand into a
+//               ring of 2 (an mbarrier with complete_tx per stage)
 //   warp 1      allocates the tensor memory; one lane issues the MMAs and their commits
-//   warps 2..5  dequantise each half column tile of weights from the ring into the MMA's A operand
-//               (fp16, K-major, no swizzle), then run the epilogue from the accumulator
+//   warps 2..17 warps 2 + 2i and 3 + 2i dequantise row tile i of each half column tile from the ring
+//               into the MMA's A operand (fp16, K-major, no swizzle), then, with the
+//               accumulator's lane quarter (warp % 4) and 16 of its columns, run the epilogue
 //
 // Arithmetic. A weight is dequantised with its format's float32 arithmetic (int4: (q - z) s,
 // milcpu shiftScale) and rounded to fp16; int8 codes go in as exact integers and their row scale is
@@ -36,11 +38,16 @@ namespace {
 
 constexpr int kTcRows = 128;                       // rows of a CTA tile: 8 row tiles (the MMA's M)
 constexpr int kTcTiles = kTcRows / kTileRows;      // 8
-constexpr int kTcStages = 2;                       // ring stages, a column tile each
-constexpr int kTcThreads = 6 * 32;
+constexpr int kTcMaxW = 6;                         // most weight ring stages (a column tile's 8 tiles each)
+constexpr int kTcBStages = 2;                      // tokens' operand ring stages (the operand sits in L2)
+constexpr int kTcSmem = 230400;                    // dynamic shared memory a CTA may take
+constexpr int kTcDeq = 16;                         // dequantising warps: two a row tile
+constexpr int kTcThreads = (2 + kTcDeq) * 32;
 constexpr int kTcHalf = kTileCols / 2;             // columns of one A buffer
-constexpr int kTcABytes = kTcRows * kTcHalf * 2;   // 32 KB
-constexpr int kTcStepA = kTcRows * 16 * 2;         // bytes of A per 16 columns (one MMA's K)
+// bytes of A per 16 columns (one MMA's K): 128 rows x 32 bytes, and 16 more so that the 4 K-steps
+// a warp's store instruction touches fall on different banks
+constexpr int kTcStepA = kTcRows * 16 * 2 + 16;
+constexpr int kTcABytes = (kTcHalf / 16) * kTcStepA;
 constexpr int kTcMaxN = 64;
 constexpr long long kTcSpin = 2000000000ll;        // clock cycles a wait may take
 
@@ -70,8 +77,12 @@ __device__ __forceinline__ bool tc_try(uint64_t *b, unsigned parity) {
 // Waits for the phase of the given parity to complete, at most kTcSpin cycles; on running out it
 // records code in *status (the first one) and returns.
 __device__ __forceinline__ void tc_wait(uint64_t *b, unsigned parity, int *status, int code) {
+  if (tc_try(b, parity)) return;
   const long long t0 = clock64();
-  while (!tc_try(b, parity)) {
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (tc_try(b, parity)) return;
     if (clock64() - t0 > kTcSpin) {
       atomicCAS(status, 0, code);
       return;
@@ -135,66 +146,62 @@ __device__ __forceinline__ int tc_aoff(int r, int kl) {
   return (kl >> 4) * kTcStepA + (r >> 3) * 256 + ((kl >> 3) & 1) * 128 + (r & 7) * 16;
 }
 
-// Packs 8 float values rounded to fp16 into 16 bytes.
-__device__ __forceinline__ uint4 tc_pack8(const float (&f)[8]) {
-  uint4 o;
-  __half2 h;
-  h = __floats2half2_rn(f[0], f[1]); o.x = *reinterpret_cast<uint32_t *>(&h);
-  h = __floats2half2_rn(f[2], f[3]); o.y = *reinterpret_cast<uint32_t *>(&h);
-  h = __floats2half2_rn(f[4], f[5]); o.z = *reinterpret_cast<uint32_t *>(&h);
-  h = __floats2half2_rn(f[6], f[7]); o.w = *reinterpret_cast<uint32_t *>(&h);
-  return o;
+// Four byte codes (or nibbles, already shifted into the low half of each byte) of w as two fp16
+// pairs 1024 + code (the exponent trick: fp16 0x6400 | u is 1024 + u for u < 1024).
+__device__ __forceinline__ void tc_magic4(uint32_t w, __half2 &lo, __half2 &hi) {
+  const uint32_t a = prmt(w, 0x64646464u, 0x5140u), b = prmt(w, 0x64646464u, 0x7362u);
+  lo = *reinterpret_cast<const __half2 *>(&a);
+  hi = *reinterpret_cast<const __half2 *>(&b);
 }
-
-// float(q) of the byte (or nibble) codes 0..255 by the exponent trick (exact).
-__device__ __forceinline__ float tc_u2f(uint32_t q) { return __uint_as_float(0x4B000000u | q) - 8388608.0f; }
+__device__ __forceinline__ uint32_t tc_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 
 // Half h (columns 128h .. 128h + 127) of one repacked 16 x 256 tile into the A buffer at rows
-// 16 i .. 16 i + 15. The tile's 16-byte pieces (common.h's tile_pos): piece (o, lane = 4 g + c)
-// holds rows g and g + 8, elements 8o .. 8o + 7 of group c (and, int4, group c + 4 in the high
-// nibbles; int8: pieces 4h + o). A thread takes 4 pieces (o = 0..3) of one lane; the lanes of a
-// warp are ordered so that 8 consecutive threads write one 128-byte run.
+// 16 i .. 16 i + 15, by one warp. The tile's 16-byte pieces (common.h's tile_pos): piece (o, lane =
+// 4 g + c) holds rows g and g + 8 (words 0, 2 and 1, 3), elements 8o .. 8o + 7 of group c (and, int4,
+// group c + 4 in the high nibbles; int8: pieces 4h + o). Lane (g, c) takes pieces o0 and o0 + 1 and
+// writes 8 fp16 values a row a piece. int4: (q - z) s with fp16 arithmetic (q exact, then two roundings);
+// int8: the code itself (exact), the row scale comes in the epilogue.
 template <int KIND>
 __device__ __forceinline__ void tc_dequant_half(const uint8_t *__restrict__ tile, int h, uint8_t *abuf, int i,
-                                                int lane_ord, bool present) {
-  const int lane = 4 * (lane_ord & 7) + (lane_ord >> 3);  // lane (g, c) of the tile's layout
+                                                int lane, int o0, bool present) {
   const int g = lane >> 2, c = lane & 3;
-  float s0 = 0.f, z0 = 0.f, s1 = 0.f, z1 = 0.f;
+  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));  // 1024
+  const __half2 k1152 = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1024 + 128
+  __half2 s0 = k1024, s1 = k1024, z0 = k1024, z1 = k1024;
   if (KIND == kKindInt4 && present) {
     const uint4 sz = *reinterpret_cast<const uint4 *>(tile + kTileCodes4 + lane * 16);
-    const uint32_t sw = h ? sz.y : sz.x, zw = h ? sz.w : sz.z;  // (s, s) of rows g, g + 8 at half h
-    s0 = __half2float(__ushort_as_half(uint16_t(sw & 0xFFFF)));
-    s1 = __half2float(__ushort_as_half(uint16_t(sw >> 16)));
-    z0 = __half2float(__ushort_as_half(uint16_t(zw & 0xFFFF)));
-    z1 = __half2float(__ushort_as_half(uint16_t(zw >> 16)));
+    const uint32_t sw = h ? sz.y : sz.x, zw = h ? sz.w : sz.z;  // (s of row g, row g + 8) at half h
+    s0 = __half2half2(__ushort_as_half(uint16_t(sw & 0xFFFF)));
+    s1 = __half2half2(__ushort_as_half(uint16_t(sw >> 16)));
+    z0 = __half2half2(__ushort_as_half(uint16_t(zw & 0xFFFF)));
+    z1 = __half2half2(__ushort_as_half(uint16_t(zw >> 16)));
   }
 #pragma unroll
-  for (int o = 0; o < 4; ++o) {
+  for (int o = o0; o < o0 + 2; ++o) {
     uint4 out0 = make_uint4(0, 0, 0, 0), out1 = make_uint4(0, 0, 0, 0);
     if (present) {
       const int piece = KIND == kKindInt8 ? 4 * h + o : o;
       const uint4 w = *reinterpret_cast<const uint4 *>(tile + (piece * 32 + lane) * 16);
-      float a[8], b[8];
-      if (KIND == kKindInt8) {
+      const uint32_t words[4] = {w.x, w.z, w.y, w.w};  // row g: e8 0-3, 4-7; row g + 8: e8 0-3, 4-7
+      uint32_t r[8];
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          a[p] = float(int8_t((w.x >> (8 * p)) & 0xFF));
-          a[4 + p] = float(int8_t((w.z >> (8 * p)) & 0xFF));
-          b[p] = float(int8_t((w.y >> (8 * p)) & 0xFF));
-          b[4 + p] = float(int8_t((w.w >> (8 * p)) & 0xFF));
+      for (int k = 0; k < 4; ++k) {
+        __half2 lo, hi;
+        if (KIND == kKindInt8) {
+          tc_magic4(words[k] ^ 0x80808080u, lo, hi);  // 1024 + (code + 128)
+          lo = __hsub2(lo, k1152);
+          hi = __hsub2(hi, k1152);
+        } else {
+          tc_magic4((words[k] >> (4 * h)) & 0x0F0F0F0Fu, lo, hi);
+          const __half2 zz = k < 2 ? z0 : z1, ss = k < 2 ? s0 : s1;
+          lo = __hmul2(__hsub2(__hsub2(lo, k1024), zz), ss);
+          hi = __hmul2(__hsub2(__hsub2(hi, k1024), zz), ss);
         }
-      } else {
-        const int sh = 4 * h;
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          a[p] = __fmul_rn(__fsub_rn(tc_u2f((w.x >> (8 * p + sh)) & 15u), z0), s0);
-          a[4 + p] = __fmul_rn(__fsub_rn(tc_u2f((w.z >> (8 * p + sh)) & 15u), z0), s0);
-          b[p] = __fmul_rn(__fsub_rn(tc_u2f((w.y >> (8 * p + sh)) & 15u), z1), s1);
-          b[4 + p] = __fmul_rn(__fsub_rn(tc_u2f((w.w >> (8 * p + sh)) & 15u), z1), s1);
-        }
+        r[2 * k] = tc_bits(lo);
+        r[2 * k + 1] = tc_bits(hi);
       }
-      out0 = tc_pack8(a);
-      out1 = tc_pack8(b);
+      out0 = make_uint4(r[0], r[1], r[2], r[3]);
+      out1 = make_uint4(r[4], r[5], r[6], r[7]);
     }
     const int kl = 32 * c + 8 * o;
     *reinterpret_cast<uint4 *>(abuf + tc_aoff(16 * i + g, kl)) = out0;
@@ -206,38 +213,93 @@ struct TcArgs {
   const uint8_t *tiles;
   const float *row_scale, *bias;
   const uint8_t *xop;  // the tokens' fp16 operand: per column tile npad x 256 values (act_quant)
-  int rtiles, ktiles, rows, tile_bytes, ntok, npad, splits;
+  int rtiles, ktiles, rows, tile_bytes, ntok, npad, splits, wstages;
   GemvOut out;
   int *status;
 };
 
 __device__ int tc_status_word;  // the first wait that ran out in any launch (0: none)
 
-// The epilogue's named barrier over the four dequant warps.
-__device__ __forceinline__ void tc_epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// The epilogue's named barrier over the dequantising warps.
+__device__ __forceinline__ void tc_epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kTcDeq * 32) : "memory"); }
+
+// The last steps of 16 tokens t0 .. t0 + 15 of tile row `row` (this thread's row; the lanes of a
+// warp hold 32 consecutive rows): row scale, bias, and the output mode.
+template <int KIND>
+__device__ __forceinline__ void tc_finish(const TcArgs &a, int row, int lane, int mt, int t0, float (&v)[16]) {
+  const GemvOut &out = a.out;
+  const bool valid = row < a.rtiles * kTileRows;
+  float scale = 1.f, bias = 0.f;
+  if (valid && KIND == kKindInt8) scale = a.row_scale[row];
+  if (valid && a.bias) bias = a.bias[row];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) v[e] = v[e] * scale + bias;
+  if (out.mode == kGlu) {
+    // tile rows 0-7 gate, 8-15 up: lane l (l % 16 < 8) pairs with lane l + 8
+    const int r16 = lane & 15, o = (row >> 4) * (kTileRows / 2) + r16;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float u = __shfl_down_sync(0xffffffffu, v[e], 8);
+      if (t0 + e < a.ntok && valid && r16 < 8 && o < a.rows) {
+        const float gv = v[e];
+        // blocks.SiLU: x / (1 + exp(-x)) (internal/llm/blocks/blocks.go:395-399)
+        out.y[size_t(t0 + e) * out.ldy + o] = gv / (1.0f + expf(-gv)) * u;
+      }
+    }
+  } else if (out.mode == kLogits) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      unsigned long long key = 0ull;
+      if (t0 + e < a.ntok && valid && row < a.rows) {
+        const uint16_t hb = __half_as_ushort(__float2half_rn(v[e]));
+        if (out.logits) out.logits[size_t(t0 + e) * out.ldy + row] = hb;
+        key = argmax_key(hb, uint32_t(row));
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) {
+        const unsigned long long o2 = __shfl_xor_sync(0xffffffffu, key, off);
+        key = o2 > key ? o2 : key;
+      }
+      if (lane == 0 && key) atomicMax(&out.amax[(t0 + e) * kAmaxSlots + (mt % kAmaxSlots)], key);
+    }
+  } else if (valid && row < a.rows) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      if (t0 + e >= a.ntok) continue;
+      float *p = out.y + size_t(t0 + e) * out.ldy + row;
+      *p = out.mode == kAdd ? *p + v[e] : v[e];
+    }
+  }
+}
 
 template <int KIND>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t tc_smem[];
-  __shared__ uint64_t full[kTcStages], empty[kTcStages], afull[2], aempty[2], done;
+  __shared__ uint64_t wfull[kTcMaxW], wempty[kTcMaxW], bfull[kTcBStages], bempty[kTcBStages];
+  __shared__ uint64_t afull[2], aempty[2], done;
   __shared__ uint32_t tmem_base;
   __shared__ int last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mt = blockIdx.x / a.splits, sp = blockIdx.x % a.splits;
   const int per = a.ktiles / a.splits, rem = a.ktiles % a.splits;
   const int kt0 = sp * per + min(sp, rem), nkt = per + (sp < rem ? 1 : 0);
+  const int WS = a.wstages;
   const int raw_bytes = kTcTiles * a.tile_bytes, b_bytes = a.npad * kTileCols * 2;
   uint8_t *raw = tc_smem;
-  uint8_t *bop = raw + kTcStages * raw_bytes;
-  uint8_t *aop = bop + kTcStages * b_bytes;
+  uint8_t *bop = raw + WS * raw_bytes;
+  uint8_t *aop = bop + kTcBStages * b_bytes;
   pdl_trigger();
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
-      tc_bar_init(&full[s], 1);
-      tc_bar_init(&empty[s], 5);  // the 4 dequant warps (weights read) + the MMA commit (tokens read)
+    for (int s = 0; s < WS; ++s) {
+      tc_bar_init(&wfull[s], 1);
+      tc_bar_init(&wempty[s], kTcDeq);  // the dequantising warps have read the stage
+    }
+    for (int s = 0; s < kTcBStages; ++s) {
+      tc_bar_init(&bfull[s], 1);
+      tc_bar_init(&bempty[s], 1);  // the MMA commit
     }
     for (int h = 0; h < 2; ++h) {
-      tc_bar_init(&afull[h], 4);
+      tc_bar_init(&afull[h], kTcDeq);
       tc_bar_init(&aempty[h], 1);
     }
     tc_bar_init(&done, 1);
@@ -255,22 +317,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
   const uint32_t tmem = tmem_base;
 
   if (warp == 0) {
-    // producer: the 8 weight tiles and the tokens' operand of each column tile
     if (lane == 0) {
+      // the weights: the 8 tiles of each column tile, WS column tiles ahead
       int present = 0;
       for (int i = 0; i < kTcTiles; ++i) present += mt * kTcTiles + i < a.rtiles;
       for (int j = 0; j < nkt; ++j) {
-        const int s = j % kTcStages, kt = kt0 + j;
-        if (j >= kTcStages) tc_wait(&empty[s], ((j / kTcStages) - 1) & 1, a.status, 1);
-        tc_expect_tx(&full[s], unsigned(present * a.tile_bytes + b_bytes));
+        const int s = j % WS, kt = kt0 + j;
+        if (j >= WS) tc_wait(&wempty[s], ((j / WS) - 1) & 1, a.status, 1);
+        tc_expect_tx(&wfull[s], unsigned(present * a.tile_bytes));
         for (int i = 0; i < kTcTiles; ++i) {
           const int rt = mt * kTcTiles + i;
           if (rt < a.rtiles)
             tc_bulk(raw + s * raw_bytes + i * a.tile_bytes, a.tiles + (size_t(rt) * a.ktiles + kt) * a.tile_bytes,
-                    unsigned(a.tile_bytes), &full[s]);
+                    unsigned(a.tile_bytes), &wfull[s]);
         }
-        if (j == 0) pdl_wait();  // the operand is the previous kernel's output
-        tc_bulk(bop + s * b_bytes, a.xop + size_t(kt) * b_bytes, unsigned(b_bytes), &full[s]);
+      }
+    } else if (lane == 16) {
+      // the tokens' operand (the previous kernel's output), two column tiles ahead
+      pdl_wait();
+      for (int j = 0; j < nkt; ++j) {
+        const int s = j % kTcBStages, kt = kt0 + j;
+        if (j >= kTcBStages) tc_wait(&bempty[s], ((j / kTcBStages) - 1) & 1, a.status, 7);
+        tc_expect_tx(&bfull[s], unsigned(b_bytes));
+        tc_bulk(bop + s * b_bytes, a.xop + size_t(kt) * b_bytes, unsigned(b_bytes), &bfull[s]);
       }
     }
   } else if (warp == 1) {
@@ -279,8 +348,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
       const uint32_t idesc = tc_idesc(a.npad);
       int acc = 0;
       for (int j = 0; j < nkt; ++j) {
-        const int s = j % kTcStages;
-        tc_wait(&full[s], (j / kTcStages) & 1, a.status, 2);
+        const int s = j % kTcBStages;
+        tc_wait(&bfull[s], (j / kTcBStages) & 1, a.status, 2);
         for (int h = 0; h < 2; ++h) {
           tc_wait(&afull[h], j & 1, a.status, 3);
           tc_fence_after();
@@ -295,116 +364,74 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
           }
           tc_commit(&aempty[h]);
         }
-        tc_commit(&empty[s]);
+        tc_commit(&bempty[s]);
       }
       tc_commit(&done);
     }
   } else {
-    // dequantisation (warps 2..5), then the epilogue
-    const int dw = warp - 2;
+    // dequantisation (warps 2 + 2i and 3 + 2i: row tile i, pieces 0-1 and 2-3), then the epilogue
+    const int dw = warp - 2, ti = dw >> 1;
+    const bool present = mt * kTcTiles + ti < a.rtiles;
     for (int j = 0; j < nkt; ++j) {
-      const int s = j % kTcStages;
-      tc_wait(&full[s], (j / kTcStages) & 1, a.status, 4);
-      const uint8_t *rs = raw + s * raw_bytes;
+      const int s = j % WS;
+      tc_wait(&wfull[s], (j / WS) & 1, a.status, 4);
+      const uint8_t *tile = raw + s * raw_bytes + ti * a.tile_bytes;
       for (int h = 0; h < 2; ++h) {
         if (j >= 1) tc_wait(&aempty[h], (j - 1) & 1, a.status, 5);
-        uint8_t *ab = aop + h * kTcABytes;
-        for (int i = dw; i < kTcTiles; i += 4)
-          tc_dequant_half<KIND>(rs + i * a.tile_bytes, h, ab, i, lane, mt * kTcTiles + i < a.rtiles);
+        tc_dequant_half<KIND>(tile, h, aop + h * kTcABytes, ti, lane, 2 * (dw & 1), present);
         tc_fence_proxy();
         __syncwarp();
         if (lane == 0) tc_arrive(&afull[h]);
       }
       __syncwarp();
-      if (lane == 0) tc_arrive(&empty[s]);
+      if (lane == 0) tc_arrive(&wempty[s]);
     }
     tc_wait(&done, 0, a.status, 6);
     tc_fence_after();
-    // this warp's quarter of the accumulator: rows 32 q + lane, all npad columns (tokens)
-    const int q = warp & 3;
-    const int rl = 32 * q + lane;
-    float v[kTcMaxN];
-#pragma unroll
-    for (int c = 0; c < kTcMaxN / 16; ++c) {
-      if (c * 16 < a.npad) {
-        float t16[16];
-        tc_ld16(tmem + (uint32_t(32 * q) << 16) + uint32_t(16 * c), t16);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[16 * c + e] = t16[e];
-      }
-    }
     pdl_wait();
+    // this warp's quarter of the accumulator (rows 32 q + lane) and 16 of its columns (tokens)
+    const int q = warp & 3, t0 = 16 * (dw >> 2);
+    const int row = mt * kTcRows + 32 * q + lane;  // tile row index (16 rows a tile)
+    const uint32_t taddr = tmem + (uint32_t(32 * q) << 16) + uint32_t(t0);
     const int rows_pad = (gridDim.x / a.splits) * kTcRows;
-    const int row = mt * kTcRows + rl;  // tile row index (16 rows a tile)
-    if (a.splits > 1) {
-      float *w = a.out.ws + size_t(sp) * kTcMaxN * rows_pad + row;
+    const bool mine = t0 < a.npad;  // uniform over the warp
+    if (a.splits == 1) {
+      if (mine) {
+        float v[16];
+        tc_ld16(taddr, v);
+        tc_finish<KIND>(a, row, lane, mt, t0, v);
+      }
+    } else {
+      if (mine) {
+        float v[16];
+        tc_ld16(taddr, v);
+        float *w = a.out.ws + size_t(sp) * kTcMaxN * rows_pad + row;
 #pragma unroll
-      for (int t = 0; t < kTcMaxN; ++t)
-        if (t < a.ntok) w[size_t(t) * rows_pad] = v[t];
+        for (int e = 0; e < 16; ++e)
+          if (t0 + e < a.ntok) w[size_t(t0 + e) * rows_pad] = v[e];
+      }
       __threadfence();
       tc_epi_sync();
       if (dw == 0 && lane == 0) last = atomicAdd(&a.out.tickets[mt], 1) == a.splits - 1;
       tc_epi_sync();
-      if (!last) goto teardown;
-      __threadfence();
+      if (last) {
+        __threadfence();
+        if (mine) {
+          float v[16];
 #pragma unroll
-      for (int t = 0; t < kTcMaxN; ++t) {
-        if (t < a.ntok) {
-          float acc = 0.f;
-          for (int k = 0; k < a.splits; ++k) acc += __ldcg(a.out.ws + (size_t(k) * kTcMaxN + t) * rows_pad + row);
-          v[t] = acc;
-        }
-      }
-      if (dw == 0 && lane == 0) a.out.tickets[mt] = 0;  // for the next launch
-    }
-    {
-      const GemvOut &out = a.out;
-      const bool valid = row < a.rtiles * kTileRows;
-      float scale = 1.f, bias = 0.f;
-      if (valid && KIND == kKindInt8) scale = a.row_scale[row];
-      if (valid && a.bias) bias = a.bias[row];
-#pragma unroll
-      for (int t = 0; t < kTcMaxN; ++t) v[t] = v[t] * scale + bias;
-      if (out.mode == kGlu) {
-        // tile rows 0-7 gate, 8-15 up: lane l (l % 16 < 8) pairs with lane l + 8
-        const int r16 = lane & 15, o = (row >> 4) * (kTileRows / 2) + r16;
-#pragma unroll
-        for (int t = 0; t < kTcMaxN; ++t) {
-          const float u = __shfl_down_sync(0xffffffffu, v[t], 8);
-          if (t < a.ntok && valid && r16 < 8 && o < a.rows) {
-            const float gv = v[t];
-            // blocks.SiLU: x / (1 + exp(-x)) (internal/llm/blocks/blocks.go:395-399)
-            out.y[size_t(t) * out.ldy + o] = gv / (1.0f + expf(-gv)) * u;
+          for (int e = 0; e < 16; ++e) {
+            float acc = 0.f;
+            if (t0 + e < a.ntok)
+              for (int k = 0; k < a.splits; ++k)
+                acc += __ldcg(a.out.ws + (size_t(k) * kTcMaxN + t0 + e) * rows_pad + row);
+            v[e] = acc;
           }
+          tc_finish<KIND>(a, row, lane, mt, t0, v);
         }
-      } else if (out.mode == kLogits) {
-#pragma unroll
-        for (int t = 0; t < kTcMaxN; ++t) {
-          if (t >= a.ntok) continue;
-          unsigned long long key = 0ull;
-          if (valid && row < a.rows) {
-            const uint16_t hb = __half_as_ushort(__float2half_rn(v[t]));
-            if (out.logits) out.logits[size_t(t) * out.ldy + row] = hb;
-            key = argmax_key(hb, uint32_t(row));
-          }
-#pragma unroll
-          for (int off = 16; off; off >>= 1) {
-            const unsigned long long o2 = __shfl_xor_sync(0xffffffffu, key, off);
-            key = o2 > key ? o2 : key;
-          }
-          if (lane == 0 && key) atomicMax(&out.amax[t * kAmaxSlots + (mt % kAmaxSlots)], key);
-        }
-      } else if (valid && row < a.rows) {
-#pragma unroll
-        for (int t = 0; t < kTcMaxN; ++t) {
-          if (t >= a.ntok) continue;
-          float *p = out.y + size_t(t) * out.ldy + row;
-          *p = out.mode == kAdd ? *p + v[t] : v[t];
-        }
+        if (dw == 0 && lane == 0) a.out.tickets[mt] = 0;  // for the next launch
       }
     }
   }
-teardown:
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -413,8 +440,14 @@ teardown:
   }
 }
 
+// The weight stages that fit beside the operand ring and the A buffers, and the shared memory.
+int tc_wstages(int tile_bytes, int npad) {
+  const int room = kTcSmem - kTcBStages * npad * kTileCols * 2 - 2 * kTcABytes;
+  return std::min(kTcMaxW, room / (kTcTiles * tile_bytes));
+}
 size_t tc_smem_bytes(int tile_bytes, int npad) {
-  return size_t(kTcStages) * (kTcTiles * tile_bytes + npad * kTileCols * 2) + 2 * kTcABytes;
+  return size_t(tc_wstages(tile_bytes, npad)) * kTcTiles * tile_bytes + size_t(kTcBStages) * npad * kTileCols * 2 +
+         2 * kTcABytes;
 }
 
 }  // namespace
@@ -427,7 +460,7 @@ char *tc_gemm_prepare() {
   int dev = 0;
   HC_TRY_CUDA(cudaGetDevice(&dev));
   HC_TRY_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&g_tc_status[dev & 63]), tc_status_word));
-  const int mx = int(tc_smem_bytes(kTileCodes8, kTcMaxN));
+  const int mx = kTcSmem;
   HC_TRY_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<kKindInt8>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx));
   HC_TRY_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<kKindInt4>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx));
   return nullptr;
@@ -439,8 +472,9 @@ int tc_splits(const DevMat &W, int sms, size_t ws_floats) {
   long best_cost = -1;
   for (int s = 1; s <= std::min(W.ktiles, 16); ++s) {
     if (s > 1 && size_t(s) * kTcMaxN * mtiles * kTcRows > ws_floats) break;
+    // a CTA's fixed cost (the first copies' latency, the epilogue) is about two column tiles'
     const long waves = (long(mtiles) * s + sms - 1) / sms;
-    const long cost = waves * ((W.ktiles + s - 1) / s);
+    const long cost = waves * ((W.ktiles + s - 1) / s + 2);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = s;
@@ -457,7 +491,7 @@ void tc_gemm(const DevMat &W, const uint8_t *xop, int ntok, const GemvOut &out, 
   cudaGetDevice(&dev);
   int *status = g_tc_status[dev & 63];
   const TcArgs a{W.tiles, W.row_scale, W.bias, xop, W.rtiles, W.ktiles, W.rows, W.tile_bytes, ntok, npad, splits,
-                 out, status};
+                 tc_wstages(W.tile_bytes, npad), out, status};
   const size_t smem = tc_smem_bytes(W.tile_bytes, npad);
   if (W.kind == kKindInt8)
     launch_pdl(tc_gemm_kernel<kKindInt8>, dim3(mtiles * splits), dim3(kTcThreads), smem, st, a);
