@@ -438,6 +438,14 @@ def run_c5(args, lm, world, rank, dist, K, W):
         return dec, prm, dev_ms, kv
 
     run(W, False)
+    if args.profile:  # --profile N: N more steps between cudaProfilerStart/Stop (for ncu), no timing
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        run(args.profile, False)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        sess.close()
+        return None
     launches0 = sess.stats()["launches"]
     if dist:
         dist.barrier()
@@ -484,6 +492,8 @@ def run_default(args, rank, world, local, dist):
     clocks.start()
     c5 = run_c5(args, lm, world, rank, dist, K, W)
     clk = clocks.stop()
+    if c5 is None:
+        return
     bs1 = run_bs1(args, lm, model, dev, world, dist, K, W)
     # the dominant kernel class of the C5 step: the batched GEMV (64 tokens on the MMA's n), on the
     # largest matrix of a layer (gate/up, 12288 x 2048)
@@ -845,7 +855,8 @@ def main():
     ap.add_argument("--cols", type=int, default=2048, help="--workload linear: matrix columns")
     ap.add_argument("--ntok", type=int, default=64, help="--workload linear: tokens a call")
     ap.add_argument("--profile", type=int, default=0,
-                    help="--workload linear: also run this many calls between cudaProfilerStart/Stop (for ncu)")
+                    help="--workload linear / c5: run this many calls (steps) between cudaProfilerStart/Stop "
+                         "after the warm-up, for ncu (c5: then exit without timing)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))

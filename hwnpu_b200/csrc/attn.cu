@@ -169,7 +169,13 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
       r.ks = __half2float(__ushort_as_half(pk.kscale[ph]));
       r.vs = __half2float(__ushort_as_half(pk.vscale[ph]));
       kp = reinterpret_cast<const uint32_t *>(pk.k + (ph * kPage + j % kPage) * HD + l8 * E);
-      vp = reinterpret_cast<const uint32_t *>(pk.v + (ph * kPage + j % kPage) * HD + l8 * E);
+      // the page's values are transposed ([dim][position]): this lane's E dims of key j, a byte each
+      const int8_t *vb = pk.v + ph * kPage * HD + size_t(l8 * E) * kPage + j % kPage;
+#pragma unroll
+      for (int i = 0; i < KW; ++i)
+        r.v[i] = uint32_t(uint8_t(vb[(4 * i) * kPage])) | (uint32_t(uint8_t(vb[(4 * i + 1) * kPage])) << 8) |
+                 (uint32_t(uint8_t(vb[(4 * i + 2) * kPage])) << 16) | (uint32_t(uint8_t(vb[(4 * i + 3) * kPage])) << 24);
+      vp = nullptr;
     } else {
       int sl = slot0 + (j - k0);
       if (sl >= g.cap) sl -= g.cap;
@@ -179,16 +185,22 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float *__restrict
     if (KW % 4 == 0) {
 #pragma unroll
       for (int i = 0; i < KW / 4; ++i) {
-        const uint4 a = reinterpret_cast<const uint4 *>(kp)[i], b = reinterpret_cast<const uint4 *>(vp)[i];
+        const uint4 a = reinterpret_cast<const uint4 *>(kp)[i];
         r.k[4 * i] = a.x; r.k[4 * i + 1] = a.y; r.k[4 * i + 2] = a.z; r.k[4 * i + 3] = a.w;
-        r.v[4 * i] = b.x; r.v[4 * i + 1] = b.y; r.v[4 * i + 2] = b.z; r.v[4 * i + 3] = b.w;
+        if (!PAGED) {
+          const uint4 b = reinterpret_cast<const uint4 *>(vp)[i];
+          r.v[4 * i] = b.x; r.v[4 * i + 1] = b.y; r.v[4 * i + 2] = b.z; r.v[4 * i + 3] = b.w;
+        }
       }
     } else {
 #pragma unroll
       for (int i = 0; i < KW / 2; ++i) {
-        const uint2 a = reinterpret_cast<const uint2 *>(kp)[i], b = reinterpret_cast<const uint2 *>(vp)[i];
+        const uint2 a = reinterpret_cast<const uint2 *>(kp)[i];
         r.k[2 * i] = a.x; r.k[2 * i + 1] = a.y;
-        r.v[2 * i] = b.x; r.v[2 * i + 1] = b.y;
+        if (!PAGED) {
+          const uint2 b = reinterpret_cast<const uint2 *>(vp)[i];
+          r.v[2 * i] = b.x; r.v[2 * i + 1] = b.y;
+        }
       }
     }
   };
@@ -327,6 +339,7 @@ void qkv_post(const float *qkv, const StepTok *toks, int ntok, const AttnGeom &g
 void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g,
                 const uint16_t *kcache, const uint16_t *vcache, int splits, float *part_ml,
                 float *part_o, cudaStream_t st, const PagedKV *paged, const float *kv_stage) {
+  if (paged && attn_paged_tc(q, toks, ntok, g, *paged, splits, part_ml, part_o, kv_stage, st)) return;
   dim3 grid(splits, g.kv_heads, ntok);
   const int rep = g.heads / g.kv_heads;
   const PagedKV pk = paged ? *paged : PagedKV{};
@@ -384,11 +397,11 @@ __global__ void __launch_bounds__(128) kv_append_int8_kernel(const float *__rest
     if (m / 127.0f > s_old) {
       s_new = __half2float(__float2half_ru(m / 127.0f));
       if (off > 0 && s_old > 0.f) {
-        // requantise the page's earlier rows to the larger scale
-        // (rows 0..off-1 are contiguous: 16 bytes a lane a pass, at most 4 passes)
+        // requantise the page's earlier rows to the larger scale: the whole page (16 bytes a lane
+        // a pass); rows not written yet are rewritten when their turn comes
         const float f = s_old / s_new;
         uint4 *rows = reinterpret_cast<uint4 *>(pool + ph * kPage * HD);
-        const int n16 = off * HD / 16;
+        const int n16 = kPage * HD / 16;
 #pragma unroll 4
         for (int i = lane; i < n16; i += 32) {
           uint4 w = rows[i];
@@ -408,11 +421,15 @@ __global__ void __launch_bounds__(128) kv_append_int8_kernel(const float *__rest
       }
       if (lane == 0) scales[ph] = __half_as_ushort(__float2half_rn(s_new));
     }
-    int8_t *row = pool + (ph * kPage + off) * HD;
     const float inv = s_new > 0.f ? 1.0f / s_new : 0.f;
+    int8_t *pg = pool + ph * kPage * HD;
 #pragma unroll
-    for (int k = 0; k < E; ++k)
-      row[lane + 32 * k] = int8_t(fminf(fmaxf(rintf(x[k] * inv), -127.f), 127.f));
+    for (int k = 0; k < E; ++k) {
+      const int8_t q = int8_t(fminf(fmaxf(rintf(x[k] * inv), -127.f), 127.f));
+      // keys row-major [position][dim]; values transposed [dim][position] (kPagedV)
+      if (is_v) pg[(lane + 32 * k) * kPage + off] = q;
+      else pg[off * HD + lane + 32 * k] = q;
+    }
     __syncwarp();
   }
 }

@@ -522,6 +522,7 @@ char *gemv_prepare() {
 #undef HC_SET_K
 #undef HC_SET
   if (char *e = tc_gemm_prepare()) return e;
+  if (char *e = attn_tc_prepare()) return e;
   HC_TRY_CUDA(cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev));
   done[dev] = true;
   return nullptr;

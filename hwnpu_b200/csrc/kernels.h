@@ -65,9 +65,14 @@ struct GemvOut {
 //  kActF16         fp16 values in the tensor-core GEMV's operand layout (tcgemm.cu): per column tile
 //                  npad x 256 values, npad = ntok rounded up to 16, padding rows zero
 enum ActLayout : int { kActAuto = 0, kActTokenMajor = 1, kActF16 = 2 };
-// The layout gemv() reads for W at ntok tokens: 9..64 tokens of int8 / int4 go to the tensor cores.
+// The layout gemv() reads for W at ntok tokens: 9..64 tokens of int8 / int4 matrices of at least
+// kTcMinRows rows go to the tensor cores. Below that a matrix has too few 128-row tiles to fill
+// the SMs, and the split-K reduction across CTAs costs more than the tensor cores save (measured on
+// B200 at 64 tokens: 2,048 x 2,048 takes 11.7 us on the MMA-sync GEMV against 19.4 us, 4,096 x 2,048
+// 19.3 us against 16.4 us).
+constexpr int kTcMinRows = 4096;
 inline ActLayout act_layout(const DevMat &W, int ntok) {
-  return ntok > 8 && W.kind != kKindMx ? kActF16 : kActAuto;
+  return ntok > 8 && W.kind != kKindMx && W.rows >= kTcMinRows ? kActF16 : kActAuto;
 }
 inline int tc_npad(int ntok) { return (ntok + 15) / 16 * 16; }
 
@@ -128,9 +133,10 @@ struct AttnGeom {
 // RMS norm of q and k (when qn/kn are set), RoPE with the fp16 tables rope[pos][hd/2] (cos, sin
 // pairs as fp16 bits), q into q_out (float32 [ntok][heads][hd]) and k, v as fp16 into the
 // cache at (slot, kv_head, pos).
-// The paged int8 KV cache of one layer (HC_KV_INT8_PAGED): pages of kPage positions, each
-// [kv_heads][kPage][hd] int8 for keys and values, an fp16 scale per (page, head) for each, and
-// the block table [slots][max_pages] of page ids.
+// The paged int8 KV cache of one layer (HC_KV_INT8_PAGED): pages of kPage positions, per (page,
+// kv head) the keys [kPage][hd] int8 (a position's row contiguous) and the values transposed,
+// [hd][kPage] (a dimension's 16 positions contiguous: the operand the attention's P.V integer MMA
+// reads), an fp16 scale per (page, head) for each, and the block table [slots][max_pages].
 constexpr int kPage = 16;
 struct PagedKV {
   const int8_t *k = nullptr, *v = nullptr;
@@ -157,6 +163,12 @@ void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g
                 const uint16_t *kcache, const uint16_t *vcache, int splits, float *part_ml,
                 float *part_o, cudaStream_t st, const PagedKV *paged = nullptr,
                 const float *kv_stage = nullptr);
+
+// attn_split over the paged int8 cache on the integer tensor cores (attn_tc.cu), for head_dim 64 or
+// 128 and 1, 2 or 4 heads a kv head; false (nothing launched) for other shapes.
+bool attn_paged_tc(const float *q, const StepTok *toks, int ntok, const AttnGeom &g, const PagedKV &pk, int splits,
+                   float *part_ml, float *part_o, const float *kv_stage, cudaStream_t st);
+char *attn_tc_prepare();
 
 // Embedding rows of the step's tokens into x (float32 [ntok][hidden]): from an fp16 table, or
 // (table nullptr) from the tied head's tiles, dequantised and rounded to fp16. Also resets amax.

@@ -44,6 +44,7 @@ namespace {
 constexpr int kMaxSplits = 64;
 constexpr int kTcTickets = 4096;  // row tiles of 128 rows a tensor-core GEMV may have (524,288 rows)
 constexpr int kSplitKeys = 1024;  // keys a split reads, at most, for the chunk's longest context
+constexpr int kSplitKeysPaged = 1024;  // the same over the paged int8 cache
 
 // Attention splits of every (token, kv head) of a chunk of n tokens whose longest context is
 // max_len positions: enough CTAs to fill the SMs twice (as for one token when n <= 8), and at
@@ -53,9 +54,12 @@ int splits_for(const hc_session *s, int n, int max_len) {
   const int kv = int(s->m->d.kv_heads);
   // up to 8 tokens take the one-token count, so that a speculative verify row, or any row of a
   // small batch, is computed exactly as a one-token step (hc_generate) computes it
-  int sp = (2 * s->m->sms) / (kv * (n <= 8 ? 1 : n));
+  const int rows = kv * (n <= 8 ? 1 : n);
+  // the paged cache's tensor-core kernel: 4 warps a split, 3 CTAs a SM
+  const bool wide = s->paged;
+  int sp = ((wide ? 3 : 2) * s->m->sms) / rows;
   int by_len = 1;
-  while (by_len < kMaxSplits && by_len * kSplitKeys < max_len) by_len *= 2;
+  while (by_len < kMaxSplits && by_len * (wide ? kSplitKeysPaged : kSplitKeys) < max_len) by_len *= 2;
   return std::max(1, std::min(kMaxSplits, std::max(sp, by_len)));
 }
 

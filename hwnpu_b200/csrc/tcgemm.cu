@@ -6,9 +6,10 @@
 // there are too few row tiles to fill the SMs), and all n tokens: one tcgen05.mma of M = 128,
 // N = n rounded up to 16, K = 16 (kind::f16, float32 accumulator in tensor memory) per 16 columns.
 //
-//   warp 0      producers: lane 0 bulk-copies (cp.async.bulk, no multicast) each column tile's 8
-//               weight tiles into a ring of up to 6 stages, lane 16 the tokens' fp16 operand into a
-//               ring of 2 (an mbarrier with complete_tx per stage)
+//   warp 0      bulk-copies (cp.async.bulk, no multicast) each column tile's 8 weight tiles into a
+//               ring of up to 6 stages (an mbarrier with complete_tx per stage), from the kernel's
+//               start: the weights do not depend on the kernel before
+//   warp 18     bulk-copies the tokens' fp16 operand into a ring of 2, once the kernel before is done
 //   warp 1      allocates the tensor memory; one lane issues the MMAs and their commits
 //   warps 2..17 warps 2 + 2i and 3 + 2i dequantise row tile i of each half column tile from the ring
 //               into the MMA's A operand (fp16, K-major, no swizzle), then, with the
@@ -42,7 +43,8 @@ constexpr int kTcMaxW = 6;                         // most weight ring stages (a
 constexpr int kTcBStages = 2;                      // tokens' operand ring stages (the operand sits in L2)
 constexpr int kTcSmem = 230400;                    // dynamic shared memory a CTA may take
 constexpr int kTcDeq = 16;                         // dequantising warps: two a row tile
-constexpr int kTcThreads = (2 + kTcDeq) * 32;
+constexpr int kTcBWarp = 2 + kTcDeq;                // the warp that copies the tokens' operand
+constexpr int kTcThreads = (3 + kTcDeq) * 32;
 constexpr int kTcHalf = kTileCols / 2;             // columns of one A buffer
 // bytes of A per 16 columns (one MMA's K): 128 rows x 32 bytes, and 16 more so that the 4 K-steps
 // a warp's store instruction touches fall on different banks
@@ -332,8 +334,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
                     unsigned(a.tile_bytes), &wfull[s]);
         }
       }
-    } else if (lane == 16) {
-      // the tokens' operand (the previous kernel's output), two column tiles ahead
+    }
+  } else if (warp == kTcBWarp) {
+    if (lane == 0) {
+      // the tokens' operand (the previous kernel's output), two column tiles ahead; a warp of its
+      // own, so that waiting for the previous kernel holds back none of the weight copies
       pdl_wait();
       for (int j = 0; j < nkt; ++j) {
         const int s = j % kTcBStages, kt = kt0 + j;
@@ -417,14 +422,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
       if (last) {
         __threadfence();
         if (mine) {
+          // the splits' partials in split order, 16 independent loads a split (one L2 round trip
+          // a split, not one a value)
           float v[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            float acc = 0.f;
-            if (t0 + e < a.ntok)
-              for (int k = 0; k < a.splits; ++k)
-                acc += __ldcg(a.out.ws + (size_t(k) * kTcMaxN + t0 + e) * rows_pad + row);
-            v[e] = acc;
+          for (int e = 0; e < 16; ++e) v[e] = 0.f;
+          for (int k = 0; k < a.splits; ++k) {
+            const float *src = a.out.ws + (size_t(k) * kTcMaxN + t0) * rows_pad + row;
+            float u[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) u[e] = t0 + e < a.ntok ? __ldcg(src + size_t(e) * rows_pad) : 0.f;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] += u[e];
           }
           tc_finish<KIND>(a, row, lane, mt, t0, v);
         }

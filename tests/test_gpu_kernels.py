@@ -47,7 +47,7 @@ class Loaded:
 
 
 FORMATS = [A.HC_FMT_INT8_ROW, A.HC_FMT_INT4_SYM_G32, A.HC_FMT_INT4_ASYM_G32, A.HC_FMT_MXFP4]
-SHAPES = [(40, 2048), (100, 2816 // 32 * 32), (37, 6144), (256, 1024), (64, 2880), (8, 64)]
+SHAPES = [(40, 2048), (100, 2816 // 32 * 32), (37, 6144), (256, 1024), (64, 2880), (8, 64), (4104, 768)]
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
@@ -101,12 +101,13 @@ def test_gemv(device, fmt, shape, ntok):
         tol = 1e-5
     else:
         want = x.astype(np.float64) @ oracle_dequant(lin).astype(np.float64).T
-        # up to 8 tokens: int8 hi/lo activations (about 15 bits); 9..64: the tensor-core GEMV's fp16
-        # operands (the weight and the activation each rounded to fp16, about 2^-12 of a product)
-        tol = 1e-4 if ntok <= 8 else 1e-3
+        # up to 8 tokens, and matrices under 4,096 rows: int8 hi/lo activations (about 15 bits);
+        # 9..64 tokens of larger matrices (4104 x 768 here): the tensor-core GEMV's fp16 operands
+        # (the weight and the activation each rounded to fp16, about 2^-12 of a product)
+        tol = 1e-4 if ntok <= 8 or rows < 4096 else 1e-3
     scale = np.abs(want).max()
     assert np.abs(got - want).max() <= tol * scale + 1e-7, np.abs(got - want).max() / scale
-    if ntok > 8 and fmt != A.HC_FMT_MXFP4:
+    if ntok > 8 and fmt != A.HC_FMT_MXFP4 and rows >= 4096:
         # and no wait of the tensor-core GEMV ran out
         A.check(A.lib().hc_device_check(device.h))
 
