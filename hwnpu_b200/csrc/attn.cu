@@ -360,83 +360,122 @@ void attn_split(const float *q, const StepTok *toks, int ntok, const AttnGeom &g
 
 // Appends the chunk's new key and value rows (float32 from qkv_post) to the paged int8 cache. The
 // tokens of one sequence are consecutive in a chunk (a sequence is listed once a call), so the
-// chunk splits into runs of tokens that write the same page; one warp a (kv head, key | value, run)
-// walks its run in order, and the rows of one page are never written by two warps at once. A
-// page's scale is the fp16 rounding up of max|x| / 127 over its rows; when a new row needs a
-// larger scale, the rows already in the page are requantised to it (q' = round_even(q * s_old /
-// s_new)), so every value stays within [-127, 127].
+// chunk splits into runs of tokens that write the same page; one CTA a (run, kv head, key | value)
+// (the CTA of the run's first token; the others return at once). The cache's rule is sequential: a
+// page's scale is the fp16 rounding up of max|x| / 127 over its rows; when a new row needs a larger
+// scale, the rows already in the page are requantised to it (q' = round_even(q * s_old / s_new)),
+// so every value stays within [-127, 127]. Rows interact only through that sequence of scales, so
+// the CTA takes the run's row maxima, walks them once for the scale each row is written at and the
+// requantisations that follow it, and then every value takes its own chain at once: an earlier row
+// of the page through all of the run's requantisations, a new row through those after it. The
+// result is the row-by-row one exactly.
 template <int HD>
 __global__ void __launch_bounds__(128) kv_append_int8_kernel(const float *__restrict__ stage,
                                                             const StepTok *__restrict__ toks, int ntok,
                                                             int kv_heads, PagedKV pk) {
+  constexpr int E = HD / 32;
+  __shared__ float s_max[kPage], s_sr[kPage], s_ef[kPage];
+  __shared__ int s_er[kPage], s_nev;
+  __shared__ float s_final;
   pdl_trigger();
   pdl_wait();
-  constexpr int E = HD / 32;
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (gw >= 2 * kv_heads * ntok) return;
-  const int t0 = gw / (2 * kv_heads), kvh = (gw >> 1) % kv_heads, is_v = gw & 1;
+  const int t0 = blockIdx.x / (2 * kv_heads), kvh = (blockIdx.x >> 1) % kv_heads, is_v = blockIdx.x & 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   auto same_page = [&](const StepTok &a, const StepTok &b) { return a.slot == b.slot && a.pos / kPage == b.pos / kPage; };
-  if (t0 > 0 && same_page(toks[t0 - 1], toks[t0])) return;  // not the first token of its run
-  int8_t *pool = const_cast<int8_t *>(is_v ? pk.v : pk.k);
+  if (t0 > 0 && same_page(toks[t0 - 1], toks[t0])) return;  // not the first token of its run (uniform)
+  const StepTok tk0 = toks[t0];
+  int R = 1;
+  while (t0 + R < ntok && R < kPage && same_page(tk0, toks[t0 + R])) ++R;
+  const int off0 = tk0.pos % kPage;
+  const int page = pk.btab[size_t(tk0.slot) * pk.max_pages + tk0.pos / kPage];
+  const size_t ph = size_t(page) * kv_heads + kvh;
+  int8_t *pg = const_cast<int8_t *>(is_v ? pk.v : pk.k) + ph * kPage * HD;
   uint16_t *scales = const_cast<uint16_t *>(is_v ? pk.vscale : pk.kscale);
-  for (int t = t0; t < ntok && (t == t0 || same_page(toks[t0], toks[t])); ++t) {
-    const StepTok tk = toks[t];
-    const int page = pk.btab[size_t(tk.slot) * pk.max_pages + tk.pos / kPage], off = tk.pos % kPage;
-    const size_t ph = size_t(page) * kv_heads + kvh;
-    const float *src = stage + ((size_t(t) * 2 + is_v) * kv_heads + kvh) * HD;
-    float x[E], m = 0.f;
+  // warp w holds rows w, w + 4, w + 8, w + 12 of the run (E values a lane) and their maxima
+  float x[kPage / 4][E];
+#pragma unroll
+  for (int i = 0; i < kPage / 4; ++i) {
+    const int r = warp + 4 * i;
+    float m = 0.f;
 #pragma unroll
     for (int k = 0; k < E; ++k) {
-      x[k] = src[lane + 32 * k];
-      m = fmaxf(m, fabsf(x[k]));
+      x[i][k] = r < R ? stage[((size_t(t0 + r) * 2 + is_v) * kv_heads + kvh) * HD + lane + 32 * k] : 0.f;
+      m = fmaxf(m, fabsf(x[i][k]));
     }
     m = warp_max(m);
-    const float s_old = off == 0 ? 0.f : __half2float(__ushort_as_half(scales[ph]));
-    float s_new = s_old;
-    if (m / 127.0f > s_old) {
-      s_new = __half2float(__float2half_ru(m / 127.0f));
-      if (off > 0 && s_old > 0.f) {
-        // requantise the page's earlier rows to the larger scale: the whole page (16 bytes a lane
-        // a pass); rows not written yet are rewritten when their turn comes
-        const float f = s_old / s_new;
-        uint4 *rows = reinterpret_cast<uint4 *>(pool + ph * kPage * HD);
-        const int n16 = kPage * HD / 16;
-#pragma unroll 4
-        for (int i = lane; i < n16; i += 32) {
-          uint4 w = rows[i];
-          uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            uint32_t o = 0;
-#pragma unroll
-            for (int bb = 0; bb < 4; ++bb) {
-              const float q = float(int8_t((u[k] >> (8 * bb)) & 0xff));
-              o |= uint32_t(uint8_t(int8_t(fminf(fmaxf(rintf(q * f), -127.f), 127.f)))) << (8 * bb);
-            }
-            u[k] = o;
-          }
-          rows[i] = make_uint4(u[0], u[1], u[2], u[3]);
+    if (lane == 0 && r < R) s_max[r] = m;
+  }
+  __syncthreads();
+  const float s_first = off0 == 0 ? 0.f : __half2float(__ushort_as_half(scales[ph]));
+  if (threadIdx.x == 0) {
+    float sc = s_first;
+    int nev = 0;
+    for (int r = 0; r < R; ++r) {
+      const float m = s_max[r];
+      if (m / 127.0f > sc) {
+        const float s_new = __half2float(__float2half_ru(m / 127.0f));
+        if (off0 + r > 0 && sc > 0.f) {
+          s_ef[nev] = sc / s_new;
+          s_er[nev] = r;
+          ++nev;
         }
+        sc = s_new;
       }
-      if (lane == 0) scales[ph] = __half_as_ushort(__float2half_rn(s_new));
+      s_sr[r] = sc;
     }
-    const float inv = s_new > 0.f ? 1.0f / s_new : 0.f;
-    int8_t *pg = pool + ph * kPage * HD;
+    s_nev = nev;
+    s_final = sc;
+  }
+  __syncthreads();
+  const int nev = s_nev;
+  auto requant = [](float q, float f) { return fminf(fmaxf(rintf(q * f), -127.f), 127.f); };
+  if (off0 > 0 && nev > 0) {
+    // the page's earlier rows through every requantisation of the run: keys rows 0..off0-1
+    // (contiguous), values the whole 16-byte row of each dimension (bytes past off0 are written below)
+    uint4 *rows = reinterpret_cast<uint4 *>(pg);
+    const int n16 = is_v ? HD : off0 * HD / 16;
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+      uint4 w = rows[i];
+      uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint32_t o = 0;
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+          float q = float(int8_t((u[k] >> (8 * bb)) & 0xff));
+          for (int e = 0; e < nev; ++e) q = requant(q, s_ef[e]);
+          o |= uint32_t(uint8_t(int8_t(q))) << (8 * bb);
+        }
+        u[k] = o;
+      }
+      rows[i] = make_uint4(u[0], u[1], u[2], u[3]);
+    }
+    __syncthreads();
+  }
+  // the new rows: each at its own scale, then through the requantisations after it
+#pragma unroll
+  for (int i = 0; i < kPage / 4; ++i) {
+    const int r = warp + 4 * i;
+    if (r >= R) continue;
+    const float sr = s_sr[r];
+    const float inv = sr > 0.f ? 1.0f / sr : 0.f;
+    const int off = off0 + r;
 #pragma unroll
     for (int k = 0; k < E; ++k) {
-      const int8_t q = int8_t(fminf(fmaxf(rintf(x[k] * inv), -127.f), 127.f));
-      // keys row-major [position][dim]; values transposed [dim][position] (kPagedV)
-      if (is_v) pg[(lane + 32 * k) * kPage + off] = q;
-      else pg[off * HD + lane + 32 * k] = q;
+      float q = fminf(fmaxf(rintf(x[i][k] * inv), -127.f), 127.f);
+      for (int e = 0; e < nev; ++e)
+        if (s_er[e] > r) q = requant(q, s_ef[e]);
+      // keys row-major [position][dim]; values transposed [dim][position]
+      if (is_v) pg[(lane + 32 * k) * kPage + off] = int8_t(q);
+      else pg[off * HD + lane + 32 * k] = int8_t(q);
     }
-    __syncwarp();
   }
+  if (threadIdx.x == 0 && s_final != s_first) scales[ph] = __half_as_ushort(__float2half_rn(s_final));
 }
 
 void kv_append_int8(const float *stage, const StepTok *toks, int ntok, int kv_heads, int hd, const PagedKV &pk,
                     cudaStream_t st) {
-  const int warps = 2 * kv_heads * ntok, grid = (warps + 3) / 4;
+  const int grid = 2 * kv_heads * ntok;  // a CTA a (token, kv head, key | value)
   if (hd == 128)
     launch_pdl(kv_append_int8_kernel<128>, dim3(grid), dim3(128), 0, st, stage, toks, ntok, kv_heads, pk);
   else
