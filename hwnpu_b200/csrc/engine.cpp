@@ -375,14 +375,9 @@ struct hc_linear {
   int ordinal = 0;
   hc::DevLinear w;
   uint8_t *act = nullptr;  // activation tiles of up to kMaxChunk tokens
-  float *ws = nullptr;     // the tensor-core GEMV's split-K partials and tickets
-  int *tickets = nullptr;
-  size_t ws_floats = 0;
   ~hc_linear() {
     cudaSetDevice(ordinal);
     if (act) cudaFree(act);
-    if (ws) cudaFree(ws);
-    if (tickets) cudaFree(tickets);
   }
 };
 
@@ -400,13 +395,6 @@ HC_API char *hc_linear_load(hc_device *d, const hc_linear_desc *desc, hc_linear 
   void *a = nullptr;
   if (char *e = hc::dev_alloc(&a, size_t(l->w.m.ktiles) * hc::kActTile * hc::kMaxChunk, "activation tiles")) return e;
   l->act = static_cast<uint8_t *>(a);
-  const int mtiles = (l->w.m.rtiles + 7) / 8;
-  l->ws_floats = size_t(16) * hc::kMaxChunk * mtiles * 128;  // up to 16 splits
-  if (char *e = hc::dev_alloc(&a, l->ws_floats * sizeof(float), "split-K partials")) return e;
-  l->ws = static_cast<float *>(a);
-  if (char *e = hc::dev_alloc(&a, sizeof(int) * mtiles, "split-K tickets")) return e;
-  l->tickets = static_cast<int *>(a);
-  HC_TRY_CUDA(cudaMemset(l->tickets, 0, sizeof(int) * mtiles));
   *out = l.release();
   return nullptr;
 }
@@ -440,9 +428,6 @@ HC_API char *hc_linear_run(hc_linear *l, const float *x, int32_t ntok, float *y,
     hc::act_quant(x + size_t(t0) * W.cols, W.cols, W.cols, n, nullptr, 1.f, 0.f, l->act, W.ktiles, st, nullptr,
                   hc::act_layout(W, n));
     hc::GemvOut o;
-    o.ws = l->ws;
-    o.tickets = l->tickets;
-    o.ws_floats = l->ws_floats;
     o.mode = hc::kStore;
     o.y = y + size_t(t0) * W.rows;
     o.ldy = W.rows;

@@ -96,9 +96,6 @@ struct hc_session {
   int32_t *midx = nullptr;
   int *mcnt = nullptr, *mlist = nullptr;
   uint8_t *act2 = nullptr;
-  float *tc_ws = nullptr;  // the tensor-core GEMV's split-K partials and tickets
-  int *tc_tickets = nullptr;
-  size_t tc_ws_floats = 0;
   hc::StepTok *toks_dev = nullptr, *toks_host = nullptr;
   uint16_t *logits_dev = nullptr;
   unsigned long long *amax = nullptr;

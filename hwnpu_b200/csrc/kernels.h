@@ -51,11 +51,6 @@ struct GemvOut {
   int ldy = 0;
   uint16_t *logits = nullptr;           // kLogits: [t][ldy] fp16 bits, or nullptr
   unsigned long long *amax = nullptr;   // kLogits: [t], see argmax_key in misc.cu
-  // the tensor-core GEMV's split-K partials (ws_floats floats) and its per-row-tile tickets (zeroed
-  // once; each launch leaves them zero), or null: no split
-  float *ws = nullptr;
-  int *tickets = nullptr;
-  size_t ws_floats = 0;
 };
 
 // The activation operand a GEMV of ntok tokens reads (act_quant, attn_merge_quant):
@@ -67,9 +62,9 @@ struct GemvOut {
 enum ActLayout : int { kActAuto = 0, kActTokenMajor = 1, kActF16 = 2 };
 // The layout gemv() reads for W at ntok tokens: 9..64 tokens of int8 / int4 matrices of at least
 // kTcMinRows rows go to the tensor cores. Below that a matrix has too few 128-row tiles to fill
-// the SMs, and the split-K reduction across CTAs costs more than the tensor cores save (measured on
-// B200 at 64 tokens: 2,048 x 2,048 takes 11.7 us on the MMA-sync GEMV against 19.4 us, 4,096 x 2,048
-// 19.3 us against 16.4 us).
+// the SMs without splitting its columns over a cluster, and the split's fixed costs outweigh what
+// the tensor cores save (measured on B200 at 64 tokens: 2,048 x 2,048 takes 11.7 us on the MMA-sync
+// GEMV against 22.0 us; 4,096 x 2,048 takes 12.3 us on the tensor cores against 19.3 us).
 constexpr int kTcMinRows = 4096;
 inline ActLayout act_layout(const DevMat &W, int ntok) {
   return ntok > 8 && W.kind != kKindMx && W.rows >= kTcMinRows ? kActF16 : kActAuto;

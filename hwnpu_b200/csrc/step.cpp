@@ -26,8 +26,6 @@ hc_session::~hc_session() {
                   (void *)act, (void *)part_ml, (void *)part_o, (void *)toks_dev, (void *)logits_dev,
                   (void *)amax, (void *)am_dev, (void *)res_dev})
     if (p) cudaFree(p);
-  for (void *p : {(void *)tc_ws, (void *)tc_tickets})
-    if (p) cudaFree(p);
   for (void *p : {(void *)xn, (void *)oatt, (void *)mlog, (void *)mw, (void *)hh, (void *)ey, (void *)midx,
                   (void *)mcnt, (void *)mlist, (void *)act2})
     if (p) cudaFree(p);
@@ -42,7 +40,6 @@ hc_session::~hc_session() {
 namespace {
 
 constexpr int kMaxSplits = 64;
-constexpr int kTcTickets = 4096;  // row tiles of 128 rows a tensor-core GEMV may have (524,288 rows)
 constexpr int kSplitKeys = 1024;  // keys a split reads, at most, for the chunk's longest context
 constexpr int kSplitKeysPaged = 1024;  // the same over the paged int8 cache
 
@@ -130,15 +127,6 @@ void release_pages(hc_session *s, int seq, int len) {
     }
 }
 
-// The output settings every GEMV of a session shares: its split-K workspace.
-hc::GemvOut gemv_out(const hc_session *s) {
-  hc::GemvOut o;
-  o.ws = s->tc_ws;
-  o.tickets = s->tc_tickets;
-  o.ws_floats = s->tc_ws_floats;
-  return o;
-}
-
 // Enqueues one chunk of n tokens (already in toks_dev) on the session's stream; returns the
 // number of kernels launched. Only `heads` rows go through the final norm and the head: row j is
 // chunk token toks[j].head_src (the rows a caller reads; none for the inside of a long prompt).
@@ -161,7 +149,7 @@ int enqueue_chunk(hc_session *s, int n, bool accept, int splits, int heads) {
     const hc::AttnGeom g = geom(s, w.window);
     hc::act_quant(s->x, D, D, n, w.in_norm, nc.scale, nc.eps16, s->act, w.qkv->m.ktiles, st, nullptr,
                   hc::act_layout(w.qkv->m, n));
-    hc::GemvOut o1 = gemv_out(s);
+    hc::GemvOut o1;
     o1.mode = hc::kStore; o1.y = s->qkv; o1.ldy = W;
     hc::gemv(w.qkv->m, s->act, n, o1, st);
     hc::qkv_post(s->qkv, s->toks_dev, n, g, w.q_norm, w.k_norm, m->norm_mid.scale, m->norm_mid.eps16,
@@ -174,12 +162,12 @@ int enqueue_chunk(hc_session *s, int n, bool accept, int splits, int heads) {
     }
     hc::attn_merge_quant(s->part_ml, s->part_o, w.sinks, n, H, hd, splits, s->act, w.o->m.ktiles, nullptr, st,
                          hc::act_layout(w.o->m, n));
-    hc::GemvOut o2 = gemv_out(s);
+    hc::GemvOut o2;
     o2.mode = hc::kAdd; o2.y = s->x; o2.ldy = D;
     hc::gemv(w.o->m, s->act, n, o2, st);
     hc::act_quant(s->x, D, D, n, w.post_norm, m->norm_mid.scale, m->norm_mid.eps16, s->act, w.gu->m.ktiles, st,
                   nullptr, hc::act_layout(w.gu->m, n));
-    hc::GemvOut o3 = gemv_out(s);
+    hc::GemvOut o3;
     o3.mode = hc::kGlu; o3.y = s->h; o3.ldy = F;
     hc::gemv(w.gu->m, s->act, n, o3, st);
     hc::act_quant(s->h, F, F, n, nullptr, 1.f, 0.f, s->act, w.down->m.ktiles, st, nullptr,
@@ -190,7 +178,7 @@ int enqueue_chunk(hc_session *s, int n, bool accept, int splits, int heads) {
   if (heads > 0) {
     hc::act_quant(s->x, D, D, heads, m->final_norm, m->norm_head.scale, m->norm_head.eps16, s->act,
                   m->head->m.ktiles, st, heads == n ? nullptr : s->toks_dev, hc::act_layout(m->head->m, heads));
-    hc::GemvOut oh = gemv_out(s);
+    hc::GemvOut oh;
     oh.mode = hc::kLogits; oh.ldy = V; oh.logits = s->logits_dev; oh.amax = s->amax;
     hc::gemv(m->head->m, s->act, heads, oh, st);
     hc::amax_to_index(s->amax, heads, s->am_dev, st);
@@ -414,10 +402,6 @@ HC_API char *hc_session_new(hc_model *m, const hc_session_opts *opts, hc_session
   if (char *e = alloc(&s->x, size_t(T) * D, "hidden states")) return e;
   if (char *e = alloc(&s->qkv, size_t(T) * (H + 2 * KV) * hd, "qkv")) return e;
   if (char *e = alloc(&s->kv_stage, size_t(T) * 2 * KV * hd, "new key and value rows")) return e;
-  s->tc_ws_floats = size_t(4) << 20;  // 16 MB of split-K partials
-  if (char *e = alloc(&s->tc_ws, s->tc_ws_floats, "split-K partials")) return e;
-  if (char *e = alloc(&s->tc_tickets, size_t(kTcTickets), "split-K tickets")) return e;
-  HC_TRY_CUDA(cudaMemset(s->tc_tickets, 0, sizeof(int) * kTcTickets));
   if (char *e = alloc(&s->q, size_t(T) * H * hd, "queries")) return e;
   if (char *e = alloc(&s->h, size_t(T) * F, "mlp activations")) return e;
   if (char *e = alloc(&s->act, size_t(T) * ktiles * hc::kActTile, "activation tiles")) return e;

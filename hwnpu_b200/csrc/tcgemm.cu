@@ -22,9 +22,10 @@
 // differs from the same row computed by the one-token GEMV (int8 hi/lo activations) by the fp16
 // roundings, about 2^-12 of a product; both are within the model tolerance of the oracle.
 //
-// With splits > 1 each CTA writes its float32 partial sums to a workspace, and the last CTA of a
-// row tile (a ticket) adds them in split order and runs the epilogue: the result does not depend
-// on which CTA finishes first.
+// With splits > 1 the splits of a row tile run as one thread block cluster: each CTA leaves its
+// float32 partial sums in its own shared memory, and after a cluster barrier CTA r adds a share
+// of the rows over all the splits, in split order, through distributed shared memory, and runs
+// the epilogue on them: the result does not depend on which CTA finishes first.
 //
 // Every mbarrier wait is bounded (about a second of SM clocks): a wait that runs out records an
 // error code in *status and proceeds, so that no thread waits forever; the kernel still waits for
@@ -222,8 +223,21 @@ struct TcArgs {
 
 __device__ int tc_status_word;  // the first wait that ran out in any launch (0: none)
 
-// The epilogue's named barrier over the dequantising warps.
-__device__ __forceinline__ void tc_epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kTcDeq * 32) : "memory"); }
+// The thread block cluster of a row tile's splits: every thread of every CTA of the cluster
+// arrives and waits (release / acquire: shared-memory writes before it are seen by the cluster
+// after it).
+__device__ __forceinline__ void tc_cluster_sync() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// A float of cluster CTA `rank`'s shared memory at this CTA's address p of the same variable.
+__device__ __forceinline__ float tc_ld_cluster(const float *p, int rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(tc_saddr(p)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
 
 // The last steps of 16 tokens t0 .. t0 + 15 of tile row `row` (this thread's row; the lanes of a
 // warp hold 32 consecutive rows): row scale, bias, and the output mode.
@@ -280,7 +294,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
   __shared__ uint64_t wfull[kTcMaxW], wempty[kTcMaxW], bfull[kTcBStages], bempty[kTcBStages];
   __shared__ uint64_t afull[2], aempty[2], done;
   __shared__ uint32_t tmem_base;
-  __shared__ int last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mt = blockIdx.x / a.splits, sp = blockIdx.x % a.splits;
   const int per = a.ktiles / a.splits, rem = a.ktiles % a.splits;
@@ -398,7 +411,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
     const int q = warp & 3, t0 = 16 * (dw >> 2);
     const int row = mt * kTcRows + 32 * q + lane;  // tile row index (16 rows a tile)
     const uint32_t taddr = tmem + (uint32_t(32 * q) << 16) + uint32_t(t0);
-    const int rows_pad = (gridDim.x / a.splits) * kTcRows;
     const bool mine = t0 < a.npad;  // uniform over the warp
     if (a.splits == 1) {
       if (mine) {
@@ -406,40 +418,48 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a) 
         tc_ld16(taddr, v);
         tc_finish<KIND>(a, row, lane, mt, t0, v);
       }
-    } else {
-      if (mine) {
+    } else if (mine) {
+      // this split's partial sums into the CTA's own shared memory (the A buffers, free now),
+      // [token][128 rows], for the cluster's reduction below
+      float v[16];
+      tc_ld16(taddr, v);
+      float *red = reinterpret_cast<float *>(aop);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) red[(t0 + e) * kTcRows + 32 * q + lane] = v[e];
+    }
+  }
+  if (a.splits > 1) {
+    // the splits of a row tile are one thread block cluster: split r adds rows [r RR, r RR + RR) of
+    // every split's partials, in split order, through distributed shared memory, and runs the
+    // epilogue on them (RR = 128 / splits: one or more 16-row tiles, whose GLU pairs and argmax
+    // lanes stay in one warp)
+    tc_cluster_sync();
+    if (warp >= 2 && warp < 2 + kTcDeq) {
+      const int dw = warp - 2;
+      const int RR = kTcRows / a.splits;
+      const int rgs = (RR + 31) / 32;  // row groups of 32 lanes
+      const float *red = reinterpret_cast<const float *>(aop);
+      for (int u = dw; u < rgs * 4; u += kTcDeq) {
+        const int rg = u >> 2, t0 = 16 * (u & 3);
+        if (t0 >= a.npad) continue;
+        const int rl = sp * RR + 32 * rg + lane;  // the tile-local row
+        const bool mine = 32 * rg + lane < RR;
+        // split by split, its 16 values loaded together (one remote round trip a split)
         float v[16];
-        tc_ld16(taddr, v);
-        float *w = a.out.ws + size_t(sp) * kTcMaxN * rows_pad + row;
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          if (t0 + e < a.ntok) w[size_t(t0 + e) * rows_pad] = v[e];
-      }
-      __threadfence();
-      tc_epi_sync();
-      if (dw == 0 && lane == 0) last = atomicAdd(&a.out.tickets[mt], 1) == a.splits - 1;
-      tc_epi_sync();
-      if (last) {
-        __threadfence();
-        if (mine) {
-          // the splits' partials in split order, 16 independent loads a split (one L2 round trip
-          // a split, not one a value)
-          float v[16];
+        for (int e = 0; e < 16; ++e) v[e] = 0.f;
+        for (int k = 0; k < a.splits; ++k) {
+          float u[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) v[e] = 0.f;
-          for (int k = 0; k < a.splits; ++k) {
-            const float *src = a.out.ws + (size_t(k) * kTcMaxN + t0) * rows_pad + row;
-            float u[16];
+          for (int e = 0; e < 16; ++e) u[e] = mine ? tc_ld_cluster(red + (t0 + e) * kTcRows + rl, k) : 0.f;
 #pragma unroll
-            for (int e = 0; e < 16; ++e) u[e] = t0 + e < a.ntok ? __ldcg(src + size_t(e) * rows_pad) : 0.f;
-#pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] += u[e];
-          }
-          tc_finish<KIND>(a, row, lane, mt, t0, v);
+          for (int e = 0; e < 16; ++e) v[e] += u[e];
         }
-        if (dw == 0 && lane == 0) a.out.tickets[mt] = 0;  // for the next launch
+        // rows outside this split's share take part in the warp's shuffles with nothing to write
+        tc_finish<KIND>(a, mine ? mt * kTcRows + rl : 0x7fffffff, lane, mt, t0, v);
       }
     }
+    tc_cluster_sync();  // no CTA leaves (or reuses its shared memory) while others still read it
   }
   tc_fence_before();
   __syncthreads();
@@ -475,13 +495,13 @@ char *tc_gemm_prepare() {
   return nullptr;
 }
 
-int tc_splits(const DevMat &W, int sms, size_t ws_floats) {
+// Column-tile splits of a row tile (one thread block cluster, so 1, 2, 4 or 8): the fewest waves
+// of CTAs times the column tiles a CTA walks, plus a CTA's fixed cost of about two column tiles'.
+int tc_splits(const DevMat &W, int sms) {
   const int mtiles = (W.rtiles + kTcTiles - 1) / kTcTiles;
   int best = 1;
   long best_cost = -1;
-  for (int s = 1; s <= std::min(W.ktiles, 16); ++s) {
-    if (s > 1 && size_t(s) * kTcMaxN * mtiles * kTcRows > ws_floats) break;
-    // a CTA's fixed cost (the first copies' latency, the epilogue) is about two column tiles'
+  for (int s = 1; s <= 8 && s <= W.ktiles; s *= 2) {
     const long waves = (long(mtiles) * s + sms - 1) / sms;
     const long cost = waves * ((W.ktiles + s - 1) / s + 2);
     if (best_cost < 0 || cost < best_cost) {
@@ -495,17 +515,32 @@ int tc_splits(const DevMat &W, int sms, size_t ws_floats) {
 void tc_gemm(const DevMat &W, const uint8_t *xop, int ntok, const GemvOut &out, int sms, cudaStream_t st) {
   const int npad = (ntok + 15) / 16 * 16;
   const int mtiles = (W.rtiles + kTcTiles - 1) / kTcTiles;
-  const int splits = (out.ws && out.tickets) ? tc_splits(W, sms, out.ws_floats) : 1;
+  const int splits = tc_splits(W, sms);
   int dev = 0;
   cudaGetDevice(&dev);
   int *status = g_tc_status[dev & 63];
   const TcArgs a{W.tiles, W.row_scale, W.bias, xop, W.rtiles, W.ktiles, W.rows, W.tile_bytes, ntok, npad, splits,
                  tc_wstages(W.tile_bytes, npad), out, status};
   const size_t smem = tc_smem_bytes(W.tile_bytes, npad);
+  // programmatic stream serialization (as launch_pdl) and the splits of a row tile as one cluster
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(mtiles * splits);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = unsigned(splits);
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
   if (W.kind == kKindInt8)
-    launch_pdl(tc_gemm_kernel<kKindInt8>, dim3(mtiles * splits), dim3(kTcThreads), smem, st, a);
+    cudaLaunchKernelEx(&cfg, tc_gemm_kernel<kKindInt8>, a);
   else
-    launch_pdl(tc_gemm_kernel<kKindInt4>, dim3(mtiles * splits), dim3(kTcThreads), smem, st, a);
+    cudaLaunchKernelEx(&cfg, tc_gemm_kernel<kKindInt4>, a);
 }
 
 int tc_status_take() {
