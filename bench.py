@@ -222,6 +222,38 @@ def cpu_c5(sample, world, steps):
     return dec / total_s
 
 
+def cpu_c3(threads):
+    """The oracle's C3 decode rate on this host, a bounded sample: the model's layer shapes on 2 of
+    its 24 layers (vocabulary 201088, weights from the oracle's own generator), a 128-id prompt and
+    8 greedy steps of one sequence; the per-token cost of the 2 layers is scaled to 24 and the
+    head's cost added once. Returns (tokens/s, description)."""
+    import dataclasses
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as O
+    from hwnpu_b200 import synth
+
+    t0 = time.perf_counter()
+    c3 = dataclasses.replace(synth.C3, name="c3-2layers", layers=2)
+    model = synth.Model(c3, seed=0, gen=O.OracleGen)
+    sess = O.OracleSession(model, 160, threads=threads)
+    logits = sess.step(list(O.OracleGen.tokens(1, c3.vocab, 128)))[0]
+    a = time.perf_counter()
+    steps = 8
+    for _ in range(steps):
+        tok = O.lib().or_argmax_f16(O.p(logits, O._u16p), c3.vocab)
+        logits = sess.step([tok])[0]
+    per2 = (time.perf_counter() - a) / steps
+    sess.close()
+    # the head (201088 x 2880 bf16) is part of per2 once; the 2 layers are scaled to 24
+    head_s = 201088 * 2880 * 2 / 20e9  # its bytes at a 20 GB/s host stream, a generous estimate
+    per_tok = max(per2 - head_s, 0.0) * 12 + head_s
+    wall = time.perf_counter() - t0
+    return 1.0 / per_tok, (f"oracle C3 on {threads} threads: 2 of its 24 layers (full vocabulary) timed over "
+                           f"{steps} greedy steps after a 128-id prompt, {1e3 * per2:.0f} ms a token, the layers "
+                           f"scaled to 24 (batch 16 costs 16 tokens on the CPU); {wall:.0f} s of CPU work")
+
+
 def run_reference(args, rank, world):
     """--impl reference: the oracle's C5 rate (and bs1 rate) on the host's cores, rank 0 only."""
     if rank != 0:
@@ -234,6 +266,10 @@ def run_reference(args, rank, world):
         value = cpu_c5(s, world, args.steps)
         sample = s.describe() + f"; extrapolated to {args.steps} steps of the C5 schedule ({C5_SEQS} sequences)"
         config = c5_config(args, world)
+    elif args.workload == "c3":
+        value, sample = cpu_c3(cores)
+        config = {"workload": f"C3 greedy decode after {C3_PROMPT}-id prompts, batch 16 (oracle sample)",
+                  "model": "C3 24L d2880 64q/8kv hd64, 32 MXFP4 experts (2880) top-4, window 128, sinks, YaRN"}
     else:
         s = CpuSample(cores, A.HC_KV_F16)
         value = 1.0 / s.token_s(PROMPT + (PASS + 1) / 2.0)
@@ -336,6 +372,14 @@ def run_bs1(args, lm, model, dev, world, dist, K, W):
     sess.generate(first, W)
     sess.truncate(base)
     stream = torch.cuda.ExternalStream(sess.stream())
+    if args.profile:  # --profile N: N greedy steps between cudaProfilerStart/Stop (for ncu), no timing
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        sess.generate(first, args.profile)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        sess.close()
+        return None
     launches0 = sess.stats()["launches"]
 
     def barrier():
@@ -495,12 +539,12 @@ def run_default(args, rank, world, local, dist):
     if c5 is None:
         return
     bs1 = run_bs1(args, lm, model, dev, world, dist, K, W)
-    # the dominant kernel class of the C5 step: the batched GEMV (64 tokens on the MMA's n), on the
-    # largest matrix of a layer (gate/up, 12288 x 2048)
+    # the GEMV class of the C5 step (its chunks of 64 tokens), on the largest matrix of a layer
+    # (gate/up, 12288 x 2048): the tensor-core GEMV (tcgen05, tokens on the MMA's N)
     gu = hb.synth.Linear.quantize(hb.synth.normal(5, "bench.gate_up", 12288 * 2048, 0.02).reshape(12288, 2048),
                                   hb._abi.HC_FMT_INT4_ASYM_G32)
-    roof = kernel_roofline(dev, gu, 64, "gemm_tn_kernel<int4, 64 tokens> on the C2 gate/up 12288x2048 "
-                           "(+ its activation quantiser)", "gemm_tn_c2_gateup64")
+    roof = kernel_roofline(dev, gu, 64, "tc_gemm_kernel<int4> (tcgen05.mma, 64 tokens) on the C2 gate/up "
+                           "12288x2048 (+ its fp16 operand writer)", "tc_gemm_c2_gateup64")
     bs1["roofline"] = kernel_roofline(dev, gu, 1, "gemv_kernel<int4, 1 token> on the C2 gate/up 12288x2048 "
                                       "(+ its activation quantiser)", "gemv_c2_gateup1")
     lm.close()
@@ -548,7 +592,7 @@ def run_bs1_line(args, rank, world, local, dist, workload):
     clk = clocks.stop()
     lm.close()
     dev.close()
-    if rank != 0:
+    if rank != 0 or r is None:
         return
     cfg = r.pop("config")
     if workload == "c1":

@@ -425,13 +425,15 @@ HC_API char *hc_linear_run(hc_linear *l, const float *x, int32_t ntok, float *y,
   const hc::DevMat &W = l->w.m;
   for (int t0 = 0; t0 < ntok; t0 += hc::kMaxChunk) {
     const int n = std::min(hc::kMaxChunk, ntok - t0);
-    hc::act_quant(x + size_t(t0) * W.cols, W.cols, W.cols, n, nullptr, 1.f, 0.f, l->act, W.ktiles, st, nullptr,
-                  hc::act_layout(W, n));
+    hc::ActSrc src;
+    src.x = x + size_t(t0) * W.cols;
+    src.ldx = W.cols;
+    src.n = W.cols;
     hc::GemvOut o;
     o.mode = hc::kStore;
     o.y = y + size_t(t0) * W.rows;
     o.ldy = W.rows;
-    hc::gemv(W, l->act, n, o, st);
+    hc::gemv_x(W, src, n, l->act, o, st);
   }
   HC_TRY_CUDA(cudaGetLastError());
   return nullptr;

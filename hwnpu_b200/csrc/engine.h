@@ -72,9 +72,9 @@ struct hc_session {
   int cap = 0, splits = 1;
   uint16_t *kc = nullptr, *vc = nullptr;  // [layers][slots][kv_heads][cap][hd] fp16
   size_t layer_kv = 0;                    // elements of one layer's cache
-  // HC_KV_INT8_PAGED: page pools [layers][pages][kv_heads][16][hd] int8, scales
-  // [layers][pages][kv_heads] fp16, the block table [slots][max_pages] (device, and its host copy)
-  // and the free pages
+  // HC_KV_INT8_PAGED: page pools of int8 keys [layers][pages][kv_heads][16][hd] and values stored
+  // transposed [layers][pages][kv_heads][hd][16], scales [layers][pages][kv_heads] fp16, the block
+  // table [slots][max_pages] (device, and its host copy) and the free pages
   bool paged = false;
   int8_t *kp = nullptr, *vp = nullptr;
   uint16_t *kps = nullptr, *vps = nullptr;

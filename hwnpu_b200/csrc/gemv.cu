@@ -7,6 +7,7 @@
 // rows, the exact integer dot products of 8 columns of 4 groups at once (common.h). Lane (g, c)
 // then scales its rows g, g+8 by the weight scale (and zero point) and the activation's scale of
 // its groups c and 4 + c in float32; 2 shuffles add the 4 lanes of a row.
+#include <algorithm>
 #include <mutex>
 
 #include "device.cuh"
@@ -24,17 +25,19 @@ __device__ __forceinline__ size_t act_tn_offset(int kt, int G, int b, int nb) {
 }
 
 // The end of both GEMV kernels: part[w][t][r] holds warp w's sum for token t and row r of its row
-// tile; the wpr warps of a row tile are added, scaled and written as out.mode says, for tokens
+// tile, of row-tile block blk (default blockIdx.x); the wpr warps of a row tile are added, scaled and written as out.mode says, for tokens
 // t < nt. Ends with the argmax atomics of kLogits (bmax is the CTA's per-token key, zeroed before).
 template <int KIND, int NT>
 __device__ __forceinline__ void gemv_finish(float (*part)[NT][kTileRows], unsigned long long *bmax, int nt,
                                             const float *__restrict__ row_scale, const float *__restrict__ bias,
-                                            int rtiles, int rows, int wpr, const GemvOut &out, int warps = 8) {
+                                            int rtiles, int rows, int wpr, const GemvOut &out, int warps = 8,
+                                            int blk = -1) {
   const int rpc = warps / wpr;
+  if (blk < 0) blk = blockIdx.x;
   __syncthreads();
   for (int idx = threadIdx.x; idx < rpc * NT * kTileRows; idx += blockDim.x) {
     const int l2 = idx / (NT * kTileRows), t = (idx / kTileRows) % NT, r16 = idx % kTileRows;
-    const int tile_r = blockIdx.x * rpc + l2;
+    const int tile_r = blk * rpc + l2;
     if (tile_r >= rtiles || t >= nt) continue;
     auto value = [&](int rr) {
       float v = 0.f;
@@ -76,52 +79,261 @@ __device__ __forceinline__ void gemv_finish(float (*part)[NT][kTileRows], unsign
   }
 }
 
+__device__ double block_sum_d(double v, double *sh) {
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  double t = 0;
+  if (threadIdx.x < 32) {
+    t = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0;
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) sh[0] = t;
+  }
+  __syncthreads();
+  t = sh[0];
+  __syncthreads();
+  return t;
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Shared memory of the fused one-token GEMV: the activation tiles [NT][ktiles].
+__host__ __device__ constexpr size_t gv_smem(int nt, int ktiles) { return size_t(nt) * ktiles * kActTile; }
+
+// The RMS norm's column order, shared by act_quant_kernel and act_build so that both add the same
+// per-thread partial sums: in round k, lane (sub = lane / 8, i = lane % 8) of warp w holds the 4
+// columns 32 G + 4i .. + 3 of group G = 32k + 4w + sub (groups: ktiles x 8, a multiple of 8, so a
+// warp's 4 groups are all in range or all past the end).
+__device__ __forceinline__ int act_group(int k, int warp, int lane) { return k * 32 + warp * 4 + (lane >> 3); }
+
+// Four columns of a row, 0 past n; a 16-byte load when the row allows it.
+__device__ __forceinline__ void load4(const float *p, int c0, int n, bool vec, float v[4]) {
+  if (vec && c0 + 3 < n) {
+    const float4 q = *reinterpret_cast<const float4 *>(p + c0);
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = c0 + e < n ? p[c0 + e] : 0.f;
+  }
+}
+
+// Quantises group G from its 8 lanes' 4 values each (quant_vals' arithmetic: the maximum and the
+// integer sum are order-free, the rest per element) into the token-major tiles at tt.
+__device__ __forceinline__ void quant4(const float v[4], uint8_t *tt, int G, int lane) {
+  const int i4 = (lane & 7) * 4;
+  float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const bool nz = m > 0.f;
+  const float qi = nz ? 127.0f / m : 0.f;  // quant_vals' inv and S
+  const float S = nz ? m / 127.0f : 0.f;
+  uint32_t hw = 0, lw = 0;
+  int xs = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float h = rintf(v[e] * qi);
+    const float rr = fmaf(-h, S, v[e]);
+    const float l = fminf(fmaxf(rintf(rr * (256.0f * qi)), -127.f), 127.f);
+    const int hq = int(int8_t(h)), lq = int(int8_t(l));
+    hw |= uint32_t(uint8_t(hq)) << (8 * e);
+    lw |= uint32_t(uint8_t(lq)) << (8 * e);
+    xs += hq * 256 + lq;
+  }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) xs += __shfl_xor_sync(0xffffffffu, xs, o);
+  uint8_t *tile = tt + size_t(G / kGroupsPerTile) * kActTile;
+  const int gi = G % kGroupsPerTile;
+  *reinterpret_cast<uint32_t *>(tile + gi * 64 + i4) = hw;
+  *reinterpret_cast<uint32_t *>(tile + gi * 64 + 32 + i4) = lw;
+  if ((lane & 7) == 0)
+    *reinterpret_cast<float2 *>(tile + kGroupsPerTile * 64 + gi * 8) =
+        make_float2(S, nz ? float(xs) * (1.0f / 256.0f) : 0.f);
+}
+
+// The normed value of a column: act_quant_kernel's arithmetic.
+__device__ __forceinline__ float norm_val(float x, float inv, float unit, float r, float w) {
+  const float xs = unit ? x : x * inv;
+  const float y = xs * r;
+  return y * w;
+}
+
+// The activation tiles of NT rows into shared memory, by a CTA of 256 threads, with the bytes of
+// act_quant_kernel. Rows of up to RM rounds (2 x 1024 columns) are read once, into registers,
+// with their norm weights, and quantised from there after the sum of squares; longer rows are
+// read again for the quantisation.
+template <int NT>
+__device__ void act_build(const ActSrc &src, int ktiles, uint8_t *sm) {
+  __shared__ double red[32];
+  constexpr int RM = 2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i4 = (lane & 7) * 4;
+  const float inv = src.scale == 1.f ? 1.f : 1.f / src.scale;
+  const bool unit = src.scale == 1.f;
+  const int n = src.n, groups = ktiles * kGroupsPerTile, rounds = (groups + 31) / 32;
+  const bool wvec = (reinterpret_cast<uintptr_t>(src.norm_w) & 15) == 0;
+#pragma unroll 1
+  for (int t = 0; t < NT; ++t) {
+    const float *xt = src.x + size_t(src.rows ? src.rows[t].head_src : t) * src.ldx;
+    const bool vec = (reinterpret_cast<uintptr_t>(xt) & 15) == 0;
+    uint8_t *tt = sm + size_t(t) * ktiles * kActTile;
+    if (rounds <= RM) {
+      float v[RM][4], w[RM][4];
+#pragma unroll
+      for (int k = 0; k < RM; ++k) {
+        const int G = act_group(k, warp, lane);
+        const bool in = k < rounds && G < groups;
+        float z[4] = {0.f, 0.f, 0.f, 0.f};
+        if (in) load4(xt, G * kGroup + i4, n, vec, v[k]);
+        else for (int e = 0; e < 4; ++e) v[k][e] = 0.f;
+        if (in && src.norm_w) load4(src.norm_w, G * kGroup + i4, n, wvec, w[k]);
+        else for (int e = 0; e < 4; ++e) w[k][e] = z[e];
+      }
+      float r = 1.f;
+      if (src.norm_w) {
+        double s = 0;
+#pragma unroll
+        for (int k = 0; k < RM; ++k) {
+          const int c0 = act_group(k, warp, lane) * kGroup + i4;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (k < rounds && c0 + e < n && act_group(k, warp, lane) < groups) {
+              const float xs = unit ? v[k][e] : v[k][e] * inv;
+              const float sq = xs * xs;
+              s += double(sq);
+            }
+          }
+        }
+        s = block_sum_d(s, red);
+        const float ms = float(s / double(n));
+        r = float(1.0 / sqrt(double(ms) + double(src.eps16)));
+      }
+#pragma unroll
+      for (int k = 0; k < RM; ++k) {
+        const int G = act_group(k, warp, lane);
+        if (k >= rounds || k * 32 + warp * 4 >= groups) break;  // uniform over the warp
+        float q[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          q[e] = src.norm_w && G * kGroup + i4 + e < n ? norm_val(v[k][e], inv, unit, r, w[k][e]) : v[k][e];
+        quant4(q, tt, G, lane);
+      }
+    } else {
+      float r = 1.f;
+      if (src.norm_w) {
+        double s = 0;
+#pragma unroll 1
+        for (int k = 0; k < rounds; ++k) {
+          const int G = act_group(k, warp, lane);
+          if (G >= groups) break;
+          float x[4];
+          load4(xt, G * kGroup + i4, n, vec, x);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (G * kGroup + i4 + e < n) {
+              const float xs = unit ? x[e] : x[e] * inv;
+              const float sq = xs * xs;
+              s += double(sq);
+            }
+          }
+        }
+        s = block_sum_d(s, red);
+        const float ms = float(s / double(n));
+        r = float(1.0 / sqrt(double(ms) + double(src.eps16)));
+      }
+#pragma unroll 2
+      for (int k = 0; k < rounds; ++k) {
+        const int G = act_group(k, warp, lane);
+        if (k * 32 + warp * 4 >= groups) break;  // uniform over the warp
+        float x[4], w[4];
+        load4(xt, G * kGroup + i4, n, vec, x);
+        if (src.norm_w) {
+          load4(src.norm_w, G * kGroup + i4, n, wvec, w);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (G * kGroup + i4 + e < n) x[e] = norm_val(x[e], inv, unit, r, w[e]);
+        }
+        quant4(x, tt, G, lane);
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// One token-a-column GEMV. A CTA takes the row-tile blocks blockIdx.x, + gridDim.x, ... (a block:
+// 8 / wpr row tiles): one when the activation tiles come from act (the grid covers them all),
+// several when act is null and the CTA builds the tiles from src once, into shared memory, for
+// all its blocks (the grid is then capped at the CTAs the SMs hold at once).
 template <int KIND, int NT>
 __global__ void __launch_bounds__(256) gemv_kernel(const uint8_t *__restrict__ tiles,
                                                    const float *__restrict__ row_scale,
                                                    const float *__restrict__ bias,
                                                    const uint8_t *__restrict__ act, int rtiles,
-                                                   int ktiles, int rows, int wpr, GemvOut out) {
+                                                   int ktiles, int rows, int wpr, GemvOut out, ActSrc src) {
   constexpr int TB = KIND == kKindInt8 ? kTileInt8 : (KIND == kKindInt4 ? kTileInt4 : kTileMx);
+  extern __shared__ __align__(16) uint8_t gv_act[];  // the activation tiles when act is null
   __shared__ float part[8][NT][kTileRows];
   __shared__ unsigned long long bmax[NT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int rpc = 8 / wpr;
   const int lrt = warp / wpr, ks = warp % wpr;
-  const int rt = blockIdx.x * rpc + lrt;
+  const int nblk = (rtiles + rpc - 1) / rpc;
   pdl_trigger();
   if (threadIdx.x < NT) bmax[threadIdx.x] = 0ull;
-  float vg[NT], vg8[NT];
-#pragma unroll
-  for (int t = 0; t < NT; ++t) vg[t] = vg8[t] = 0.f;
   // the first weight tile does not depend on the kernels before: load it before waiting for them
-  const bool mine = rt < rtiles && ks < ktiles;
+  int blk = blockIdx.x;
+  bool mine = blk * rpc + lrt < rtiles && ks < ktiles;
   WTile<KIND> wt;
-  if (mine) wt.load(tiles + (size_t(rt) * ktiles + ks) * TB, lane);
+  if (mine) wt.load(tiles + (size_t(blk * rpc + lrt) * ktiles + ks) * TB, lane);
   pdl_wait();
-  if (mine) {
-    for (int kt = ks; kt < ktiles; kt += wpr) {
-      WTile<KIND> nx;  // the next tile in flight while this one computes
-      if (kt + wpr < ktiles) nx.load(tiles + (size_t(rt) * ktiles + kt + wpr) * TB, lane);
+  if (!act) {  // uniform: build the activation tiles from the rows (while the first tile loads)
+    act_build<NT>(src, ktiles, gv_act);
+    act = gv_act;
+  }
+#pragma unroll 1
+  for (;;) {
+    const int rt = blk * rpc + lrt;
+    float vg[NT], vg8[NT];
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        BFrag<KIND> bf;
-        bf.load(act + (size_t(t) * ktiles + kt) * kActTile, lane);
-        wa_mma<KIND>(wt, bf, vg[t], vg8[t]);
+    for (int t = 0; t < NT; ++t) vg[t] = vg8[t] = 0.f;
+    if (mine) {
+      for (int kt = ks; kt < ktiles; kt += wpr) {
+        WTile<KIND> nx;  // the next tile in flight while this one computes
+        if (kt + wpr < ktiles) nx.load(tiles + (size_t(rt) * ktiles + kt + wpr) * TB, lane);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          BFrag<KIND> bf;
+          bf.load(act + (size_t(t) * ktiles + kt) * kActTile, lane);
+          wa_mma<KIND>(wt, bf, vg[t], vg8[t]);
+        }
+        wt = nx;
       }
-      wt = nx;
     }
-  }
+    // the next block's first tile in flight during this block's reduction
+    const int nb = blk + gridDim.x;
+    const bool nmine = nb < nblk && nb * rpc + lrt < rtiles && ks < ktiles;
+    if (nmine) wt.load(tiles + (size_t(nb * rpc + lrt) * ktiles + ks) * TB, lane);
 #pragma unroll
-  for (int t = 0; t < NT; ++t) {
-    const float a = quad_sum(vg[t]), b = quad_sum(vg8[t]);
-    if (c == 0) {
-      part[warp][t][g] = a;
-      part[warp][t][g + 8] = b;
+    for (int t = 0; t < NT; ++t) {
+      const float a = quad_sum(vg[t]), b = quad_sum(vg8[t]);
+      if (c == 0) {
+        part[warp][t][g] = a;
+        part[warp][t][g + 8] = b;
+      }
     }
+    gemv_finish<KIND, NT>(part, bmax, NT, row_scale, bias, rtiles, rows, wpr, out, 8, blk);
+    if (nb >= nblk) break;
+    __syncthreads();  // part is rewritten by the next block
+    blk = nb;
+    mine = nmine;
   }
-  gemv_finish<KIND, NT>(part, bmax, NT, row_scale, bias, rtiles, rows, wpr, out);
 }
 
 // ---- the batched GEMV: tokens on the MMA's n ----------------------------------------------
@@ -133,13 +345,6 @@ __global__ void __launch_bounds__(256) gemv_kernel(const uint8_t *__restrict__ t
 // 16 rows x 8 tokens, which lane (g, c) scales for rows g, g + 8 and tokens 2c, 2c + 1 with the
 // same float32 arithmetic as the token-a-column GEMV (wa_mma): s S (hi + lo/256 - z Xq) for int4,
 // S (hi + lo/256) for int8, 2^(e-127) S hi for mxfp4.
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // Dynamic shared memory of gemm_tn_kernel<KIND, nb, warps, ..>: warps x 2 stages of nb x 576 bytes
 // (the larger of that and the warps x 8nb x 16 float partials).
@@ -306,17 +511,37 @@ __global__ void __launch_bounds__(WARPS * 32) gemm_tn_kernel(const uint8_t *__re
   gemv_finish<KIND, NT>(part, bmax, ntok, row_scale, bias, rtiles, rows, wpr, out, WARPS);
 }
 
+int dev_sms();
+constexpr int kGvSlab = 128 * 1024;  // the activation tiles a CTA builds, at most
+template <int KIND>
+int gemv_occupancy(int ntok, int smem);
+
+// The token-a-column GEMV of 1..8 tokens: a CTA a block when the activation tiles come from act;
+// when the CTAs build them (act null), as many CTAs as the SMs hold, each over several blocks.
+template <int KIND>
+void gv_launch(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, const ActSrc &src,
+               cudaStream_t st) {
+  const int wpr = W.ktiles >= 8 ? 8 : (W.ktiles >= 4 ? 4 : (W.ktiles >= 2 ? 2 : 1));
+  const int rpc = 8 / wpr;
+  const int nblk = (W.rtiles + rpc - 1) / rpc;
+  const size_t smem = act ? 0 : gv_smem(ntok, W.ktiles);
+  const int grid = act ? nblk : std::min(nblk, dev_sms() * gemv_occupancy<KIND>(ntok, int(smem)));
+  switch (ntok) {
+#define HC_NT(n)                                                                                     \
+  case n:                                                                                            \
+    launch_pdl(gemv_kernel<KIND, n>, dim3(grid), dim3(256), smem, st, W.tiles, W.row_scale, W.bias, act, \
+               W.rtiles, W.ktiles, W.rows, wpr, out, src);                                           \
+    break;
+    HC_NT(1) HC_NT(2) HC_NT(3) HC_NT(4) HC_NT(5) HC_NT(6) HC_NT(7) HC_NT(8)
+#undef HC_NT
+  }
+}
+
+// The batched GEMV of 9..64 tokens.
 template <int KIND>
 void launch_kind(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, int wpr,
                  int grid, cudaStream_t st) {
   switch (ntok) {
-#define HC_NT(n)                                                                          \
-  case n:                                                                                 \
-    launch_pdl(gemv_kernel<KIND, n>, dim3(grid), dim3(256), 0, st, W.tiles, W.row_scale, W.bias, act, \
-               W.rtiles, W.ktiles, W.rows, wpr, out);                                    \
-    break;
-    HC_NT(1) HC_NT(2) HC_NT(3) HC_NT(4) HC_NT(5) HC_NT(6) HC_NT(7) HC_NT(8)
-#undef HC_NT
     default: {
       // narrow matrices (few row tiles): 16 warps a row tile, two to a k-tile's groups
       const bool narrow = W.rtiles < kTnNarrowRows;
@@ -344,23 +569,6 @@ void launch_kind(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &o
 }
 
 // ---- the activation quantiser --------------------------------------------------------------
-
-__device__ double block_sum_d(double v, double *sh) {
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) sh[warp] = v;
-  __syncthreads();
-  double t = 0;
-  if (threadIdx.x < 32) {
-    t = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0;
-    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    if (threadIdx.x == 0) sh[0] = t;
-  }
-  __syncthreads();
-  t = sh[0];
-  __syncthreads();
-  return t;
-}
 
 // The batched layout: group G of k-tile kt for token t.
 __device__ __forceinline__ void quant_group_tn(float v, uint8_t *act, int kt, int G, int t, int nb, int lane) {
@@ -399,12 +607,20 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const float *__restrict_
   const float *xt = x + size_t(rows ? rows[t].head_src : t) * ldx;
   const float inv = scale == 1.f ? 1.f : 1.f / scale;
   float r = 1.f;
-  if (norm_w) {
+  if (norm_w) {  // act_build's per-thread column order (act_group)
     double s = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const float xs = scale == 1.f ? xt[i] : xt[i] * inv;
-      const float sq = xs * xs;
-      s += double(sq);
+    const int groups = ktiles * kGroupsPerTile, i4 = (lane & 7) * 4;
+    for (int k = 0; k * 32 < groups; ++k) {
+      const int G = act_group(k, warp, lane);
+      if (G >= groups) break;
+      for (int e = 0; e < 4; ++e) {
+        const int i = G * kGroup + i4 + e;
+        if (i < n) {
+          const float xs = scale == 1.f ? xt[i] : xt[i] * inv;
+          const float sq = xs * xs;
+          s += double(sq);
+        }
+      }
     }
     s = block_sum_d(s, red);
     const float ms = float(s / double(n));
@@ -502,6 +718,12 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ tiles, const float *_
 
 namespace {
 int g_sms[64];  // SMs of each device (gemv_prepare)
+constexpr int kGvSmem = 160 * 1024;  // the one-token GEMV's dynamic shared memory, at most
+int dev_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return g_sms[dev & 63] ? g_sms[dev & 63] : 148;
+}
 }  // namespace
 
 char *gemv_prepare() {
@@ -521,6 +743,13 @@ char *gemv_prepare() {
   HC_SET_K(kKindInt8) HC_SET_K(kKindInt4) HC_SET_K(kKindMx)
 #undef HC_SET_K
 #undef HC_SET
+#define HC_SETG(K, n)                                                                                \
+  HC_TRY_CUDA(cudaFuncSetAttribute(gemv_kernel<K, n>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmem));
+#define HC_SETG_K(K) HC_SETG(K, 1) HC_SETG(K, 2) HC_SETG(K, 3) HC_SETG(K, 4) HC_SETG(K, 5) HC_SETG(K, 6) \
+  HC_SETG(K, 7) HC_SETG(K, 8)
+  HC_SETG_K(kKindInt8) HC_SETG_K(kKindInt4) HC_SETG_K(kKindMx)
+#undef HC_SETG_K
+#undef HC_SETG
   if (char *e = tc_gemm_prepare()) return e;
   if (char *e = attn_tc_prepare()) return e;
   HC_TRY_CUDA(cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev));
@@ -528,11 +757,55 @@ char *gemv_prepare() {
   return nullptr;
 }
 
+namespace {
+// CTAs of gemv_kernel<KIND, ntok> one SM holds with smem bytes of activation tiles.
+template <int KIND>
+int gemv_occupancy(int ntok, int smem) {
+  static std::mutex mu;
+  static int cache[9][64];  // [ntok][smem / 4 KB] + 1, 0 = not asked yet
+  const int key = smem >> 12;
+  std::lock_guard<std::mutex> lk(mu);
+  if (key < 64 && cache[ntok][key]) return cache[ntok][key] - 1;
+  int b = 0;
+  switch (ntok) {
+#define HC_NT(n) \
+  case n: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, gemv_kernel<KIND, n>, 256, smem); break;
+    HC_NT(1) HC_NT(2) HC_NT(3) HC_NT(4) HC_NT(5) HC_NT(6) HC_NT(7) HC_NT(8)
+#undef HC_NT
+  }
+  if (b < 1) b = 1;
+  if (key < 64) cache[ntok][key] = b + 1;
+  return b;
+}
+
+}  // namespace
+
+int gemv_x(const DevMat &W, const ActSrc &src, int ntok, uint8_t *act, const GemvOut &out, cudaStream_t st) {
+  if (ntok <= 8 && gv_smem(ntok, W.ktiles) <= size_t(kGvSlab)) {
+    switch (W.kind) {
+      case kKindInt8: gv_launch<kKindInt8>(W, nullptr, ntok, out, src, st); break;
+      case kKindInt4: gv_launch<kKindInt4>(W, nullptr, ntok, out, src, st); break;
+      case kKindMx: gv_launch<kKindMx>(W, nullptr, ntok, out, src, st); break;
+    }
+    return 1;
+  }
+  act_quant(src.x, src.ldx, src.n, ntok, src.norm_w, src.scale, src.eps16, act, W.ktiles, st, src.rows,
+            act_layout(W, ntok));
+  gemv(W, act, ntok, out, st);
+  return 2;
+}
+
 void gemv(const DevMat &W, const uint8_t *act, int ntok, const GemvOut &out, cudaStream_t st) {
   if (act_layout(W, ntok) == kActF16) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    tc_gemm(W, act, ntok, out, g_sms[dev & 63] ? g_sms[dev & 63] : 148, st);
+    tc_gemm(W, act, ntok, out, dev_sms(), st);
+    return;
+  }
+  if (ntok <= 8) {
+    switch (W.kind) {
+      case kKindInt8: gv_launch<kKindInt8>(W, act, ntok, out, ActSrc{}, st); break;
+      case kKindInt4: gv_launch<kKindInt4>(W, act, ntok, out, ActSrc{}, st); break;
+      case kKindMx: gv_launch<kKindMx>(W, act, ntok, out, ActSrc{}, st); break;
+    }
     return;
   }
   const int wpr = W.ktiles >= 8 ? 8 : (W.ktiles >= 4 ? 4 : (W.ktiles >= 2 ? 2 : 1));

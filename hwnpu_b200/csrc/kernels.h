@@ -98,6 +98,20 @@ struct StepTok {
   int32_t run0 = -1;
 };
 
+// The rows a GEMV's activation is made from (act_quant's arguments): ntok rows of x (stride ldx, n
+// columns; row t is rows[t].head_src when rows is set), normed with norm_w (when set) as act_quant.
+struct ActSrc {
+  const float *x = nullptr;
+  int ldx = 0, n = 0;
+  const float *norm_w = nullptr;
+  float scale = 1.f, eps16 = 0.f;
+  const StepTok *rows = nullptr;
+};
+// y = x W^T from the rows themselves: up to 8 tokens the GEMV builds their activation tiles in
+// shared memory first (one launch, no act_quant); otherwise act_quant into act (sized for ntok
+// tokens of W) and gemv. Returns the kernels launched.
+int gemv_x(const DevMat &W, const ActSrc &src, int ntok, uint8_t *act, const GemvOut &out, cudaStream_t st);
+
 // Blocks of 8 tokens of the batched activation layout that 9..64 tokens take (0: token-major).
 inline int act_tn_blocks(int ntok) { return ntok > 8 ? (ntok + 7) / 8 : 0; }
 

@@ -127,6 +127,18 @@ void release_pages(hc_session *s, int seq, int len) {
     }
 }
 
+// The rows a GEMV reads, normed as nc says (norm_w null: as they are).
+hc::ActSrc src_of(const float *x, int ldx, int n, const float *norm_w, const hc::NormCfg &nc) {
+  hc::ActSrc a;
+  a.x = x;
+  a.ldx = ldx;
+  a.n = n;
+  a.norm_w = norm_w;
+  a.scale = norm_w ? nc.scale : 1.f;
+  a.eps16 = norm_w ? nc.eps16 : 0.f;
+  return a;
+}
+
 // Enqueues one chunk of n tokens (already in toks_dev) on the session's stream; returns the
 // number of kernels launched. Only `heads` rows go through the final norm and the head: row j is
 // chunk token toks[j].head_src (the rows a caller reads; none for the inside of a long prompt).
@@ -147,11 +159,9 @@ int enqueue_chunk(hc_session *s, int n, bool accept, int splits, int heads) {
     uint16_t *vcl = s->paged ? nullptr : s->vc + li * s->layer_kv;
     const hc::PagedKV pk = s->paged ? paged_of(s, li) : hc::PagedKV{};
     const hc::AttnGeom g = geom(s, w.window);
-    hc::act_quant(s->x, D, D, n, w.in_norm, nc.scale, nc.eps16, s->act, w.qkv->m.ktiles, st, nullptr,
-                  hc::act_layout(w.qkv->m, n));
     hc::GemvOut o1;
     o1.mode = hc::kStore; o1.y = s->qkv; o1.ldy = W;
-    hc::gemv(w.qkv->m, s->act, n, o1, st);
+    k += hc::gemv_x(w.qkv->m, src_of(s->x, D, D, w.in_norm, nc), n, s->act, o1, st);
     hc::qkv_post(s->qkv, s->toks_dev, n, g, w.q_norm, w.k_norm, m->norm_mid.scale, m->norm_mid.eps16,
                  s->rope, s->q, kcl, vcl, s->kv_stage, st);
     hc::attn_split(s->q, s->toks_dev, n, g, kcl, vcl, splits, s->part_ml, s->part_o, st, s->paged ? &pk : nullptr,
@@ -165,24 +175,20 @@ int enqueue_chunk(hc_session *s, int n, bool accept, int splits, int heads) {
     hc::GemvOut o2;
     o2.mode = hc::kAdd; o2.y = s->x; o2.ldy = D;
     hc::gemv(w.o->m, s->act, n, o2, st);
-    hc::act_quant(s->x, D, D, n, w.post_norm, m->norm_mid.scale, m->norm_mid.eps16, s->act, w.gu->m.ktiles, st,
-                  nullptr, hc::act_layout(w.gu->m, n));
     hc::GemvOut o3;
     o3.mode = hc::kGlu; o3.y = s->h; o3.ldy = F;
-    hc::gemv(w.gu->m, s->act, n, o3, st);
-    hc::act_quant(s->h, F, F, n, nullptr, 1.f, 0.f, s->act, w.down->m.ktiles, st, nullptr,
-                  hc::act_layout(w.down->m, n));
-    hc::gemv(w.down->m, s->act, n, o2, st);
-    k += 10;
+    k += hc::gemv_x(w.gu->m, src_of(s->x, D, D, w.post_norm, m->norm_mid), n, s->act, o3, st);
+    k += hc::gemv_x(w.down->m, src_of(s->h, F, F, nullptr, hc::NormCfg{}), n, s->act, o2, st);
+    k += 4;  // qkv_post, attn_split, attn_merge_quant, the o GEMV
   }
   if (heads > 0) {
-    hc::act_quant(s->x, D, D, heads, m->final_norm, m->norm_head.scale, m->norm_head.eps16, s->act,
-                  m->head->m.ktiles, st, heads == n ? nullptr : s->toks_dev, hc::act_layout(m->head->m, heads));
     hc::GemvOut oh;
     oh.mode = hc::kLogits; oh.ldy = V; oh.logits = s->logits_dev; oh.amax = s->amax;
-    hc::gemv(m->head->m, s->act, heads, oh, st);
+    hc::ActSrc hs = src_of(s->x, D, D, m->final_norm, m->norm_head);
+    hs.rows = heads == n ? nullptr : s->toks_dev;
+    k += hc::gemv_x(m->head->m, hs, heads, s->act, oh, st);
     hc::amax_to_index(s->amax, heads, s->am_dev, st);
-    k += 3;
+    ++k;
   }
   if (accept) { hc::spec_accept(s->am_dev, s->toks_dev, n, s->res_dev, st); ++k; }
   return k;
