@@ -25,6 +25,7 @@ Workloads c2 / c1 (bs1 lines), c3 (the MoE model at batch 1 and 16), c4 (specula
 """
 
 import argparse
+import dataclasses
 import hashlib
 import json
 import os
@@ -321,9 +322,10 @@ def profiled_traffic(name):
 
 
 def kernel_roofline(dev, lin, ntok, label, profile_name, reps=50):
-    """The GEMV class of a step on one of its matrices, timed alone with CUDA events on torch's stream
-    (hc_linear_run: its activation quantiser launch included): algorithmic bytes = the matrix's
-    weight bytes per launch."""
+    """The GEMV class of a step on one of its matrices, timed alone: reps calls of hc_linear_run
+    (its activation launch, if any, included) captured in one CUDA graph, as a step runs them, and
+    timed with CUDA events around the graph's replay on torch's stream; algorithmic bytes = the
+    matrix's weight bytes per call."""
     import ctypes as C
 
     import torch
@@ -336,19 +338,27 @@ def kernel_roofline(dev, lin, ntok, label, profile_name, reps=50):
     y = torch.empty(ntok, lin.rows, device="cuda")
     cs = torch.cuda.current_stream()
 
-    def once():
+    def once(st):
         A.check(A.lib().hc_linear_run(h, C.c_void_p(x.data_ptr()), ntok, C.c_void_p(y.data_ptr()),
-                                      C.c_void_p(cs.cuda_stream)))
+                                      C.c_void_p(st.cuda_stream)))
 
     for _ in range(5):
-        once()
+        once(cs)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        gs = torch.cuda.current_stream()
+        for _ in range(reps):
+            once(gs)
+    graph.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(cs)
-    for _ in range(reps):
-        once()
+    graph.replay()
     e1.record(cs)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
+    del graph
     A.lib().hc_linear_free(h)
     wbytes = sum(a.nbytes for a in (lin.data, lin.scales, lin.zeros, lin.exps) if a is not None)
     peak, kind = peaks()
@@ -530,7 +540,10 @@ def run_default(args, rank, world, local, dist):
 
     K, W = args.steps, max(3, args.warmup)
     dev = hb.Device(local)
-    model = hb.Model(hb.C2, seed=0)
+    if args.layers and not args.profile:
+        raise SystemExit("--layers only shrinks the model of a --profile capture; bench lines use all 28")
+    cfg = dataclasses.replace(hb.C2, layers=args.layers) if args.layers else hb.C2
+    model = hb.Model(cfg, seed=0)
     lm = dev.load_model(model)
     clocks = Clocks(local)
     clocks.start()
@@ -546,7 +559,7 @@ def run_default(args, rank, world, local, dist):
     roof = kernel_roofline(dev, gu, 64, "tc_gemm_kernel<int4> (tcgen05.mma, 64 tokens) on the C2 gate/up "
                            "12288x2048 (+ its fp16 operand writer)", "tc_gemm_c2_gateup64")
     bs1["roofline"] = kernel_roofline(dev, gu, 1, "gemv_kernel<int4, 1 token> on the C2 gate/up 12288x2048 "
-                                      "(+ its activation quantiser)", "gemv_c2_gateup1")
+                                      "(its activation quantisation built in)", "gemv_c2_gateup1")
     lm.close()
     dev.close()
     if dist:
@@ -866,19 +879,28 @@ def run_linear(args, local):
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
     reps = max(1, args.steps)
+    # the reps calls as one CUDA graph (as a step runs them), timed around its replay
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        gs = torch.cuda.current_stream()
+        for _ in range(reps):
+            A.check(A.lib().hc_linear_run(h, C.c_void_p(x.data_ptr()), n, C.c_void_p(y.data_ptr()),
+                                          C.c_void_p(gs.cuda_stream)))
+    graph.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(cs)
-    for _ in range(reps):
-        once()
+    graph.replay()
     e1.record(cs)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
+    del graph
     wbytes = lin.data.nbytes + lin.scales.nbytes + (lin.zeros.nbytes if lin.zeros is not None else 0)
     peak, kind = peaks()
     print(json.dumps({"workload": "linear", "rows": rows, "cols": cols, "ntok": n, "us_per_call": ms * 1e3,
                       "weight_gbs": wbytes / (ms / 1e3) / 1e9, "frac_hbm": wbytes / (ms / 1e3) / 1e9 / peak,
                       "int_tops_useful": 2.0 * rows * cols * n / (ms / 1e3) / 1e12,
-                      "note": "includes the activation quantiser launch(es)"}), flush=True)
+                      "note": "a CUDA graph of the calls; includes the activation quantiser launch, if any"}), flush=True)
     A.lib().hc_linear_free(h)
     dev.close()
 
@@ -901,6 +923,8 @@ def main():
     ap.add_argument("--profile", type=int, default=0,
                     help="--workload linear / c5: run this many calls (steps) between cudaProfilerStart/Stop "
                          "after the warm-up, for ncu (c5: then exit without timing)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="with --profile on the C5 workload: a model of this many C2 layers (a small ncu case)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
