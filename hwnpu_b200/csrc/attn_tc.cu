@@ -243,9 +243,11 @@ __global__ void __launch_bounds__(kAtWarps * 32) attn_paged_tc_kernel(const floa
         mma_s8s8(d[2 * pg + 1], qa[J][0], 0u, qa[J][1], 0u, b10, b11);
       }
     }
-    // hi + lo / 256 per score (the hi and lo rows are REP rows apart: lanes 4 REP apart)
+    // hi + lo / 256 per score (the hi and lo rows are REP rows apart: lanes 4 REP apart); only a
+    // pair that reaches outside [k0, kc1) masks positions (uniform over the warp)
     float sc[8];
     const float sa = qsr * ksa * g.score_scale, sb = qsr * ksb * g.score_scale;
+    const bool full = 16 * pa >= k0 && 16 * (pa + 2) <= kc1;
 #pragma unroll
     for (int tl = 0; tl < 4; ++tl) {
 #pragma unroll
@@ -253,9 +255,14 @@ __global__ void __launch_bounds__(kAtWarps * 32) attn_paged_tc_kernel(const floa
         const int raw = d[tl][e];
         const int other = __shfl_xor_sync(0xffffffffu, raw, 4 * REP);
         const float v = row_hi ? float(raw) + float(other) * (1.0f / 256.0f) : float(other) + float(raw) * (1.0f / 256.0f);
-        const int pos = 16 * (pa + (tl >> 1)) + 4 * cq + 2 * (tl & 1) + e;
-        const bool ok = pos >= k0 && pos < kc1;
-        sc[(tl >> 1) * 4 + 2 * (tl & 1) + e] = ok ? v * ((tl >> 1) ? sb : sa) : -INFINITY;
+        sc[(tl >> 1) * 4 + 2 * (tl & 1) + e] = v * ((tl >> 1) ? sb : sa);
+      }
+    }
+    if (!full) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int pos = 16 * (pa + (k >> 2)) + 4 * cq + (k & 3);
+        if (pos < k0 || pos >= kc1) sc[k] = -INFINITY;
       }
     }
     // the online softmax of this row's head over the pair's 32 positions (the quad holds them all)
@@ -264,12 +271,13 @@ __global__ void __launch_bounds__(kAtWarps * 32) attn_paged_tc_kernel(const floa
     for (int k = 1; k < 8; ++k) mx = fmaxf(mx, sc[k]);
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    // every pair holds a position of [k0, kc1), so m_new is finite: exp(-inf) gives the zeros
     const float m_new = fmaxf(m_r, mx);
-    const float corr = m_r == -INFINITY ? 0.f : expf(m_r - m_new);
+    const float corr = __expf(m_r - m_new);
     float p[8], psum = 0.f;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      p[k] = sc[k] == -INFINITY ? 0.f : expf(sc[k] - m_new);
+      p[k] = __expf(sc[k] - m_new);
       psum += p[k];
     }
     psum += __shfl_xor_sync(0xffffffffu, psum, 1);
