@@ -243,60 +243,70 @@ __global__ void __launch_bounds__(kAtWarps * 32) attn_paged_tc_kernel(const floa
         mma_s8s8(d[2 * pg + 1], qa[J][0], 0u, qa[J][1], 0u, b10, b11);
       }
     }
-    // hi + lo / 256 per score (the hi and lo rows are REP rows apart: lanes 4 REP apart); only a
-    // pair that reaches outside [k0, kc1) masks positions (uniform over the warp)
-    float sc[8];
+    // A head's hi-row lane and lo-row lane (4 REP lanes apart) share the head's scores: the hi lane
+    // takes page a's 4 positions, the lo lane page b's, each combining hi + lo / 256 from its own
+    // sum and the partner's; the softmax sums and the weights' codes are then exchanged, so each lane
+    // does half of the per-position work. Only a pair that reaches outside [k0, kc1) masks
+    // positions (uniform over the warp).
+    constexpr int PX = 4 * REP;
+    float sc[4];
     const float sa = qsr * ksa * g.score_scale, sb = qsr * ksb * g.score_scale;
     const bool full = 16 * pa >= k0 && 16 * (pa + 2) <= kc1;
 #pragma unroll
-    for (int tl = 0; tl < 4; ++tl) {
+    for (int u = 0; u < 2; ++u) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int raw = d[tl][e];
-        const int other = __shfl_xor_sync(0xffffffffu, raw, 4 * REP);
-        const float v = row_hi ? float(raw) + float(other) * (1.0f / 256.0f) : float(other) + float(raw) * (1.0f / 256.0f);
-        sc[(tl >> 1) * 4 + 2 * (tl & 1) + e] = v * ((tl >> 1) ? sb : sa);
+        const int mine = row_hi ? d[u][e] : d[2 + u][e];
+        const int give = row_hi ? d[2 + u][e] : d[u][e];
+        const int got = __shfl_xor_sync(0xffffffffu, give, PX);
+        const float v = row_hi ? float(mine) + float(got) * (1.0f / 256.0f) : float(got) + float(mine) * (1.0f / 256.0f);
+        sc[2 * u + e] = v * (row_hi ? sa : sb);
       }
     }
+    const int my_page = pa + (row_hi ? 0 : 1);
     if (!full) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int pos = 16 * (pa + (k >> 2)) + 4 * cq + (k & 3);
+      for (int k = 0; k < 4; ++k) {
+        const int pos = 16 * my_page + 4 * cq + k;
         if (pos < k0 || pos >= kc1) sc[k] = -INFINITY;
       }
     }
-    // the online softmax of this row's head over the pair's 32 positions (the quad holds them all)
-    float mx = sc[0];
-#pragma unroll
-    for (int k = 1; k < 8; ++k) mx = fmaxf(mx, sc[k]);
+    // the online softmax of this row's head over the pair's 32 positions (the quad and its partner)
+    float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, PX));
     // every pair holds a position of [k0, kc1), so m_new is finite: exp(-inf) gives the zeros
     const float m_new = fmaxf(m_r, mx);
     const float corr = __expf(m_r - m_new);
-    float p[8], psum = 0.f;
+    float p[4], psum = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < 4; ++k) {
       p[k] = __expf(sc[k] - m_new);
       psum += p[k];
     }
     psum += __shfl_xor_sync(0xffffffffu, psum, 1);
     psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+    psum += __shfl_xor_sync(0xffffffffu, psum, PX);
     l_r = l_r * corr + psum;
     m_r = m_new;
     // the weights times each page's value scale over the pair's larger one, as int8 hi/lo (B of
-    // the value MMA: column gq, positions 4 cq .. 4 cq + 3 of page a in b0, of page b in b1)
+    // the value MMA: column gq, positions 4 cq .. 4 cq + 3 of page a in b0, of page b in b1): each
+    // lane codes its page's 4 weights both ways and hands the partner the half it needs
     const float vsm = fmaxf(vsa, vsb);
     const float fa = vsm > 0.f ? vsa / vsm * 127.0f : 0.f, fb = vsm > 0.f ? vsb / vsm * 127.0f : 0.f;
-    float w8[8];
+    const float f = row_hi ? fa : fb;
+    float wh[4], wl[4];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float x = p[k] * (k < 4 ? fa : fb);
-      const float hi = rintf(x);
-      w8[k] = row_hi ? hi : fminf(fmaxf(rintf((x - hi) * 256.0f), -127.f), 127.f);
+    for (int k = 0; k < 4; ++k) {
+      const float x = p[k] * f;
+      wh[k] = rintf(x);
+      wl[k] = fminf(fmaxf(rintf((x - wh[k]) * 256.0f), -127.f), 127.f);
     }
-    const uint32_t pb0 = row_used ? at_pack4(w8[0], w8[1], w8[2], w8[3]) : 0u;
-    const uint32_t pb1 = row_used ? at_pack4(w8[4], w8[5], w8[6], w8[7]) : 0u;
+    const uint32_t my_hi = at_pack4(wh[0], wh[1], wh[2], wh[3]), my_lo = at_pack4(wl[0], wl[1], wl[2], wl[3]);
+    const uint32_t got_codes = __shfl_xor_sync(0xffffffffu, row_hi ? my_lo : my_hi, PX);
+    const uint32_t pb0 = row_used ? (row_hi ? my_hi : got_codes) : 0u;
+    const uint32_t pb1 = row_used ? (row_hi ? got_codes : my_lo) : 0u;
     // each column's head's rescale (from the score row of that head: lane 4 h)
     const float c0 = __shfl_sync(0xffffffffu, corr, 4 * (col0 % REP));
     const float c1 = __shfl_sync(0xffffffffu, corr, 4 * (col1 % REP));
