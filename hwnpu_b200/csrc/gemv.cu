@@ -781,7 +781,10 @@ int gemv_occupancy(int ntok, int smem) {
 }  // namespace
 
 int gemv_x(const DevMat &W, const ActSrc &src, int ntok, uint8_t *act, const GemvOut &out, cudaStream_t st) {
-  if (ntok <= 8 && gv_smem(ntok, W.ktiles) <= size_t(kGvSlab)) {
+  // one token: the CTAs build the tiles themselves; for 2..8 the build's per-token norm passes
+  // would run one after another in every CTA, and one act_quant launch (a CTA a token and column
+  // tile) is faster
+  if (ntok == 1 && gv_smem(ntok, W.ktiles) <= size_t(kGvSlab)) {
     switch (W.kind) {
       case kKindInt8: gv_launch<kKindInt8>(W, nullptr, ntok, out, src, st); break;
       case kKindInt4: gv_launch<kKindInt4>(W, nullptr, ntok, out, src, st); break;

@@ -107,7 +107,7 @@ struct ActSrc {
   float scale = 1.f, eps16 = 0.f;
   const StepTok *rows = nullptr;
 };
-// y = x W^T from the rows themselves: up to 8 tokens the GEMV builds their activation tiles in
+// y = x W^T from the rows themselves: for one token the GEMV builds its activation tiles in
 // shared memory first (one launch, no act_quant); otherwise act_quant into act (sized for ntok
 // tokens of W) and gemv. Returns the kernels launched.
 int gemv_x(const DevMat &W, const ActSrc &src, int ntok, uint8_t *act, const GemvOut &out, cudaStream_t st);
