@@ -283,9 +283,9 @@ HC_API char *hc_seq_truncate(hc_session *s, int32_t seq, int32_t len);
 /* Session.Pos (session.go:13). */
 HC_API char *hc_seq_pos(hc_session *s, int32_t seq, int32_t *pos);
 /* Session.ExportRows / ImportRows (decode.go:1859,1883): the keys and values of positions
- * [start, start+n) of every layer, in the session's KV format, packed as
- * [layer][k|v][kv_head][n][row bytes] (+ scales for HC_KV_INT8_PAGED pages). With dst NULL only
- * *need is written. */
+ * [start, start+n) of every layer, fp16, packed as [layer][k|v][kv_head][n][row bytes]. With dst
+ * NULL only *need is written. A session over the paged int8 cache (HC_KV_INT8_PAGED) returns an
+ * error from both. */
 HC_API char *hc_seq_export_rows(hc_session *s, int32_t seq, int32_t start, int32_t n, void *dst,
                                 uint64_t cap, uint64_t *need);
 HC_API char *hc_seq_import_rows(hc_session *s, int32_t seq, int32_t start, int32_t n,
