@@ -366,6 +366,9 @@ OR_API int32_t or_session_pos(or_session *s) { return s->pos; }
 OR_API void or_truncate(or_session *s, int32_t len) {
   if (len >= 0 && len < s->pos) s->pos = len;
 }
+OR_API void or_page_write(int8_t *page_rows, uint16_t *scale, int32_t off, const float *x, int32_t hd) {
+  page_write(page_rows, scale, off, x, hd);
+}
 
 namespace {
 

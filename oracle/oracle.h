@@ -100,5 +100,8 @@ OR_API int32_t or_step(or_session *s, const int32_t *tokens, int32_t n, int32_t 
 OR_API int32_t or_speculate(or_session *s, const int32_t *toks, int32_t n, int32_t *next,
                             uint16_t *logits_last);
 OR_API void or_truncate(or_session *s, int32_t len);
+/* One row written into a page of the paged int8 cache, as an int8-paged session writes it (the
+ * page's rows [16][hd] and its fp16 scale bits are updated in place; off: the row's slot). */
+OR_API void or_page_write(int8_t *page_rows, uint16_t *scale, int32_t off, const float *x, int32_t hd);
 
 #endif

@@ -51,6 +51,7 @@ SIG = {
     "or_step": (C.c_int32, [C.c_void_p, _i32p, C.c_int32, C.c_int32, _u16p]),
     "or_speculate": (C.c_int32, [C.c_void_p, _i32p, C.c_int32, _i32p, _u16p]),
     "or_truncate": (None, [C.c_void_p, C.c_int32]),
+    "or_page_write": (None, [_i8p, _u16p, C.c_int32, _f32p, C.c_int32]),
 }
 
 

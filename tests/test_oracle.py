@@ -342,6 +342,51 @@ def test_oracle_paged_int8_close_to_fp16():
     f16.close()
 
 
+def _page_write_np(rows, scale_bits, off, x):
+    """The paged int8 cache's write rule restated in numpy float32: the page scale is the fp16
+    rounding up of max|x| / 127 over its rows; a row that needs a larger scale requantises the
+    earlier rows to it (q' = round_even(q * (s_old / s_new)), clamped to +-127); the row is then
+    round_even(x * (1 / s)), clamped."""
+    f32 = np.float32
+    m = f32(np.abs(x).max())
+    s_old = f32(0) if off == 0 else f32(np.uint16(scale_bits).view(np.float16))
+    s_new = s_old
+    need = f32(m / f32(127))
+    if need > s_old:
+        h = np.float16(need)
+        if f32(h) < need:
+            h = np.nextafter(h, np.float16(np.inf))
+        s_new = f32(h)
+        if off > 0 and s_old > 0:
+            fac = f32(s_old / s_new)
+            rows[:off] = np.clip(np.rint(rows[:off].astype(f32) * fac), -127, 127).astype(np.int8)
+        scale_bits = int(np.float16(s_new).view(np.uint16))
+    inv = f32(f32(1) / s_new) if s_new > 0 else f32(0)
+    rows[off] = np.clip(np.rint(x.astype(f32) * inv), -127, 127).astype(np.int8)
+    return scale_bits
+
+
+def test_oracle_page_write_matches_restatement():
+    # the oracle's page writes (or_page_write, the rule its int8-paged sessions use) against an
+    # independent numpy restatement, byte for byte, over pages whose rows grow, shrink and jump in
+    # magnitude (so scales grow and earlier rows are requantised, several times a page)
+    rng = np.random.default_rng(5)
+    hd = 128
+    for page in range(40):
+        got = np.zeros((16, hd), np.int8)
+        want = np.zeros((16, hd), np.int8)
+        gs = C.c_uint16(0)
+        ws = 0
+        for off in range(16):
+            x = (rng.standard_normal(hd) * rng.choice([0.01, 0.1, 1.0, 7.0, 40.0])).astype(np.float32)
+            if page % 7 == 0 and off == 3:
+                x[:] = 0.0  # an all-zero row keeps the scale
+            L().or_page_write(O.p(got, O._i8p), C.byref(gs), off, O.p(x, O._f32p), hd)
+            ws = _page_write_np(want, ws, off, x)
+            assert int(gs.value) == ws, (page, off)
+            assert np.array_equal(got, want), (page, off)
+
+
 # a gpt-oss-shaped model small enough for the CPU: sliding layers of a window of 8 alternate with
 # full ones, 8 experts, top 2
 TINY_GPTOSS = synth.Config("tiny-gptoss", 2, 256, 256, 4, 2, 64, 500, A.HC_FMT_MXFP4, norm_scale=False,
